@@ -1,0 +1,383 @@
+#!/usr/bin/env python
+"""Mixtral-block forward+backward throughput on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
+
+One step is one pass of the block lens over one batch: zero the parameter
+adjoint, forward (get), backward (put) and, with N > 1 GPUs, the
+data-parallel reduction of the parameter adjoint over NCCL.  Inputs are
+seeded synthetic tensors of the workload's shapes (no dataset exists for this
+path): matrices ~ N(0, 0.02^2), RMSNorm weights 1, x and dy ~ N(0, 1).
+
+Prints one JSON line (rank 0).  `value` is whole-job tokens/s with inputs
+resident in HBM; `e2e` is the same metric through the public C-ABI call with
+the step's inputs copied from pinned host memory and its input cotangent read
+back every step; `roofline` is the expert gate/up grouped GEMM against the
+measured bf16 peak; `cpu_baseline` is the CPU oracle (a port of the crate's
+single-threaded CPU lens) on a bounded sample of the same workload.
+
+`--impl reference` times that CPU lens instead, on all host cores (one
+independent sample per worker process), and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "dependent-optics_b200"))
+sys.path.insert(0, str(ROOT / "tests"))
+
+METRIC = "Mixtral-block fwd+bwd tokens/s at 1/2/4/8 B200; % of bf16 tensor peak"
+
+WORKLOADS = {
+    # Mixtral-8x7B-shaped block, bf16 weights / fp32 accumulate, balanced routing
+    "mixtral8x7b_block": dict(cfg=dict(vocab=32000, dim=4096, layers=1, heads=32, kv_heads=8,
+                                       head_dim=128, intermediate=14336, experts=8, top_k=2,
+                                       rms_eps=1e-5, rope_theta=1e6, sliding_window=4096),
+                              batch=8, seq=4096, precision="bf16", skew=False),
+    # same, with a Zipf(s=1.2) per-expert logit bias scaled to 2.0
+    "mixtral8x7b_block_skewed": dict(cfg=dict(vocab=32000, dim=4096, layers=1, heads=32,
+                                              kv_heads=8, head_dim=128, intermediate=14336,
+                                              experts=8, top_k=2, rms_eps=1e-5, rope_theta=1e6,
+                                              sliding_window=4096),
+                                     batch=8, seq=4096, precision="bf16", skew=True),
+    # dense block (one expert, top-1, full causal attention)
+    "dense_block": dict(cfg=dict(vocab=32000, dim=2048, layers=1, heads=16, kv_heads=16,
+                                 head_dim=128, intermediate=5632, experts=1, top_k=1,
+                                 rms_eps=1e-5, rope_theta=1e4, sliding_window=2048),
+                        batch=8, seq=2048, precision="bf16", skew=False),
+    # small Mixtral block, fp32
+    "small_mixtral_block_f32": dict(cfg=dict(vocab=32000, dim=512, layers=1, heads=8, kv_heads=2,
+                                             head_dim=64, intermediate=1408, experts=8, top_k=2,
+                                             rms_eps=1e-5, rope_theta=1e6, sliding_window=128),
+                                    batch=4, seq=512, precision="f32", skew=False),
+}
+DEFAULT_WORKLOAD = "mixtral8x7b_block"
+CPU_SAMPLE_SEQ = 4  # tokens of the CPU-oracle sample (batch 1, full widths)
+
+
+def flops_per_step(cfg, batch, seq):
+    """Algorithmic FLOPs of one block fwd+bwd: 3 x forward, selected experts
+    only, visible attention pairs only, no recomputation counted."""
+    D, H, KV, hd = cfg["dim"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"]
+    E, k, I, W = cfg["experts"], cfg["top_k"], cfg["intermediate"], cfg["sliding_window"]
+    T = batch * seq
+    vis = sum(min(s + 1, W) for s in range(seq)) * batch
+    fwd = (2 * T * (D * H * hd + 2 * D * KV * hd + H * hd * D) + 4 * hd * H * vis
+           + 2 * T * k * 3 * D * I + (2 * T * D * E if E > 1 else 0))
+    return 3 * fwd
+
+
+def zipf_bias(E, seed=0, s=1.2, scale=2.0):
+    """b_e = scale * r_e^-s with expert ranks r from a seeded permutation."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    ranks = torch.randperm(E, generator=g) + 1
+    return (scale * ranks.double() ** -s).float()
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc = index, None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out = self.proc.communicate(timeout=5)[0]
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out = self.proc.communicate()[0]
+
+    def summary(self):
+        rows = [r.split(",") for r in self.out.strip().splitlines() if r.count(",") >= 7]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" == r[4 + i].strip()})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def make_params(cfg_d, precision, seed, device):
+    import torch
+    from dop.mixtral import MixtralConfig, layer_layout
+    cfg = MixtralConfig(**cfg_d)
+    ll = layer_layout(cfg)
+    g = torch.Generator(device=device).manual_seed(seed)
+    dt = torch.bfloat16 if precision == "bf16" else torch.float32
+    P = torch.empty(ll.total, dtype=dt, device=device)
+    chunk = 1 << 28
+    for a in range(0, ll.total, chunk):  # N(0, 0.02^2) in chunks (bounded fp32 temporary)
+        b = min(ll.total, a + chunk)
+        P[a:b] = (torch.randn(b - a, generator=g, device=device) * 0.02).to(dt)
+    P[ll.attn_norm: ll.attn_norm + cfg.dim] = 1.0
+    P[ll.ffn_norm: ll.ffn_norm + cfg.dim] = 1.0
+    return cfg, ll, P
+
+
+def cpu_oracle_sample(cfg_d, seq, seed, repeats=1):
+    """Seconds for one fwd+bwd of the CPU oracle on (batch 1, seq) at full widths."""
+    import numpy as np
+    import torch
+    import oracle_ffi as orc
+    from dop.mixtral import MixtralConfig, layer_layout
+    cfg = MixtralConfig(**cfg_d)
+    ll = layer_layout(cfg)
+    g = torch.Generator().manual_seed(seed)
+    lp = (torch.randn(ll.total, generator=g) * 0.02).numpy()
+    lp[ll.attn_norm: ll.attn_norm + cfg.dim] = 1.0
+    lp[ll.ffn_norm: ll.ffn_norm + cfg.dim] = 1.0
+    x = torch.randn(seq * cfg.dim, generator=g).numpy()
+    dy = torch.randn(seq * cfg.dim, generator=g).numpy()
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        r = orc.block_forward(cfg, lp, x, 1, seq)
+        orc.block_backward(cfg, lp, r, dy)
+        times.append(time.perf_counter() - t0)
+        del r
+    return times
+
+
+def _worker(args):
+    cfg_d, seq, seed, repeats = args
+    return cpu_oracle_sample(cfg_d, seq, seed, repeats)
+
+
+def run_reference(a):
+    """CPU lens (oracle port of the crate's single-threaded CPU lens) on all
+    host cores: one independent (batch 1, seq CPU_SAMPLE_SEQ) sample per
+    worker process; tokens/s = workers * tokens / slowest worker's time."""
+    import multiprocessing as mp
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    wl = WORKLOADS[a.workload]
+    cores = os.cpu_count() or 1
+    try:
+        avail = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
+    except (ValueError, OSError):
+        avail = 64 << 30
+    from dop.mixtral import MixtralConfig, layer_layout
+    per_worker = layer_layout(MixtralConfig(**wl["cfg"])).total * 4 * 2.6 + (1 << 30)
+    workers = max(1, min(cores, int(avail * 0.7 // per_worker)))
+    ctx = mp.get_context("spawn")
+    steps = max(1, a.steps)
+    with ctx.Pool(workers) as pool:
+        res = pool.map(_worker, [(wl["cfg"], CPU_SAMPLE_SEQ, w, a.warmup + steps)
+                                 for w in range(workers)])
+    per_step = [max(r[a.warmup + i] for r in res) for i in range(steps)]
+    t = sum(per_step) / steps
+    tokens = workers * CPU_SAMPLE_SEQ
+    v = tokens / t
+    sample = (f"{workers} workers x (batch 1, seq {CPU_SAMPLE_SEQ}) at full widths of "
+              f"{a.workload}; each step = every worker's fwd+bwd")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": a.gpus,
+        "steps": steps, "warmup": a.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": a.workload, "batch": 1, "seq": CPU_SAMPLE_SEQ, **wl["cfg"]},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": workers, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(a):
+    import torch
+    import torch.distributed as dist
+    from dop import DOP_BF16, DOP_F32
+    from dop.mixtral import Block
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=dev)
+    wl = WORKLOADS[a.workload]
+    batch, seq = wl["batch"], wl["seq"]
+    T = batch * seq
+    cfg, ll, P = make_params(wl["cfg"], wl["precision"], seed=0, device=dev)  # same weights on every rank
+    prec = DOP_BF16 if wl["precision"] == "bf16" else DOP_F32
+    blk = Block(cfg, batch, seq, prec)
+    bias = None
+    if wl["skew"]:
+        bias = zipf_bias(cfg.experts).to(dev)
+        blk.set_router_bias(bias)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)  # each rank its own batch
+    X = torch.randn(T, cfg.dim, generator=g, device=dev)
+    DY = torch.randn(T, cfg.dim, generator=g, device=dev)
+    Y = torch.empty_like(X)
+    DX = torch.empty_like(X)
+    dP = torch.zeros(ll.total, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        dP.zero_()
+        blk.forward(P, X, Y, stream=stream)
+        blk.backward(P, DY, dP, DX, stream=stream)
+        if world > 1:
+            dist.all_reduce(dP)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    blk.set_timing(True)
+    launches0 = blk.launches()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    phase_acc = {}
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        ev0.record(stream)
+        for _ in range(a.steps):
+            step()
+            # phase events were recorded on `stream` inside the step; read them
+            # after the timed loop would overwrite them, so accumulate lazily
+            for name, ms in blk.phase_times():
+                phase_acc.setdefault(name, []).append(ms)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    launches = blk.launches() - launches0
+    blk.set_timing(False)
+    ms = ev0.elapsed_time(ev1) / a.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    value = world * T / (ms / 1e3)
+
+    # end to end through the public call: pinned host inputs in, dx out
+    e2e = None
+    if not a.no_e2e:
+        hx = torch.randn(T, cfg.dim, generator=torch.Generator().manual_seed(7)).pin_memory()
+        hdy = torch.randn(T, cfg.dim, generator=torch.Generator().manual_seed(8)).pin_memory()
+        hdx = torch.empty(T, cfg.dim).pin_memory()
+
+        def e2e_step():
+            X.copy_(hx, non_blocking=True)
+            DY.copy_(hdy, non_blocking=True)
+            step()
+            hdx.copy_(DX, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(1, min(a.steps, 5))
+        e0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ems = e0.elapsed_time(e1) / n_e2e
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = t.item()
+        e2e = {"value": world * T / (ems / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": 2 * T * cfg.dim * 4, "d2h_bytes_per_step": T * cfg.dim * 4}
+
+    flops = flops_per_step(wl["cfg"], batch, seq)
+    hbm, peak, peak_sus, src = measured_peaks()
+    # dominant kernel: the expert gate/up grouped GEMM (2 * rows * D * 2I FLOPs)
+    gu = phase_acc.get("expert_gate_up", [float("nan")])
+    gu_ms = sum(gu) / len(gu)
+    gu_flops = 2 * T * cfg.top_k * cfg.dim * 2 * cfg.intermediate
+    achieved = gu_flops / (gu_ms / 1e3) / 1e12
+    phases = {k: round(sum(v) / len(v), 3) for k, v in phase_acc.items()}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        ts = cpu_oracle_sample(wl["cfg"], CPU_SAMPLE_SEQ, seed=0, repeats=1)
+        cpu = {"value": CPU_SAMPLE_SEQ / ts[0], "unit": "tokens/s", "cores": 1, "kind": "port",
+               "sample": f"batch 1, seq {CPU_SAMPLE_SEQ} at the full widths of {a.workload}, "
+                         f"one fwd+bwd, single thread"}
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": wl["precision"],
+            "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) x and dy)",
+            "config": {"workload": a.workload, "batch_per_gpu": batch, "seq": seq,
+                       "global_batch": batch * world, **wl["cfg"],
+                       "parallelism": f"dp{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (x, dy are 4 B x T x D each)"},
+            "tflops": flops / (ms / 1e3) / 1e12,
+            "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / peak,
+            "roofline": {"bound": "tensor", "kernel": "expert_gate_up", "achieved": achieved,
+                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "traffic": None, "peak_source": f"{src} bf16_tflops (burst)"},
+            "phases_ms": phases,
+            "e2e": e2e, "gpu_launches": launches // max(1, a.steps) * a.steps,
+            "clocks": clk.summary(), "cpu_baseline": cpu,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    a = ap.parse_args()
+    if a.warmup < 3 and a.impl == "ours":
+        a.warmup = 3
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,389 @@
+// block.cu — the Mixtral block lens on the device.
+//
+// forward  = src/mixtral.rs:291-380 (forward_layer)
+// backward = src/mixtral.rs:434-598 (backward_layer)
+// with the crate's per-token expert loop replaced by the deterministic
+// expert permutation and grouped GEMMs over the expert-sorted rows.
+#include <cstring>
+
+#include "block.cuh"
+
+namespace dop {
+
+LayerOffsets layer_offsets(const dop_mixtral_cfg& c) {
+  LayerOffsets o{};
+  const int64_t D = c.dim, qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim;
+  int64_t at = 0;
+  o.attn_norm = at; at += D;
+  o.q = at; at += D * qd;
+  o.k = at; at += D * kvd;
+  o.v = at; at += D * kvd;
+  o.o = at; at += qd * D;
+  o.ffn_norm = at; at += D;
+  o.router = at; at += D * c.experts;
+  o.gate0 = at;
+  o.up0 = at + D * c.intermediate;
+  o.down0 = at + 2 * D * c.intermediate;
+  o.expert_stride = 3 * D * c.intermediate;
+  o.total = at + c.experts * o.expert_stride;
+  return o;
+}
+
+namespace {
+struct Carver {
+  size_t at = 0;
+  template <typename P>
+  void take(P*& p, size_t bytes, char* base) {
+    at = (at + 255) & ~size_t(255);
+    p = base ? reinterpret_cast<P*>(base + at) : nullptr;
+    at += bytes;
+  }
+};
+}  // namespace
+
+Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision)
+    : cfg(c), B(batch), S(seq), T(batch * seq), prec(precision) {
+  DOP_REQUIRE(batch >= 1 && seq >= 1, "batch and seq must be >= 1");
+  DOP_REQUIRE(c.dim >= 1 && c.heads >= 1 && c.kv_heads >= 1 && c.head_dim >= 2,
+              "bad model widths");
+  DOP_REQUIRE(c.heads % c.kv_heads == 0, "heads must be a multiple of kv_heads");
+  DOP_REQUIRE(c.head_dim % 2 == 0, "head_dim must be even");
+  DOP_REQUIRE(c.experts >= 1 && c.experts <= kMaxExperts, "experts out of range");
+  DOP_REQUIRE(c.top_k >= 1 && c.top_k <= kMaxTopK && c.top_k <= c.experts, "top_k out of range");
+  DOP_REQUIRE(c.sliding_window >= 1, "sliding_window must be >= 1");
+  DOP_REQUIRE(c.intermediate >= 1, "intermediate must be >= 1");
+  DOP_REQUIRE(precision == DOP_F32 || precision == DOP_BF16, "precision must be DOP_F32 or DOP_BF16");
+  DOP_REQUIRE(c.dim <= 1024 * 32, "dim too large");
+  DOP_REQUIRE(T * c.top_k < (int64_t)1 << 30, "too many tokens");
+  off = layer_offsets(c);
+  const int64_t D = c.dim, E = c.experts, K = c.top_k, I = c.intermediate;
+  const int64_t qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim;
+  rows_cap = round_up(T * K + E * (kRowAlign - 1), kRowAlign);
+  max_tiles = (int)(rows_cap / kRowAlign);
+  const size_t a = prec == DOP_F32 ? 4 : 2;  // activation element size
+  const int64_t chunks = ceil_div(T * K, kPermChunk);
+  part_cap = std::max<int64_t>((int64_t)sm_count() * 4 * D, 64 * D * E);
+  part_cap = std::max<int64_t>(part_cap, 64 * std::max(qd, D));
+
+  auto carve = [&](char* base_) {
+    Carver cv;
+    cv.take(x_in, 4 * T * D, base_);
+    cv.take(inv1, 4 * T, base_);
+    cv.take(mid, 4 * T * D, base_);
+    cv.take(inv2, 4 * T, base_);
+    cv.take(lse, 4 * T * c.heads, base_);
+    cv.take(probs, 4 * T * E, base_);
+    cv.take(top_p, 4 * T * K, base_);
+    cv.take(top_w, 4 * T * K, base_);
+    cv.take(row_w, 4 * rows_cap, base_);
+    cv.take(out, 4 * rows_cap * D, base_);
+    cv.take(top_i, 4 * T * K, base_);
+    cv.take(slot_row, 4 * T * K, base_);
+    cv.take(seg_off, 4 * (E + 1), base_);
+    cv.take(tile_expert, 4 * max_tiles, base_);
+    cv.take(row_token, 4 * rows_cap, base_);
+    cv.take(chunk_counts, 4 * chunks * E, base_);
+    cv.take(xn, a * T * D, base_);
+    cv.take(q, a * T * qd, base_);
+    cv.take(k, a * T * kvd, base_);
+    cv.take(v, a * T * kvd, base_);
+    cv.take(mix, a * T * qd, base_);
+    cv.take(xn2, a * T * D, base_);
+    cv.take(xp, a * rows_cap * D, base_);
+    cv.take(g, a * rows_cap * I, base_);
+    cv.take(u, a * rows_cap * I, base_);
+    cv.take(h, a * rows_cap * I, base_);
+    cv.take(qpre, 4 * T * qd, base_);
+    cv.take(kpre, 4 * T * kvd, base_);
+    cv.take(rope_cos, 4 * S * (c.head_dim / 2), base_);
+    cv.take(rope_sin, 4 * S * (c.head_dim / 2), base_);
+    cv.take(dz, 4 * T * E, base_);
+    cv.take(dh, 4 * rows_cap * I, base_);
+    cv.take(dxp, 4 * rows_cap * D, base_);
+    cv.take(dxn2, 4 * T * D, base_);
+    cv.take(dmid, 4 * T * D, base_);
+    cv.take(dxn, 4 * T * D, base_);
+    cv.take(dq, 4 * T * qd, base_);
+    cv.take(dk, 4 * T * kvd, base_);
+    cv.take(dv, 4 * T * kvd, base_);
+    cv.take(delta, 4 * T * c.heads, base_);
+    cv.take(part, 4 * part_cap, base_);
+    cv.take(dO, a * rows_cap * D, base_);
+    cv.take(dg, a * rows_cap * I, base_);
+    cv.take(du, a * rows_cap * I, base_);
+    cv.take(dmid_a, a * T * D, base_);
+    cv.take(dmix, a * T * qd, base_);
+    cv.take(dq_a, a * T * qd, base_);
+    cv.take(dk_a, a * T * kvd, base_);
+    cv.take(dv_a, a * T * kvd, base_);
+    return cv.at;
+  };
+  bytes = carve(nullptr);
+  cudaError_t e = cudaMalloc(&base, bytes);
+  if (e != cudaSuccess) {
+    base = nullptr;
+    throw Error(DOP_E_NOMEM, "cudaMalloc of " + std::to_string(bytes) + " bytes for the block: " +
+                                 cudaGetErrorString(e));
+  }
+  carve(base);
+  // RoPE table (positions 0..S-1) once per handle.
+  rope_table((int)S, (int)c.head_dim, c.rope_theta, rope_cos, rope_sin, 0, launches);
+  DOP_CHECK_CUDA(cudaStreamSynchronize(0));
+}
+
+Block::~Block() {
+  for (auto& p : phases) {
+    cudaEventDestroy(p.a);
+    cudaEventDestroy(p.b);
+  }
+  if (base) cudaFree(base);
+}
+
+void Block::ph_begin(const char* name, cudaStream_t s) {
+  if (!timing) return;
+  if (n_phases == phases.size()) {
+    Phase p{name, nullptr, nullptr};
+    DOP_CHECK_CUDA(cudaEventCreate(&p.a));
+    DOP_CHECK_CUDA(cudaEventCreate(&p.b));
+    phases.push_back(p);
+  }
+  phases[n_phases].name = name;
+  DOP_CHECK_CUDA(cudaEventRecord(phases[n_phases].a, s));
+}
+
+void Block::ph_end(cudaStream_t s) {
+  if (!timing) return;
+  DOP_CHECK_CUDA(cudaEventRecord(phases[n_phases].b, s));
+  ++n_phases;
+}
+
+template <typename Act>
+void Block::gemm(const Gemm& g, cudaStream_t s) {
+  gemm_simt<Act>(g, s, launches);
+}
+
+void Block::forward(const void* params, const float* x, float* y, cudaStream_t s) {
+  DOP_REQUIRE(params && x && y, "null pointer");
+  n_phases = 0;
+  if (prec == DOP_F32) fwd<float>((const float*)params, x, y, s);
+  else fwd<bf16>((const bf16*)params, x, y, s);
+  n_fwd_phases = n_phases;
+  have_tape = true;
+}
+
+void Block::backward(const void* params, const float* dy, float* dx, float* dparams,
+                     cudaStream_t s) {
+  DOP_REQUIRE(params && dy && dx && dparams, "null pointer");
+  if (!have_tape) throw Error(DOP_E_STATE, "backward called before forward");
+  n_phases = n_fwd_phases;
+  if (prec == DOP_F32) bwd<float>((const float*)params, dy, dx, dparams, s);
+  else bwd<bf16>((const bf16*)params, dy, dx, dparams, s);
+}
+
+template <typename Act>
+void Block::fwd(const Act* P, const float* x, float* y, cudaStream_t s) {
+  const int64_t D = cfg.dim, E = cfg.experts, K = cfg.top_k, I = cfg.intermediate;
+  const int H = (int)cfg.heads, KV = (int)cfg.kv_heads, hd = (int)cfg.head_dim;
+  const int64_t qd = (int64_t)H * hd, kvd = (int64_t)KV * hd;
+  Act* xn_ = (Act*)xn; Act* q_ = (Act*)q; Act* k_ = (Act*)k; Act* v_ = (Act*)v; Act* mix_ = (Act*)mix;
+  Act* xn2_ = (Act*)xn2; Act* xp_ = (Act*)xp; Act* g_ = (Act*)g; Act* u_ = (Act*)u; Act* h_ = (Act*)h;
+
+  // attention half: xn = rmsnorm(x); q,k,v = xn W; rope; gqa; mid = x + mix Wo
+  ph_begin("attn_norm", s);
+  rmsnorm_fwd<Act>(x, P + off.attn_norm, T, (int)D, cfg.rms_eps, xn_, inv1, x_in, s, launches);
+  ph_end(s);
+  ph_begin("qkv_gemm", s);
+  {
+    Gemm gq; gq.M = T; gq.N = qd; gq.K = D; gq.A = xn_; gq.lda = D; gq.B = P + off.q; gq.ldb = qd;
+    gq.C = qpre; gq.ldc = qd; gemm<Act>(gq, s);
+    Gemm gk = gq; gk.N = kvd; gk.B = P + off.k; gk.ldb = kvd; gk.C = kpre; gk.ldc = kvd;
+    gemm<Act>(gk, s);
+    Gemm gv = gk; gv.B = P + off.v; gv.C = v_; gv.c_f32 = std::is_same<Act, float>::value;
+    gemm<Act>(gv, s);
+  }
+  ph_end(s);
+  ph_begin("rope", s);
+  rope<float, Act>(qpre, q_, T, (int)S, H, hd, rope_cos, rope_sin, 1.f, s, launches);
+  rope<float, Act>(kpre, k_, T, (int)S, KV, hd, rope_cos, rope_sin, 1.f, s, launches);
+  Attn at; at.B = B; at.S = S; at.H = H; at.KV = KV; at.hd = hd; at.window = cfg.sliding_window;
+  at.causal = true; at.scale = 1.0f / sqrtf((float)hd);
+  ph_end(s);
+  ph_begin("attn_fwd", s);
+  attn_fwd_simt<Act>(at, q_, k_, v_, mix_, lse, s, launches);
+  ph_end(s);
+  ph_begin("o_gemm", s);
+  {
+    Gemm go; go.M = T; go.N = D; go.K = qd; go.A = mix_; go.lda = qd; go.B = P + off.o; go.ldb = D;
+    go.C = mid; go.ldc = D; go.epi = Epi::AddRes; go.R = x; go.ldr = D;
+    gemm<Act>(go, s);
+  }
+  ph_end(s);
+  // mixture half: xn2 = rmsnorm(mid); router; permute; experts; y = mid + mixed
+  ph_begin("ffn_norm_router", s);
+  rmsnorm_router<Act>(mid, P + off.ffn_norm, P + off.router, router_bias, T, (int)D, (int)E,
+                    (int)K, cfg.rms_eps, xn2_, inv2, probs, top_i, top_p, top_w, s, launches);
+  ph_end(s);
+  ph_begin("permute", s);
+  permute(top_i, top_w, T, (int)E, (int)K, chunk_counts, seg_off, tile_expert, max_tiles,
+          slot_row, row_token, row_w, rows_cap, s, launches);
+  gather_rows<Act>(xn2_, row_token, seg_off, (int)E, (int)D, rows_cap, xp_, s, launches);
+  ph_end(s);
+  ph_begin("expert_gate_up", s);
+  {
+    Gemm gg; gg.M = rows_cap; gg.N = I; gg.K = D; gg.A = xp_; gg.lda = D;
+    gg.B = P + off.gate0; gg.ldb = I; gg.C = g_; gg.ldc = I; gg.c_f32 = std::is_same<Act, float>::value;
+    gg.group = 1; gg.seg_off = seg_off; gg.tile_expert = tile_expert; gg.G = (int)E;
+    gg.b_gs = off.expert_stride;
+    gemm<Act>(gg, s);
+    Gemm gu = gg; gu.B = P + off.up0; gu.C = u_;
+    gemm<Act>(gu, s);
+  }
+  ph_end(s);
+  ph_begin("swiglu", s);
+  silu_mul<Act>(g_, u_, seg_off, (int)E, I, rows_cap, h_, s, launches);
+  ph_end(s);
+  ph_begin("expert_down", s);
+  {
+    Gemm gd; gd.M = rows_cap; gd.N = D; gd.K = I; gd.A = h_; gd.lda = I;
+    gd.B = P + off.down0; gd.ldb = D; gd.C = out; gd.ldc = D;
+    gd.group = 1; gd.seg_off = seg_off; gd.tile_expert = tile_expert; gd.G = (int)E;
+    gd.b_gs = off.expert_stride;
+    gemm<Act>(gd, s);
+  }
+  ph_end(s);
+  ph_begin("combine", s);
+  combine(mid, out, slot_row, top_w, T, (int)K, (int)D, y, s, launches);
+  ph_end(s);
+}
+
+template <typename Act>
+void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_t s) {
+  const int64_t D = cfg.dim, E = cfg.experts, K = cfg.top_k, I = cfg.intermediate;
+  const int H = (int)cfg.heads, KV = (int)cfg.kv_heads, hd = (int)cfg.head_dim;
+  const int64_t qd = (int64_t)H * hd, kvd = (int64_t)KV * hd;
+  const bool f32 = std::is_same<Act, float>::value;
+  Act* xn_ = (Act*)xn; Act* q_ = (Act*)q; Act* k_ = (Act*)k; Act* v_ = (Act*)v; Act* mix_ = (Act*)mix;
+  Act* xp_ = (Act*)xp; Act* g_ = (Act*)g; Act* u_ = (Act*)u; Act* h_ = (Act*)h;
+  Act* dO_ = (Act*)dO; Act* dg_ = (Act*)dg; Act* du_ = (Act*)du; Act* dmid_ = (Act*)dmid_a; Act* dmix_ = (Act*)dmix;
+  Act* dq_ = (Act*)dq_a; Act* dk_ = (Act*)dk_a; Act* dv_ = (Act*)dv_a;
+
+  // router Jacobian and the down projection's output cotangent
+  ph_begin("router_bwd", s);
+  router_bwd(dy, out, slot_row, top_i, top_p, top_w, probs, T, (int)E, (int)K, (int)D, dz, s,
+             launches);
+  gather_scale_rows<Act>(dy, row_token, row_w, seg_off, (int)E, (int)D, rows_cap, dO_, s, launches);
+  // dH = dO Wd^T (Wd_e is [I, D]); SwiGLU adjoint
+  ph_end(s);
+  ph_begin("expert_dh", s);
+  {
+    Gemm g1; g1.M = rows_cap; g1.N = I; g1.K = D; g1.A = dO_; g1.lda = D;
+    g1.B = P + off.down0; g1.ldb = D; g1.b_t = true; g1.C = dh; g1.ldc = I;
+    g1.group = 1; g1.seg_off = seg_off; g1.tile_expert = tile_expert; g1.G = (int)E;
+    g1.b_gs = off.expert_stride;
+    gemm<Act>(g1, s);
+  }
+  ph_end(s);
+  ph_begin("swiglu_bwd", s);
+  silu_mul_bwd<Act>(dh, g_, u_, seg_off, (int)E, I, rows_cap, dg_, du_, s, launches);
+  // dWd_e += H^T dO over expert e's rows
+  ph_end(s);
+  ph_begin("expert_dw_down", s);
+  {
+    Gemm g2; g2.M = I; g2.N = D; g2.A = h_; g2.lda = I; g2.a_t = true; g2.B = dO_; g2.ldb = D;
+    g2.C = dP + off.down0; g2.ldc = D; g2.epi = Epi::Accum;
+    g2.group = 2; g2.seg_off = seg_off; g2.G = (int)E; g2.c_gs = off.expert_stride;
+    gemm<Act>(g2, s);
+  }
+  // dXp = dG Wg^T + dU Wu^T (Wg_e, Wu_e are [D, I])
+  ph_end(s);
+  ph_begin("expert_dx", s);
+  {
+    Gemm g3; g3.M = rows_cap; g3.N = D; g3.K = I; g3.A = dg_; g3.lda = I;
+    g3.B = P + off.gate0; g3.ldb = I; g3.b_t = true; g3.C = dxp; g3.ldc = D;
+    g3.group = 1; g3.seg_off = seg_off; g3.tile_expert = tile_expert; g3.G = (int)E;
+    g3.b_gs = off.expert_stride;
+    gemm<Act>(g3, s);
+    Gemm g4 = g3; g4.A = du_; g4.B = P + off.up0; g4.epi = Epi::Accum;
+    gemm<Act>(g4, s);
+  }
+  // dWg_e += Xp^T dG, dWu_e += Xp^T dU
+  ph_end(s);
+  ph_begin("expert_dw_gate_up", s);
+  {
+    Gemm g5; g5.M = D; g5.N = I; g5.A = xp_; g5.lda = D; g5.a_t = true; g5.B = dg_; g5.ldb = I;
+    g5.C = dP + off.gate0; g5.ldc = I; g5.epi = Epi::Accum;
+    g5.group = 2; g5.seg_off = seg_off; g5.G = (int)E; g5.c_gs = off.expert_stride;
+    gemm<Act>(g5, s);
+    Gemm g6 = g5; g6.B = du_; g6.C = dP + off.up0;
+    gemm<Act>(g6, s);
+  }
+  // d_xn2 = sum_k dXp[row(t,k)] + dz Wr^T; router weight adjoint
+  ph_end(s);
+  ph_begin("unpermute_router", s);
+  unpermute_router_dx<Act>(dxp, slot_row, dz, P + off.router, T, (int)E, (int)K, (int)D, dxn2, s,
+                         launches);
+  router_dw<Act>(mid, inv2, P + off.ffn_norm, dz, T, (int)D, (int)E, dP + off.router, part,
+               part_cap, s, launches);
+  // d_mid = rmsnorm_bwd(d_xn2) + dy
+  ph_end(s);
+  ph_begin("ffn_norm_bwd", s);
+  rmsnorm_bwd<Act>(dxn2, mid, inv2, P + off.ffn_norm, dy, T, (int)D, dmid, f32 ? nullptr : dmid_,
+                 dP + off.ffn_norm, part, part_cap, s, launches);
+  const Act* dmid_op = f32 ? (const Act*)dmid : dmid_;
+  // d_mix = d_mid Wo^T (Wo is [qd, D]); dWo += mix^T d_mid
+  ph_end(s);
+  ph_begin("o_grad", s);
+  {
+    Gemm g7; g7.M = T; g7.N = qd; g7.K = D; g7.A = dmid_op; g7.lda = D;
+    g7.B = P + off.o; g7.ldb = D; g7.b_t = true; g7.C = dmix_; g7.ldc = qd; g7.c_f32 = f32;
+    gemm<Act>(g7, s);
+    Gemm g8; g8.M = qd; g8.N = D; g8.K = T; g8.A = mix_; g8.lda = qd; g8.a_t = true;
+    g8.B = dmid_op; g8.ldb = D; g8.C = dP + off.o; g8.ldc = D; g8.epi = Epi::Accum;
+    gemm<Act>(g8, s);
+  }
+  ph_end(s);
+  ph_begin("attn_bwd", s);
+  Attn at; at.B = B; at.S = S; at.H = H; at.KV = KV; at.hd = hd; at.window = cfg.sliding_window;
+  at.causal = true; at.scale = 1.0f / sqrtf((float)hd);
+  attn_bwd_simt<Act>(at, q_, k_, v_, mix_, dmix_, lse, delta, dq, dk, dv, s, launches);
+  ph_end(s);
+  ph_begin("rope_bwd", s);
+  rope<float, Act>(dq, dq_, T, (int)S, H, hd, rope_cos, rope_sin, -1.f, s, launches);
+  rope<float, Act>(dk, dk_, T, (int)S, KV, hd, rope_cos, rope_sin, -1.f, s, launches);
+  const Act* dv_op;
+  if (f32) dv_op = (const Act*)dv;
+  else { convert<Act>(dv, dv_, T * kvd, s, launches); dv_op = dv_; }
+  ph_end(s);
+  ph_begin("qkv_dgrad", s);
+  // d_xn = dq Wq^T + dk Wk^T + dv Wv^T
+  {
+    Gemm a1; a1.M = T; a1.N = D; a1.K = qd; a1.A = dq_; a1.lda = qd; a1.B = P + off.q;
+    a1.ldb = qd; a1.b_t = true; a1.C = dxn; a1.ldc = D;
+    gemm<Act>(a1, s);
+    Gemm a2 = a1; a2.K = kvd; a2.A = dk_; a2.lda = kvd; a2.B = P + off.k; a2.ldb = kvd;
+    a2.epi = Epi::Accum;
+    gemm<Act>(a2, s);
+    Gemm a3 = a2; a3.A = dv_op; a3.B = P + off.v;
+    gemm<Act>(a3, s);
+  }
+  ph_end(s);
+  ph_begin("qkv_wgrad", s);
+  // dWq += xn^T dq, dWk += xn^T dk, dWv += xn^T dv
+  {
+    Gemm w1; w1.M = D; w1.N = qd; w1.K = T; w1.A = xn_; w1.lda = D; w1.a_t = true; w1.B = dq_;
+    w1.ldb = qd; w1.C = dP + off.q; w1.ldc = qd; w1.epi = Epi::Accum;
+    gemm<Act>(w1, s);
+    Gemm w2 = w1; w2.N = kvd; w2.B = dk_; w2.ldb = kvd; w2.C = dP + off.k; w2.ldc = kvd;
+    gemm<Act>(w2, s);
+    Gemm w3 = w2; w3.B = dv_op; w3.C = dP + off.v;
+    gemm<Act>(w3, s);
+  }
+  ph_end(s);
+  // dx = rmsnorm_bwd(d_xn) + d_mid
+  ph_begin("attn_norm_bwd", s);
+  rmsnorm_bwd<Act>(dxn, x_in, inv1, P + off.attn_norm, dmid, T, (int)D, dx, (Act*)nullptr,
+                 dP + off.attn_norm, part, part_cap, s, launches);
+  ph_end(s);
+}
+
+}  // namespace dop

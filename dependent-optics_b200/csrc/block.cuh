@@ -1,0 +1,65 @@
+// block.cuh — the Mixtral block lens (get = forward, put = backward) and its
+// device residual.
+#pragma once
+
+#include "../../include/dop.h"
+#include <vector>
+
+#include "kernels.cuh"
+
+namespace dop {
+
+// Offsets of one layer's parameters inside its slice (src/mixtral.rs:135-171).
+struct LayerOffsets {
+  int64_t attn_norm, q, k, v, o, ffn_norm, router, gate0, up0, down0, expert_stride, total;
+};
+LayerOffsets layer_offsets(const dop_mixtral_cfg& c);
+
+// Device residual of one block.  Unlike the crate's LayerTape
+// (src/mixtral.rs:212-228) it holds the attention log-sum-exp instead of the
+// probabilities, the post-RoPE q/k instead of the pre-RoPE ones, and the
+// expert activations in expert-sorted (permuted) order.
+struct Block {
+  dop_mixtral_cfg cfg{};
+  int64_t B = 0, S = 0, T = 0;
+  int prec = DOP_F32;
+  LayerOffsets off{};
+  int64_t rows_cap = 0;   // capacity of the expert-sorted buffers
+  int max_tiles = 0;      // rows_cap / kRowAlign
+  int64_t launches = 0;
+  bool have_tape = false;
+  const float* router_bias = nullptr;
+  size_t bytes = 0;
+  char* base = nullptr;   // one device allocation, carved below
+
+  // residual (forward -> backward)
+  float *x_in, *inv1, *mid, *inv2, *lse, *probs, *top_p, *top_w, *row_w, *out;
+  int *top_i, *slot_row, *seg_off, *tile_expert, *row_token, *chunk_counts;
+  void *xn, *q, *k, *v, *mix, *xn2, *xp, *g, *u, *h;
+  // forward scratch
+  float *qpre, *kpre, *rope_cos, *rope_sin;
+  // backward scratch
+  float *dz, *dh, *dxp, *dxn2, *dmid, *dxn, *dq, *dk, *dv, *delta, *part;
+  int64_t part_cap;
+  void *dO, *dg, *du, *dmid_a, *dmix, *dq_a, *dk_a, *dv_a;
+
+  // per-phase CUDA-event timing (dop_block_set_timing)
+  struct Phase { const char* name; cudaEvent_t a, b; };
+  bool timing = false;
+  std::vector<Phase> phases;
+  size_t n_phases = 0, n_fwd_phases = 0;
+  void ph_begin(const char* name, cudaStream_t s);
+  void ph_end(cudaStream_t s);
+
+  Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision);
+  ~Block();
+  void forward(const void* params, const float* x, float* y, cudaStream_t s);
+  void backward(const void* params, const float* dy, float* dx, float* dparams, cudaStream_t s);
+
+ private:
+  template <typename Act> void fwd(const Act* P, const float* x, float* y, cudaStream_t s);
+  template <typename Act> void bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_t s);
+  template <typename Act> void gemm(const Gemm& g, cudaStream_t s);
+};
+
+}  // namespace dop

@@ -1,0 +1,783 @@
+// elementwise.cu — the memory-bound kernels of the Mixtral block lens:
+// RMSNorm forward (+ fused router softmax/top-k), RMSNorm backward with a
+// deterministic weight reduction, rotary embedding and its adjoint, the
+// deterministic expert permutation (count / scan / stable scatter), row
+// gather/combine, SwiGLU forward/backward, and the router Jacobian.
+//
+// Every reduction that produces a parameter adjoint is two-stage (per-chunk
+// partials in a fixed order, then a fixed-order sum): no floating-point
+// atomics, so two runs give the same bits.
+#include "kernels.cuh"
+
+namespace dop {
+
+// ---------------------------------------------------------------- RMSNorm
+// rmsnorm (src/mixtral.rs:667-684): r = 1 / sqrt(sum(x^2)/D + eps),
+// y = x * r * w.  One CTA per token row.
+template <typename T>
+__global__ void k_rmsnorm_fwd(const float* __restrict__ x, const T* __restrict__ w, int D,
+                              float eps, T* __restrict__ y, float* __restrict__ inv,
+                              float* __restrict__ x_copy) {
+  const int64_t row = blockIdx.x;
+  const float* xr = x + row * D;
+  __shared__ float red[32];
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float v = xr[i];
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float mean = red[0] / (float)D + eps;
+  const float r = 1.0f / sqrtf(mean);
+  if (threadIdx.x == 0) inv[row] = r;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float v = xr[i];
+    st(&y[row * D + i], v * r * ld(&w[i]));
+    if (x_copy) x_copy[row * D + i] = v;
+  }
+}
+
+// RMSNorm of the feed-forward input fused with the router (src/mixtral.rs:
+// 311-327, softmax :924-929, topk_renorm :931-939).  Router logits are
+// computed in fp32 from the fp32 normalised row (not from its rounded copy),
+// so routing decisions only differ from the fp32 lens at near-ties.
+// Tie-break: higher probability first, then lower expert index.
+template <typename T>
+__global__ void k_rmsnorm_router(const float* __restrict__ x, const T* __restrict__ w,
+                                 const T* __restrict__ wr, const float* __restrict__ bias, int D,
+                                 int E, int K, float eps, T* __restrict__ y,
+                                 float* __restrict__ inv, float* __restrict__ probs,
+                                 int* __restrict__ top_i, float* __restrict__ top_p,
+                                 float* __restrict__ top_w) {
+  const int64_t row = blockIdx.x;
+  const float* xr = x + row * D;
+  __shared__ float red[32];
+  __shared__ float lg[kMaxExperts * 8];  // per-warp partial logits (<= 8 warps)
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float v = xr[i];
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float r = 1.0f / sqrtf(red[0] / (float)D + eps);
+  if (threadIdx.x == 0) inv[row] = r;
+  float part[kMaxExperts];
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) part[e] = 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float xn = xr[i] * r * ld(&w[i]);
+    st(&y[row * D + i], xn);
+#pragma unroll
+    for (int e = 0; e < kMaxExperts; ++e)
+      if (e < E) part[e] += xn * ld(&wr[(int64_t)i * E + e]);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) {
+    if (e < E) {
+      float v = warp_sum(part[e]);
+      if (lane == 0) lg[warp * kMaxExperts + e] = v;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int nw = blockDim.x >> 5;
+    float z[kMaxExperts], p[kMaxExperts];
+    float m = -INFINITY;
+    for (int e = 0; e < E; ++e) {
+      float v = 0.f;
+      for (int q = 0; q < nw; ++q) v += lg[q * kMaxExperts + e];
+      if (bias) v += bias[e];
+      z[e] = v;
+      m = fmaxf(m, v);
+    }
+    float s = 0.f;
+    for (int e = 0; e < E; ++e) {
+      p[e] = expf(z[e] - m);
+    }
+    for (int e = 0; e < E; ++e) s += p[e];
+    for (int e = 0; e < E; ++e) {
+      p[e] = p[e] / s;
+      probs[row * E + e] = p[e];
+    }
+    uint64_t taken = 0;
+    int idx[kMaxTopK];
+    float pk[kMaxTopK];
+    for (int k = 0; k < K; ++k) {
+      int best = -1;
+      for (int e = 0; e < E; ++e) {
+        if (taken >> e & 1) continue;
+        if (best < 0 || p[e] > p[best]) best = e;
+      }
+      taken |= 1ull << best;
+      idx[k] = best;
+      pk[k] = p[best];
+    }
+    float sk = 0.f;
+    for (int k = 0; k < K; ++k) sk += pk[k];
+    for (int k = 0; k < K; ++k) {
+      top_i[row * K + k] = idx[k];
+      top_p[row * K + k] = pk[k];
+      top_w[row * K + k] = pk[k] / sk;
+    }
+  }
+}
+
+// rmsnorm_bwd (src/mixtral.rs:696-723) for a chunk of rows per CTA:
+// dx = r (dy*w - xhat * mean(dy*w*xhat)) (+ res), and this chunk's partial of
+// dw[i] = sum_t dy[t,i] * xhat[t,i], written to dw_part[chunk, i].
+// blockDim.x * vec covers D; each thread owns D / blockDim.x columns.
+template <typename T>
+__global__ void k_rmsnorm_bwd(const float* __restrict__ dy, const float* __restrict__ x,
+                              const float* __restrict__ inv, const T* __restrict__ w,
+                              const float* __restrict__ res, int64_t rows, int D,
+                              int rows_per_chunk, float* __restrict__ dx, T* __restrict__ dx_act,
+                              float* __restrict__ dw_part) {
+  const int chunk = blockIdx.x;
+  const int64_t r0 = (int64_t)chunk * rows_per_chunk;
+  const int64_t r1 = ::min((int64_t)(rows), (int64_t)(r0 + rows_per_chunk));
+  __shared__ float red[32];
+  constexpr int kCols = 32;  // max columns per thread (D <= 32 * blockDim)
+  float dwacc[kCols];
+  float wv[kCols];
+  const int per = (D + blockDim.x - 1) / blockDim.x;
+#pragma unroll
+  for (int c = 0; c < kCols; ++c) {
+    dwacc[c] = 0.f;
+    int i = threadIdx.x + c * blockDim.x;
+    wv[c] = (c < per && i < D) ? ld(&w[i]) : 0.f;
+  }
+  for (int64_t t = r0; t < r1; ++t) {
+    const float r = inv[t];
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < kCols; ++c) {
+      int i = threadIdx.x + c * blockDim.x;
+      if (c < per && i < D) {
+        float xhat = x[t * D + i] * r;
+        float g = dy[t * D + i];
+        dwacc[c] += g * xhat;
+        dot += g * wv[c] * xhat;
+      }
+    }
+    dot = warp_sum(dot);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = dot;
+    __syncthreads();
+    float tot = 0.f;
+    for (int q = 0; q < (int)(blockDim.x >> 5); ++q) tot += red[q];
+    const float mean = tot / (float)D;
+#pragma unroll
+    for (int c = 0; c < kCols; ++c) {
+      int i = threadIdx.x + c * blockDim.x;
+      if (c < per && i < D) {
+        float xhat = x[t * D + i] * r;
+        float v = r * (dy[t * D + i] * wv[c] - xhat * mean);
+        if (res) v += res[t * D + i];
+        dx[t * D + i] = v;
+        if (dx_act) st(&dx_act[t * D + i], v);
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < kCols; ++c) {
+    int i = threadIdx.x + c * blockDim.x;
+    if (c < per && i < D) dw_part[(int64_t)chunk * D + i] = dwacc[c];
+  }
+}
+
+// out[i] += sum_{c < chunks} part[c, i] in chunk order (deterministic).
+__global__ void k_reduce_chunks(const float* __restrict__ part, int chunks, int64_t n,
+                                float* __restrict__ out) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float s = 0.f;
+  for (int c = 0; c < chunks; ++c) s += part[(int64_t)c * n + i];
+  out[i] += s;
+}
+
+// ------------------------------------------------------------------ RoPE
+// rope_angles (src/mixtral.rs:725-739): freq_i = theta^(-(2i)/hd), angle =
+// pos * freq_i, one table row per position.
+__global__ void k_rope_table(int S, int half, int hd, float theta, float* __restrict__ cs,
+                             float* __restrict__ sn) {
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)S * half) return;
+  int s = (int)(idx / half), i = (int)(idx % half);
+  float freq = powf(theta, -(2.0f * (float)i) / (float)hd);
+  float ang = (float)s * freq;
+  float sv, cv;
+  sincosf(ang, &sv, &cv);
+  cs[idx] = cv;
+  sn[idx] = sv;
+}
+
+// rope_one (src/mixtral.rs:741-753) over [T, heads, hd]; sign -1 is the
+// adjoint (rope_qkv_transpose, :777-797).  pos = t mod S.
+template <typename TI, typename TO>
+__global__ void k_rope(const TI* __restrict__ src, TO* __restrict__ dst, int64_t T, int S,
+                       int heads, int hd, const float* __restrict__ cs,
+                       const float* __restrict__ sn, float sign) {
+  const int half = hd / 2;
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t total = T * heads * half;
+  if (idx >= total) return;
+  int i = (int)(idx % half);
+  int64_t th = idx / half;  // t * heads + h
+  int64_t t = th / heads;
+  int pos = (int)(t % S);
+  int64_t base = th * hd;
+  float c = cs[(int64_t)pos * half + i], s = sign * sn[(int64_t)pos * half + i];
+  float q1 = ld(&src[base + i]), q2 = ld(&src[base + half + i]);
+  st(&dst[base + i], q1 * c - q2 * s);
+  st(&dst[base + half + i], q2 * c + q1 * s);
+}
+
+// ------------------------------------------------- expert permutation (K7)
+// The canonical order of the (token, slot) pairs routed to an expert is the
+// token-major order (t, then slot): a stable counting sort by expert.  Each
+// expert's segment starts at a multiple of kRowAlign rows, so a GEMM row tile
+// never straddles two experts and padded rows can be zero.
+//
+// Pass 1: per chunk of kPermChunk pairs, count pairs per expert.
+__global__ void k_perm_count(const int* __restrict__ top_i, int64_t pairs, int E,
+                             int* __restrict__ chunk_counts) {
+  __shared__ int cnt[kMaxExperts];
+  if (threadIdx.x < kMaxExperts) cnt[threadIdx.x] = 0;
+  __syncthreads();
+  int64_t p = (int64_t)blockIdx.x * kPermChunk + threadIdx.x;
+  for (int q = 0; q < kPermChunk / (int)blockDim.x; ++q, p += blockDim.x)
+    if (p < pairs) atomicAdd(&cnt[top_i[p]], 1);  // integer: order-free
+  __syncthreads();
+  if (threadIdx.x < E) chunk_counts[(int64_t)blockIdx.x * E + threadIdx.x] = cnt[threadIdx.x];
+}
+
+// Pass 2 (one CTA): exclusive scan over chunks per expert, padded segment
+// offsets seg_off[E+1], and the row-tile -> expert map of the padded buffer.
+__global__ void k_perm_scan(int* __restrict__ chunk_counts, int chunks, int E,
+                            int* __restrict__ seg_off, int* __restrict__ tile_expert,
+                            int max_tiles) {
+  __shared__ int tot[kMaxExperts];
+  int e = threadIdx.x;
+  if (e < E) {
+    int run = 0;
+    for (int c = 0; c < chunks; ++c) {
+      int v = chunk_counts[(int64_t)c * E + e];
+      chunk_counts[(int64_t)c * E + e] = run;
+      run += v;
+    }
+    tot[e] = run;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int off = 0;
+    for (int q = 0; q < E; ++q) {
+      seg_off[q] = off;
+      off += (tot[q] + kRowAlign - 1) / kRowAlign * kRowAlign;
+    }
+    seg_off[E] = off;
+  }
+  __syncthreads();
+  for (int tile = threadIdx.x; tile < max_tiles; tile += blockDim.x) {
+    int row = tile * kRowAlign, ex = -1;
+    for (int q = 0; q < E; ++q)
+      if (row >= seg_off[q] && row < seg_off[q + 1]) ex = q;
+    tile_expert[tile] = ex;
+  }
+}
+
+// Pass 3: stable scatter.  Pair p's row = seg_off[e] + (pairs of expert e in
+// earlier chunks) + (pairs of expert e earlier in this chunk).  The in-chunk
+// rank uses warp match masks and a per-warp count table, so the result is
+// the same on every run.
+__global__ void k_perm_scatter(const int* __restrict__ top_i, const float* __restrict__ top_w,
+                               int64_t pairs, int E, int K, const int* __restrict__ chunk_base,
+                               const int* __restrict__ seg_off, int* __restrict__ slot_row,
+                               int* __restrict__ row_token, float* __restrict__ row_w) {
+  __shared__ int wcnt[kPermChunk / 32][kMaxExperts];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = kPermChunk / 32;
+  for (int i = threadIdx.x; i < nwarps * kMaxExperts; i += blockDim.x)
+    (&wcnt[0][0])[i] = 0;
+  __syncthreads();
+  const int64_t p = (int64_t)blockIdx.x * kPermChunk + threadIdx.x;
+  const bool valid = p < pairs;
+  const int e = valid ? top_i[p] : -1;
+  const unsigned same = __match_any_sync(0xffffffffu, e);
+  const int rank_in_warp = __popc(same & ((1u << lane) - 1u));
+  if (valid && rank_in_warp == 0) wcnt[warp][e] = __popc(same);
+  __syncthreads();
+  if (valid) {
+    int before = 0;
+    for (int q = 0; q < warp; ++q) before += wcnt[q][e];
+    int row = seg_off[e] + chunk_base[(int64_t)blockIdx.x * E + e] + before + rank_in_warp;
+    slot_row[p] = row;
+    row_token[row] = (int)(p / K);
+    row_w[row] = top_w[p];
+  }
+}
+
+// Xp[r] = xn[row_token[r]] (zero rows for padding).  One CTA per row.
+template <typename T>
+__global__ void k_gather_rows(const T* __restrict__ src, const int* __restrict__ row_token,
+                              const int* __restrict__ seg_off, int E, int D, T* __restrict__ dst) {
+  const int64_t r = blockIdx.x;
+  if (r >= seg_off[E]) return;
+  const int t = row_token[r];
+  for (int i = threadIdx.x; i < D; i += blockDim.x)
+    dst[r * D + i] = t >= 0 ? src[(int64_t)t * D + i] : T(0.f);
+}
+
+// dO[r] = row_w[r] * dy[row_token[r]] (zero rows for padding): the down
+// projection's output cotangent, d_out = w * d_mixed (src/mixtral.rs:474-477).
+template <typename T>
+__global__ void k_gather_scale_rows(const float* __restrict__ src, const int* __restrict__ row_token,
+                                    const float* __restrict__ row_w,
+                                    const int* __restrict__ seg_off, int E, int D,
+                                    T* __restrict__ dst) {
+  const int64_t r = blockIdx.x;
+  if (r >= seg_off[E]) return;
+  const int t = row_token[r];
+  const float w = t >= 0 ? row_w[r] : 0.f;
+  for (int i = threadIdx.x; i < D; i += blockDim.x)
+    st(&dst[r * D + i], t >= 0 ? w * src[(int64_t)t * D + i] : 0.f);
+}
+
+// ------------------------------------------------------------- SwiGLU
+// silu_mul (src/mixtral.rs:941-951): h = g * sigmoid(g) * u.
+template <typename T>
+__global__ void k_silu_mul(const T* __restrict__ g, const T* __restrict__ u,
+                           const int* __restrict__ seg_off, int E, int64_t I, T* __restrict__ h) {
+  int64_t n = (int64_t)seg_off[E] * I;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float z = ld(&g[i]);
+    float s = 1.0f / (1.0f + expf(-z));
+    st(&h[i], z * s * ld(&u[i]));
+  }
+}
+
+// silu_mul_bwd (src/mixtral.rs:953-964): dg = dh*u*s*(1+z(1-s)), du = dh*silu(z).
+template <typename T>
+__global__ void k_silu_mul_bwd(const float* __restrict__ dh, const T* __restrict__ g,
+                               const T* __restrict__ u, const int* __restrict__ seg_off, int E,
+                               int64_t I, T* __restrict__ dg, T* __restrict__ du) {
+  int64_t n = (int64_t)seg_off[E] * I;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float z = ld(&g[i]);
+    float s = 1.0f / (1.0f + expf(-z));
+    float dsilu = s * (1.0f + z * (1.0f - s));
+    float d = dh[i];
+    st(&dg[i], d * ld(&u[i]) * dsilu);
+    st(&du[i], d * (z * s));
+  }
+}
+
+// ------------------------------------------------------ combine (K9 tail)
+// y[t] = mid[t] + sum_k w_k * out[row(t,k)], the slot sum taken in slot
+// order from zero as in src/mixtral.rs:330-359.
+__global__ void k_combine(const float* __restrict__ mid, const float* __restrict__ out,
+                          const int* __restrict__ slot_row, const float* __restrict__ top_w,
+                          int K, int D, float* __restrict__ y) {
+  const int64_t t = blockIdx.x;
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float m = 0.f;
+    for (int k = 0; k < K; ++k) {
+      int64_t r = slot_row[t * K + k];
+      m += top_w[t * K + k] * out[r * D + i];
+    }
+    y[t * D + i] = mid[t * D + i] + m;
+  }
+}
+
+// ------------------------------------------- router Jacobian / mix bwd (K10)
+// src/mixtral.rs:456-541 for one token: dvalue_k = <dy, out_k>,
+// dvalues_k = (dvalue_k - sum_j w_j dvalue_j) / s with s = sum top_p,
+// dz = p (dp - <p, dp>).
+__global__ void k_router_bwd(const float* __restrict__ dy, const float* __restrict__ out,
+                             const int* __restrict__ slot_row, const int* __restrict__ top_i,
+                             const float* __restrict__ top_p, const float* __restrict__ top_w,
+                             const float* __restrict__ probs, int E, int K, int D,
+                             float* __restrict__ dz) {
+  const int64_t t = blockIdx.x;
+  __shared__ float red[kMaxTopK][32];
+  __shared__ float dv[kMaxTopK];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int k = 0; k < K; ++k) {
+    const int64_t r = slot_row[t * K + k];
+    float acc = 0.f;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) acc += dy[t * D + i] * out[r * D + i];
+    acc = warp_sum(acc);
+    if (lane == 0) red[k][warp] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f, wdot = 0.f;
+    for (int k = 0; k < K; ++k) s += top_p[t * K + k];
+    for (int k = 0; k < K; ++k) {
+      float v = 0.f;
+      for (int q = 0; q < (int)(blockDim.x >> 5); ++q) v += red[k][q];
+      dv[k] = v;
+      wdot += v * top_w[t * K + k];
+    }
+    float dp[kMaxExperts];
+    for (int e = 0; e < E; ++e) dp[e] = 0.f;
+    for (int k = 0; k < K; ++k) dp[top_i[t * K + k]] = dv[k] / s - wdot / s;
+    float dot = 0.f;
+    for (int e = 0; e < E; ++e) dot += probs[t * E + e] * dp[e];
+    for (int e = 0; e < E; ++e) dz[t * E + e] = probs[t * E + e] * (dp[e] - dot);
+  }
+}
+
+// d_xn2[t] = sum_k dXp[row(t,k)] + sum_e dz[t,e] * Wr[i,e]  (src/mixtral.rs:
+// 516, 535-540: expert input cotangents in slot order, then the router's).
+template <typename T>
+__global__ void k_unpermute_router_dx(const float* __restrict__ dxp,
+                                      const int* __restrict__ slot_row,
+                                      const float* __restrict__ dz, const T* __restrict__ wr,
+                                      int E, int K, int D, float* __restrict__ dxn) {
+  const int64_t t = blockIdx.x;
+  __shared__ float dzs[kMaxExperts];
+  if (threadIdx.x < E) dzs[threadIdx.x] = dz[t * E + threadIdx.x];
+  __syncthreads();
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float a = 0.f;
+    for (int k = 0; k < K; ++k) a += dxp[(int64_t)slot_row[t * K + k] * D + i];
+    float rr = 0.f;
+    for (int e = 0; e < E; ++e) rr += dzs[e] * ld(&wr[(int64_t)i * E + e]);
+    dxn[t * D + i] = a + rr;
+  }
+}
+
+// Router weight adjoint partials: part[c, i, e] = sum_{t in chunk c}
+// xn2[t,i] * dz[t,e] with xn2 recomputed in fp32 from (mid, inv, w).
+template <typename T>
+__global__ void k_router_dw(const float* __restrict__ mid, const float* __restrict__ inv,
+                            const T* __restrict__ w, const float* __restrict__ dz, int64_t rows,
+                            int D, int E, int rows_per_chunk, float* __restrict__ part) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int c = blockIdx.y;
+  if (i >= D) return;
+  const int64_t t0 = (int64_t)c * rows_per_chunk;
+  const int64_t t1 = ::min((int64_t)(rows), (int64_t)(t0 + rows_per_chunk));
+  float acc[kMaxExperts];
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) acc[e] = 0.f;
+  const float wi = ld(&w[i]);
+  for (int64_t t = t0; t < t1; ++t) {
+    float xn = mid[t * D + i] * inv[t] * wi;
+#pragma unroll
+    for (int e = 0; e < kMaxExperts; ++e)
+      if (e < E) acc[e] += xn * dz[t * E + e];
+  }
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e)
+    if (e < E) part[((int64_t)c * D + i) * E + e] = acc[e];
+}
+
+// --------------------------------------------------------------- misc
+template <typename T>
+__global__ void k_convert(const float* __restrict__ s, T* __restrict__ d, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    st(&d[i], s[i]);
+}
+
+// Column sums of x[rows, cols]: part[c, j] = sum over row chunk c.
+__global__ void k_col_part(const float* __restrict__ x, int64_t rows, int64_t cols,
+                           int rows_per_chunk, float* __restrict__ part) {
+  int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int c = blockIdx.y;
+  if (j >= cols) return;
+  int64_t r0 = (int64_t)c * rows_per_chunk, r1 = ::min((int64_t)(rows), (int64_t)(r0 + rows_per_chunk));
+  float s = 0.f;
+  for (int64_t r = r0; r < r1; ++r) s += x[r * cols + j];
+  part[(int64_t)c * cols + j] = s;
+}
+
+__global__ void k_set_chunks(const float* __restrict__ part, int chunks, int64_t n,
+                             float* __restrict__ out) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float s = 0.f;
+  for (int c = 0; c < chunks; ++c) s += part[(int64_t)c * n + i];
+  out[i] = s;
+}
+
+__global__ void k_add(float* __restrict__ d, const float* __restrict__ s, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    d[i] += s[i];
+}
+
+__global__ void k_relu_mask_bwd(float* __restrict__ dy, const uint8_t* __restrict__ m, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    if (m[i] == 0) dy[i] = 0.f;
+}
+
+// Mean-squared error, one CTA: loss = sum (y-t)^2 / n, dy = 2 (y-t) / n.
+__global__ void k_mse(const float* __restrict__ y, const float* __restrict__ t, int64_t n,
+                      float* __restrict__ loss, float* __restrict__ dy) {
+  __shared__ float red[32];
+  float acc = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+    float d = y[i] - t[i];
+    acc += d * d;
+    dy[i] = 2.0f * d / (float)n;
+  }
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int q = 0; q < (int)(blockDim.x >> 5); ++q) s += red[q];
+    *loss = s / (float)n;
+  }
+}
+
+__global__ void k_sgd(float* __restrict__ p, const float* __restrict__ g, int64_t n, float lr) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    p[i] -= lr * g[i];
+}
+
+__global__ void k_fill_i32(int* __restrict__ p, int64_t n, int v) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
+// ----------------------------------------------------------- launchers
+static int grid_for(int64_t n, int block) {
+  int64_t g = ceil_div(n, block);
+  int64_t cap = (int64_t)sm_count() * 16;
+  return (int)(g < cap ? (g > 0 ? g : 1) : cap);
+}
+
+template <typename T>
+void rmsnorm_fwd(const float* x, const T* w, int64_t rows, int D, float eps, T* y, float* inv,
+                 float* x_copy, cudaStream_t s, int64_t& launches) {
+  k_rmsnorm_fwd<T><<<(unsigned)rows, 256, 0, s>>>(x, w, D, eps, y, inv, x_copy);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename T>
+void rmsnorm_router(const float* x, const T* w, const T* wr, const float* bias, int64_t rows,
+                    int D, int E, int K, float eps, T* y, float* inv, float* probs, int* top_i,
+                    float* top_p, float* top_w, cudaStream_t s, int64_t& launches) {
+  DOP_REQUIRE(E <= kMaxExperts && K <= kMaxTopK && K <= E, "experts/top_k out of range");
+  k_rmsnorm_router<T><<<(unsigned)rows, 256, 0, s>>>(x, w, wr, bias, D, E, K, eps, y, inv, probs,
+                                                     top_i, top_p, top_w);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename T>
+void rmsnorm_bwd(const float* dy, const float* x, const float* inv, const T* w,
+                 const float* res, int64_t rows, int D, float* dx, T* dx_act, float* dw_accum,
+                 float* part_buf, int64_t part_cap, cudaStream_t s, int64_t& launches) {
+  int threads = 256;
+  while (threads < 1024 && D > threads * 32) threads *= 2;
+  DOP_REQUIRE(D <= threads * 32, "dim too large for rmsnorm_bwd");
+  int64_t chunks = std::min<int64_t>(rows, (int64_t)sm_count() * 4);
+  int rows_per_chunk = (int)ceil_div(rows, chunks);
+  chunks = ceil_div(rows, rows_per_chunk);
+  DOP_REQUIRE(chunks * D <= part_cap, "partial buffer too small");
+  k_rmsnorm_bwd<T><<<(unsigned)chunks, threads, 0, s>>>(dy, x, inv, w, res, rows, D,
+                                                          rows_per_chunk, dx, dx_act, part_buf);
+  DOP_LAUNCHED(launches);
+  k_reduce_chunks<<<(unsigned)ceil_div(D, 256), 256, 0, s>>>(part_buf, (int)chunks, D, dw_accum);
+  DOP_LAUNCHED(launches);
+}
+
+void rope_table(int S, int hd, float theta, float* cs, float* sn, cudaStream_t s,
+                int64_t& launches) {
+  int half = hd / 2;
+  int64_t n = (int64_t)S * half;
+  k_rope_table<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(S, half, hd, theta, cs, sn);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename TI, typename TO>
+void rope(const TI* src, TO* dst, int64_t T, int S, int heads, int hd, const float* cs,
+          const float* sn, float sign, cudaStream_t s, int64_t& launches) {
+  int64_t n = T * heads * (hd / 2);
+  k_rope<TI, TO><<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(src, dst, T, S, heads, hd, cs, sn,
+                                                            sign);
+  DOP_LAUNCHED(launches);
+}
+
+void permute(const int* top_i, const float* top_w, int64_t T, int E, int K, int* chunk_counts,
+             int* seg_off, int* tile_expert, int max_tiles, int* slot_row, int* row_token,
+             float* row_w, int64_t rows_cap, cudaStream_t s, int64_t& launches) {
+  int64_t pairs = T * K;
+  int chunks = (int)ceil_div(pairs, kPermChunk);
+  k_fill_i32<<<grid_for(rows_cap, 256), 256, 0, s>>>(row_token, rows_cap, -1);
+  DOP_LAUNCHED(launches);
+  k_perm_count<<<chunks, 256, 0, s>>>(top_i, pairs, E, chunk_counts);
+  DOP_LAUNCHED(launches);
+  k_perm_scan<<<1, 256, 0, s>>>(chunk_counts, chunks, E, seg_off, tile_expert, max_tiles);
+  DOP_LAUNCHED(launches);
+  k_perm_scatter<<<chunks, kPermChunk, 0, s>>>(top_i, top_w, pairs, E, K, chunk_counts, seg_off,
+                                               slot_row, row_token, row_w);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename T>
+void gather_rows(const T* src, const int* row_token, const int* seg_off, int E, int D,
+                 int64_t rows_cap, T* dst, cudaStream_t s, int64_t& launches) {
+  k_gather_rows<T><<<(unsigned)rows_cap, 256, 0, s>>>(src, row_token, seg_off, E, D, dst);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename T>
+void gather_scale_rows(const float* src, const int* row_token, const float* row_w,
+                       const int* seg_off, int E, int D, int64_t rows_cap, T* dst, cudaStream_t s,
+                       int64_t& launches) {
+  k_gather_scale_rows<T><<<(unsigned)rows_cap, 256, 0, s>>>(src, row_token, row_w, seg_off, E, D,
+                                                            dst);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename T>
+void silu_mul(const T* g, const T* u, const int* seg_off, int E, int64_t I, int64_t rows_cap,
+              T* h, cudaStream_t s, int64_t& launches) {
+  k_silu_mul<T><<<grid_for(rows_cap * I, 256), 256, 0, s>>>(g, u, seg_off, E, I, h);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename T>
+void silu_mul_bwd(const float* dh, const T* g, const T* u, const int* seg_off, int E, int64_t I,
+                  int64_t rows_cap, T* dg, T* du, cudaStream_t s, int64_t& launches) {
+  k_silu_mul_bwd<T><<<grid_for(rows_cap * I, 256), 256, 0, s>>>(dh, g, u, seg_off, E, I, dg, du);
+  DOP_LAUNCHED(launches);
+}
+
+void combine(const float* mid, const float* out, const int* slot_row, const float* top_w,
+             int64_t T, int K, int D, float* y, cudaStream_t s, int64_t& launches) {
+  k_combine<<<(unsigned)T, 256, 0, s>>>(mid, out, slot_row, top_w, K, D, y);
+  DOP_LAUNCHED(launches);
+}
+
+void router_bwd(const float* dy, const float* out, const int* slot_row, const int* top_i,
+                const float* top_p, const float* top_w, const float* probs, int64_t Tn, int E,
+                int K, int D, float* dz, cudaStream_t s, int64_t& launches) {
+  k_router_bwd<<<(unsigned)Tn, 256, 0, s>>>(dy, out, slot_row, top_i, top_p, top_w, probs, E, K,
+                                            D, dz);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename T>
+void unpermute_router_dx(const float* dxp, const int* slot_row, const float* dz, const T* wr,
+                         int64_t Tn, int E, int K, int D, float* dxn, cudaStream_t s,
+                         int64_t& launches) {
+  k_unpermute_router_dx<T><<<(unsigned)Tn, 256, 0, s>>>(dxp, slot_row, dz, wr, E, K, D, dxn);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename T>
+void router_dw(const float* mid, const float* inv, const T* w, const float* dz, int64_t rows,
+               int D, int E, float* dwr_accum, float* part_buf, int64_t part_cap,
+               cudaStream_t s, int64_t& launches) {
+  int64_t chunks = std::min<int64_t>(rows, 64);
+  int rows_per_chunk = (int)ceil_div(rows, chunks);
+  chunks = ceil_div(rows, rows_per_chunk);
+  DOP_REQUIRE(chunks * D * E <= part_cap, "partial buffer too small");
+  dim3 grid((unsigned)ceil_div(D, 128), (unsigned)chunks);
+  k_router_dw<T><<<grid, 128, 0, s>>>(mid, inv, w, dz, rows, D, E, rows_per_chunk, part_buf);
+  DOP_LAUNCHED(launches);
+  k_reduce_chunks<<<(unsigned)ceil_div((int64_t)D * E, 256), 256, 0, s>>>(part_buf, (int)chunks,
+                                                                           (int64_t)D * E, dwr_accum);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename T>
+void convert(const float* src, T* dst, int64_t n, cudaStream_t s, int64_t& launches) {
+  k_convert<T><<<grid_for(n, 256), 256, 0, s>>>(src, dst, n);
+  DOP_LAUNCHED(launches);
+}
+
+void col_sum(const float* x, int64_t rows, int64_t cols, float* out, float* part_buf,
+             int64_t part_cap, bool accumulate, cudaStream_t s, int64_t& launches) {
+  int64_t chunks = std::max<int64_t>(1, std::min<int64_t>(rows, 64));
+  int rows_per_chunk = (int)ceil_div(rows, chunks);
+  chunks = std::max<int64_t>(1, ceil_div(rows, rows_per_chunk));
+  DOP_REQUIRE(chunks * cols <= part_cap, "partial buffer too small");
+  dim3 grid((unsigned)ceil_div(cols, 128), (unsigned)chunks);
+  k_col_part<<<grid, 128, 0, s>>>(x, rows, cols, rows_per_chunk, part_buf);
+  DOP_LAUNCHED(launches);
+  if (accumulate)
+    k_reduce_chunks<<<(unsigned)ceil_div(cols, 256), 256, 0, s>>>(part_buf, (int)chunks, cols, out);
+  else
+    k_set_chunks<<<(unsigned)ceil_div(cols, 256), 256, 0, s>>>(part_buf, (int)chunks, cols, out);
+  DOP_LAUNCHED(launches);
+}
+
+void add_inplace(float* dst, const float* src, int64_t n, cudaStream_t s, int64_t& launches) {
+  k_add<<<grid_for(n, 256), 256, 0, s>>>(dst, src, n);
+  DOP_LAUNCHED(launches);
+}
+
+void relu_mask_bwd(float* dy, const uint8_t* mask, int64_t n, cudaStream_t s, int64_t& launches) {
+  k_relu_mask_bwd<<<grid_for(n, 256), 256, 0, s>>>(dy, mask, n);
+  DOP_LAUNCHED(launches);
+}
+
+void mse(const float* y, const float* t, int64_t n, float* loss, float* dy, cudaStream_t s,
+         int64_t& launches) {
+  k_mse<<<1, 1024, 0, s>>>(y, t, n, loss, dy);
+  DOP_LAUNCHED(launches);
+}
+
+void sgd(float* p, const float* g, int64_t n, float lr, cudaStream_t s, int64_t& launches) {
+  k_sgd<<<grid_for(n, 256), 256, 0, s>>>(p, g, n, lr);
+  DOP_LAUNCHED(launches);
+}
+
+// explicit instantiations for the two activation types
+#define DOP_INST(T)                                                                             \
+  template void rmsnorm_fwd<T>(const float*, const T*, int64_t, int, float, T*, float*, float*, \
+                               cudaStream_t, int64_t&);                                         \
+  template void rmsnorm_router<T>(const float*, const T*, const T*, const float*, int64_t, int, \
+                                  int, int, float, T*, float*, float*, int*, float*, float*,    \
+                                  cudaStream_t, int64_t&);                                      \
+  template void rmsnorm_bwd<T>(const float*, const float*, const float*, const T*,             \
+                               const float*, int64_t, int, float*, T*, float*, float*, int64_t, \
+                               cudaStream_t, int64_t&);                                         \
+  template void gather_scale_rows<T>(const float*, const int*, const float*, const int*, int,  \
+                                     int, int64_t, T*, cudaStream_t, int64_t&);                 \
+  template void convert<T>(const float*, T*, int64_t, cudaStream_t, int64_t&);                  \
+  template void rope<float, T>(const float*, T*, int64_t, int, int, int, const float*,         \
+                               const float*, float, cudaStream_t, int64_t&);                    \
+  template void gather_rows<T>(const T*, const int*, const int*, int, int, int64_t, T*,        \
+                               cudaStream_t, int64_t&);                                         \
+  template void silu_mul<T>(const T*, const T*, const int*, int, int64_t, int64_t, T*,         \
+                            cudaStream_t, int64_t&);                                            \
+  template void silu_mul_bwd<T>(const float*, const T*, const T*, const int*, int, int64_t,    \
+                                int64_t, T*, T*, cudaStream_t, int64_t&);                       \
+  template void unpermute_router_dx<T>(const float*, const int*, const float*, const T*,       \
+                                       int64_t, int, int, int, float*, cudaStream_t, int64_t&); \
+  template void router_dw<T>(const float*, const float*, const T*, const float*, int64_t, int,  \
+                             int, float*, float*, int64_t, cudaStream_t, int64_t&);
+
+DOP_INST(float)
+DOP_INST(bf16)
+
+}  // namespace dop

@@ -1,0 +1,203 @@
+/*
+ * dop.h — C ABI of the B200 tensor-lens library (libdop.so).
+ *
+ * The reference crate (dependent-optics, Rust) exposes its tensor lenses as
+ * Rust functions: `mixtral::forward_backward` and the private block lens
+ * `forward_layer`/`backward_layer` (src/mixtral.rs), and the small programs of
+ * src/kernel.rs.  This header is the drop-in boundary a foreign caller (a Rust
+ * `extern "C"` block, Python ctypes, C++) binds.  Conventions:
+ *
+ *   - every entry point returns an int status: 0 ok, < 0 a DOP_E_* code;
+ *     dop_last_error() returns the message of the calling thread's last error;
+ *   - device buffers are caller-owned and passed as plain pointers; residuals
+ *     ("tapes") are owned by the lens handle that wrote them;
+ *   - streams are passed as `void*` (a cudaStream_t; NULL = legacy stream);
+ *   - parameter slices use the crate's flat layout: every matrix is row-major
+ *     with the contraction index first, W[k * dout + n] (src/mixtral.rs:101-102);
+ *   - parameter adjoints are ACCUMULATED (+=), as `add_assign` into `grad`
+ *     in src/mixtral.rs:473-593; program adjoints (src/kernel.rs:342,351) are
+ *     assigned.
+ *
+ * Precision: DOP_F32 computes every contraction in fp32 (the crate's own
+ * arithmetic); DOP_BF16 keeps weights and GEMM operands in bf16 with fp32
+ * accumulation, the residual stream and all adjoints in fp32.
+ */
+#ifndef DOP_H
+#define DOP_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ errors */
+#define DOP_OK 0
+#define DOP_E_INVALID (-1)      /* bad argument (shape, null pointer, config) */
+#define DOP_E_CUDA (-2)         /* a CUDA runtime/driver call failed */
+#define DOP_E_NOMEM (-3)        /* device allocation failed */
+#define DOP_E_UNSUPPORTED (-4)  /* shape outside what the kernels implement */
+#define DOP_E_STATE (-5)        /* call order violated (backward before forward) */
+#define DOP_E_NCCL (-6)         /* a collective failed */
+#define DOP_E_TIMEOUT (-7)      /* a bounded device wait ran out */
+/* cluster.rs StageError variants (src/cluster.rs:265-292) */
+#define DOP_E_NO_DEVICE (-20)
+#define DOP_E_PARAMS_EXCEED_CLUSTER (-21)
+#define DOP_E_TAPE_EXCEEDS_CLUSTER (-22)
+#define DOP_E_TILE_EXCEEDS_DEVICES (-23)
+#define DOP_E_CODE_EXCEEDS_DEVICES (-24)
+#define DOP_E_ROUTE_UNAVAILABLE (-25)
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* dop_last_error(void);
+/* Library version string. */
+const char* dop_version(void);
+
+/* --------------------------------------------------------------- precision */
+#define DOP_F32 0
+#define DOP_BF16 1
+
+/* ------------------------------------------------------------ Mixtral config
+ * Field-for-field the crate's `MixtralConfig` (src/mixtral.rs:34-48).
+ * `sliding_window` counts the keys a query may attend to, itself included. */
+typedef struct dop_mixtral_cfg {
+  int64_t vocab;
+  int64_t dim;
+  int64_t layers;
+  int64_t heads;
+  int64_t kv_heads;
+  int64_t head_dim;
+  int64_t intermediate;
+  int64_t experts;
+  int64_t top_k;
+  float rms_eps;
+  float rope_theta;
+  int64_t sliding_window;
+} dop_mixtral_cfg;
+
+/* Offsets of one layer inside its own parameter slice (the slice starts at
+ * `attn_norm`).  Mirrors `LayerLayout` (src/mixtral.rs:115-126); gate/up/down
+ * of expert e are at gate0 + e * expert_stride etc. */
+typedef struct dop_layer_layout {
+  int64_t attn_norm, q, k, v, o, ffn_norm, router;
+  int64_t gate0, up0, down0, expert_stride;
+  int64_t total; /* floats in one layer slice */
+} dop_layer_layout;
+
+/* `layout` (src/mixtral.rs:128-181) for one layer, and the whole-model count
+ * `parameter_count` (src/mixtral.rs:183-185). */
+int dop_layer_layout_of(const dop_mixtral_cfg* cfg, dop_layer_layout* out);
+int64_t dop_parameter_count(const dop_mixtral_cfg* cfg);
+
+/* ---------------------------------------------------------- the block lens
+ * One Mixtral block as a lens.  get: x[T,D] -> y[T,D] (+ residual kept in the
+ * handle); put: (residual, dy) -> dx, dparams += grad.  Replaces the crate's
+ * `forward_layer` (src/mixtral.rs:291-380) and `backward_layer`
+ * (src/mixtral.rs:434-598).  T = batch * seq, t = b * seq + s.
+ *
+ * `params` is the layer's parameter slice (dop_layer_layout order) on the
+ * device: fp32 for DOP_F32, bf16 (uint16 bit patterns) for DOP_BF16.
+ * `x`, `y`, `dy`, `dx` are fp32 device arrays [T, D]; `dparams` is an fp32
+ * device array of dop_layer_layout.total floats that is accumulated into.
+ * `router_bias` (may be NULL) is an fp32 device array [E] added to the router
+ * logits before the softmax (the skewed-routing workload; the crate has none). */
+typedef struct dop_block dop_block;
+
+int dop_block_create(const dop_mixtral_cfg* cfg, int64_t batch, int64_t seq,
+                     int precision, dop_block** out);
+int dop_block_destroy(dop_block* blk);
+int dop_block_set_router_bias(dop_block* blk, const float* router_bias);
+int dop_block_forward(dop_block* blk, const void* params, const float* x,
+                      float* y, void* stream);
+int dop_block_backward(dop_block* blk, const void* params, const float* dy,
+                       float* dx, float* dparams, void* stream);
+/* Bytes of device memory the handle holds (residual + workspace). */
+int64_t dop_block_workspace_bytes(const dop_block* blk);
+
+/* Routing decisions of the last forward, copied to device buffers:
+ * top_i [T*k] int32, top_w [T*k] fp32 (renormalised gate), top_p [T*k] fp32,
+ * router_probs [T*E] fp32 (any may be NULL). */
+int dop_block_routing(const dop_block* blk, int32_t* top_i, float* top_w,
+                      float* top_p, float* router_probs, void* stream);
+/* The deterministic permutation of the last forward: for each (token, slot)
+ * pair in token-major order, its row in the expert-sorted buffer
+ * (slot_row [T*k] int32), the padded row offset of each expert's segment
+ * (seg_off [E+1] int32) and the token of each permuted row (row_token
+ * [rows] int32, -1 for padding; rows = dop_block_permuted_rows()). */
+int dop_block_permutation(const dop_block* blk, int32_t* slot_row,
+                          int32_t* seg_off, int32_t* row_token, void* stream);
+int64_t dop_block_permuted_rows(const dop_block* blk);
+/* Number of kernels the library launched on this handle since creation. */
+int64_t dop_block_launches(const dop_block* blk);
+/* Per-phase device timing (CUDA events on the caller's stream around each
+ * phase of forward/backward: "expert_gate_up", "attn_fwd", ...).  Off by
+ * default; dop_block_phase() synchronises the phase's events. */
+int dop_block_set_timing(dop_block* blk, int on);
+int dop_block_phase_count(const dop_block* blk);
+int dop_block_phase(const dop_block* blk, int i, const char** name, float* ms);
+
+/* ------------------------------------------------------- lens composition
+ * `compose(g, f)` means g after f (src/dlens.rs:74-113; README "compose(g, f)
+ * always means g ∘ f").  Forward runs f then g; backward runs g's put then
+ * f's; the composite residual is the pair of residuals.  A lens is a block or
+ * a composite; composites own no memory beyond a scratch activation buffer. */
+typedef struct dop_lens dop_lens;
+int dop_lens_from_block(dop_block* blk, const void* params, float* dparams,
+                        dop_lens** out);
+int dop_compose(dop_lens* g, dop_lens* f, dop_lens** out);
+int dop_lens_forward(dop_lens* l, const float* x, float* y, void* stream);
+int dop_lens_backward(dop_lens* l, const float* dy, float* dx, void* stream);
+int dop_lens_destroy(dop_lens* l);
+
+/* ---------------------------------------------------- kernel.rs programs
+ * Mirrors `Stage` / `Program` (src/kernel.rs:27-61).  Offsets index the flat
+ * f32 tape, the u8 mask tape and the flat parameter vector exactly as the
+ * crate's builders lay them out (src/kernel.rs:78-170). */
+#define DOP_STAGE_GEMM 0
+#define DOP_STAGE_ATTENTION 1
+#define DOP_STAGE_ADD 2
+typedef struct dop_stage {
+  int32_t kind;
+  int32_t relu;
+  int64_t batch, din, dout;       /* Gemm */
+  int64_t save_at, mask_at, param_at;
+  int64_t tokens, dim, x_at, probs_at; /* Attention (uses batch too) */
+  int64_t from, len;              /* Add */
+} dop_stage;
+
+typedef struct dop_program dop_program;
+int dop_program_create(const dop_stage* stages, int64_t n_stages,
+                       int64_t input_len, int64_t output_len,
+                       int64_t param_len, int64_t tape_f32, int64_t tape_u8,
+                       dop_program** out);
+int dop_program_destroy(dop_program* prog);
+/* get: y = program(x); the residual stays in the handle. */
+int dop_program_forward(dop_program* prog, const float* x, const float* params,
+                        float* y, void* stream);
+/* put: dy (NULL = the crate's sum loss, dy = 1, src/kernel.rs:237) ->
+ * dx, dparams (assigned). */
+int dop_program_backward(dop_program* prog, const float* params,
+                         const float* dy, float* dx, float* dparams,
+                         void* stream);
+/* `kernel::forward_backward` (src/kernel.rs:181-240) in one call. */
+int dop_program_forward_backward(dop_program* prog, const float* x,
+                                 const float* params, const float* dy,
+                                 float* y, float* dx, float* dparams,
+                                 void* stream);
+/* Mean-squared-error head: loss = mean((y - t)^2), dy = 2 (y - t) / n.
+ * `loss` is a device float. */
+int dop_mse_loss_grad(const float* y, const float* target, int64_t n,
+                      float* loss, float* dy, void* stream);
+
+/* ----------------------------------------------------------- utilities */
+/* fp32 -> bf16 (round to nearest even), device arrays. */
+int dop_f32_to_bf16(const float* src, uint16_t* dst, int64_t n, void* stream);
+/* p <- p - lr * g, returns nothing; `sgd_step` (src/mixtral.rs:994-1001). */
+int dop_sgd_step(float* params, const float* grad, int64_t n, float lr,
+                 void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DOP_H */
