@@ -55,6 +55,13 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
   DOP_REQUIRE(precision == DOP_F32 || precision == DOP_BF16, "precision must be DOP_F32 or DOP_BF16");
   DOP_REQUIRE(c.dim <= 1024 * 32, "dim too large");
   DOP_REQUIRE(T * c.top_k < (int64_t)1 << 30, "too many tokens");
+  if (precision == DOP_BF16) {
+    // tensor-core operands: 16-byte row strides (TMA) and 32-column SwiGLU tiles
+    DOP_REQUIRE(c.dim % 8 == 0 && (c.heads * c.head_dim) % 8 == 0 &&
+                    (c.kv_heads * c.head_dim) % 8 == 0,
+                "the bf16 lens needs dim, heads*head_dim and kv_heads*head_dim multiples of 8");
+    DOP_REQUIRE(c.intermediate % 32 == 0, "the bf16 lens needs intermediate % 32 == 0");
+  }
   off = layer_offsets(c);
   const int64_t D = c.dim, E = c.experts, K = c.top_k, I = c.intermediate;
   const int64_t qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim;
@@ -98,7 +105,7 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
     cv.take(rope_cos, 4 * S * (c.head_dim / 2), base_);
     cv.take(rope_sin, 4 * S * (c.head_dim / 2), base_);
     cv.take(dz, 4 * T * E, base_);
-    cv.take(dh, 4 * rows_cap * I, base_);
+    cv.take(dh, prec == DOP_F32 ? 4 * rows_cap * I : 0, base_);
     cv.take(dxp, 4 * rows_cap * D, base_);
     cv.take(dxn2, 4 * T * D, base_);
     cv.take(dmid, 4 * T * D, base_);
@@ -157,9 +164,22 @@ void Block::ph_end(cudaStream_t s) {
   ++n_phases;
 }
 
+// Contraction dispatch: the fp32 lens runs the CUDA-core GEMM (extra K
+// parts as accumulating passes), the bf16 lens the tcgen05 GEMM (extra K
+// parts summed in one TMEM accumulator).
 template <typename Act>
-void Block::gemm(const Gemm& g, cudaStream_t s) {
+void Block::gemm(const Gemm& g, cudaStream_t s, const GemmPart* extra, int n_extra) {
+  if (std::is_same<Act, bf16>::value) {
+    gemm_tc(g, extra, n_extra, TcEpilogue{}, s, launches);
+    return;
+  }
   gemm_simt<Act>(g, s, launches);
+  for (int i = 0; i < n_extra; ++i) {
+    Gemm gi = g;
+    gi.A = extra[i].A; gi.lda = extra[i].lda; gi.B = extra[i].B; gi.ldb = extra[i].ldb;
+    gi.K = extra[i].K; gi.epi = Epi::Accum;
+    gemm_simt<Act>(gi, s, launches);
+  }
 }
 
 void Block::forward(const void* params, const float* x, float* y, cudaStream_t s) {
@@ -234,13 +254,21 @@ void Block::fwd(const Act* P, const float* x, float* y, cudaStream_t s) {
     gg.B = P + off.gate0; gg.ldb = I; gg.C = g_; gg.ldc = I; gg.c_f32 = std::is_same<Act, float>::value;
     gg.group = 1; gg.seg_off = seg_off; gg.tile_expert = tile_expert; gg.G = (int)E;
     gg.b_gs = off.expert_stride;
-    gemm<Act>(gg, s);
-    Gemm gu = gg; gu.B = P + off.up0; gu.C = u_;
-    gemm<Act>(gu, s);
+    if (std::is_same<Act, bf16>::value) {
+      // one tensor-core pass: B = [gate | up], epilogue writes g, u and
+      // h = silu(g) * u (src/mixtral.rs:318-329)
+      TcEpilogue te; te.kind = kTcSwiGLU; te.up_B = P + off.up0;
+      te.g_out = (bf16*)g_; te.u_out = (bf16*)u_; te.h_out = (bf16*)h_; te.ldg = I;
+      gemm_tc(gg, nullptr, 0, te, s, launches);
+    } else {
+      gemm<Act>(gg, s);
+      Gemm gu = gg; gu.B = P + off.up0; gu.C = u_;
+      gemm<Act>(gu, s);
+      ph_end(s);
+      ph_begin("swiglu", s);
+      silu_mul<Act>(g_, u_, seg_off, (int)E, I, rows_cap, h_, s, launches);
+    }
   }
-  ph_end(s);
-  ph_begin("swiglu", s);
-  silu_mul<Act>(g_, u_, seg_off, (int)E, I, rows_cap, h_, s, launches);
   ph_end(s);
   ph_begin("expert_down", s);
   {
@@ -264,74 +292,80 @@ void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_
   const bool f32 = std::is_same<Act, float>::value;
   Act* xn_ = (Act*)xn; Act* q_ = (Act*)q; Act* k_ = (Act*)k; Act* v_ = (Act*)v; Act* mix_ = (Act*)mix;
   Act* xp_ = (Act*)xp; Act* g_ = (Act*)g; Act* u_ = (Act*)u; Act* h_ = (Act*)h;
-  Act* dO_ = (Act*)dO; Act* dg_ = (Act*)dg; Act* du_ = (Act*)du; Act* dmid_ = (Act*)dmid_a; Act* dmix_ = (Act*)dmix;
-  Act* dq_ = (Act*)dq_a; Act* dk_ = (Act*)dk_a; Act* dv_ = (Act*)dv_a;
+  Act* dO_ = (Act*)dO; Act* dg_ = (Act*)dg; Act* du_ = (Act*)du; Act* dmid_ = (Act*)dmid_a;
+  Act* dmix_ = (Act*)dmix; Act* dq_ = (Act*)dq_a; Act* dk_ = (Act*)dk_a; Act* dv_ = (Act*)dv_a;
 
-  // router Jacobian and the down projection's output cotangent
+  // router Jacobian (src/mixtral.rs:456-541) and the down projection's output
+  // cotangent d_out = w * dy, in expert-sorted rows
   ph_begin("router_bwd", s);
   router_bwd(dy, out, slot_row, top_i, top_p, top_w, probs, T, (int)E, (int)K, (int)D, dz, s,
              launches);
   gather_scale_rows<Act>(dy, row_token, row_w, seg_off, (int)E, (int)D, rows_cap, dO_, s, launches);
-  // dH = dO Wd^T (Wd_e is [I, D]); SwiGLU adjoint
   ph_end(s);
+  // dH = dO Wd^T (Wd_e is [I, D]) and the SwiGLU adjoint (src/mixtral.rs:478-486)
   ph_begin("expert_dh", s);
   {
     Gemm g1; g1.M = rows_cap; g1.N = I; g1.K = D; g1.A = dO_; g1.lda = D;
     g1.B = P + off.down0; g1.ldb = D; g1.b_t = true; g1.C = dh; g1.ldc = I;
     g1.group = 1; g1.seg_off = seg_off; g1.tile_expert = tile_expert; g1.G = (int)E;
     g1.b_gs = off.expert_stride;
-    gemm<Act>(g1, s);
+    if (!f32) {
+      TcEpilogue te; te.kind = kTcSwiGLUBwd; te.g_in = (const bf16*)g_; te.u_in = (const bf16*)u_;
+      te.dg_out = (bf16*)dg_; te.du_out = (bf16*)du_; te.ldg = I;
+      gemm_tc(g1, nullptr, 0, te, s, launches);
+    } else {
+      gemm<Act>(g1, s);
+      ph_end(s);
+      ph_begin("swiglu_bwd", s);
+      silu_mul_bwd<Act>(dh, g_, u_, seg_off, (int)E, I, rows_cap, dg_, du_, s, launches);
+    }
   }
   ph_end(s);
-  ph_begin("swiglu_bwd", s);
-  silu_mul_bwd<Act>(dh, g_, u_, seg_off, (int)E, I, rows_cap, dg_, du_, s, launches);
-  // dWd_e += H^T dO over expert e's rows
-  ph_end(s);
+  // dWd_e += H^T dO over expert e's rows (src/mixtral.rs:478-480)
   ph_begin("expert_dw_down", s);
   {
-    Gemm g2; g2.M = I; g2.N = D; g2.A = h_; g2.lda = I; g2.a_t = true; g2.B = dO_; g2.ldb = D;
-    g2.C = dP + off.down0; g2.ldc = D; g2.epi = Epi::Accum;
+    Gemm g2; g2.M = I; g2.N = D; g2.K = rows_cap; g2.A = h_; g2.lda = I; g2.a_t = true;
+    g2.B = dO_; g2.ldb = D; g2.C = dP + off.down0; g2.ldc = D; g2.epi = Epi::Accum;
     g2.group = 2; g2.seg_off = seg_off; g2.G = (int)E; g2.c_gs = off.expert_stride;
     gemm<Act>(g2, s);
   }
-  // dXp = dG Wg^T + dU Wu^T (Wg_e, Wu_e are [D, I])
   ph_end(s);
+  // dXp = dG Wg^T + dU Wu^T (Wg_e, Wu_e are [D, I]; src/mixtral.rs:488-516)
   ph_begin("expert_dx", s);
   {
     Gemm g3; g3.M = rows_cap; g3.N = D; g3.K = I; g3.A = dg_; g3.lda = I;
     g3.B = P + off.gate0; g3.ldb = I; g3.b_t = true; g3.C = dxp; g3.ldc = D;
     g3.group = 1; g3.seg_off = seg_off; g3.tile_expert = tile_expert; g3.G = (int)E;
     g3.b_gs = off.expert_stride;
-    gemm<Act>(g3, s);
-    Gemm g4 = g3; g4.A = du_; g4.B = P + off.up0; g4.epi = Epi::Accum;
-    gemm<Act>(g4, s);
+    GemmPart up{du_, I, P + off.up0, I, I};
+    gemm<Act>(g3, s, &up, 1);
   }
-  // dWg_e += Xp^T dG, dWu_e += Xp^T dU
   ph_end(s);
+  // dWg_e += Xp^T dG, dWu_e += Xp^T dU
   ph_begin("expert_dw_gate_up", s);
   {
-    Gemm g5; g5.M = D; g5.N = I; g5.A = xp_; g5.lda = D; g5.a_t = true; g5.B = dg_; g5.ldb = I;
-    g5.C = dP + off.gate0; g5.ldc = I; g5.epi = Epi::Accum;
+    Gemm g5; g5.M = D; g5.N = I; g5.K = rows_cap; g5.A = xp_; g5.lda = D; g5.a_t = true;
+    g5.B = dg_; g5.ldb = I; g5.C = dP + off.gate0; g5.ldc = I; g5.epi = Epi::Accum;
     g5.group = 2; g5.seg_off = seg_off; g5.G = (int)E; g5.c_gs = off.expert_stride;
     gemm<Act>(g5, s);
     Gemm g6 = g5; g6.B = du_; g6.C = dP + off.up0;
     gemm<Act>(g6, s);
   }
-  // d_xn2 = sum_k dXp[row(t,k)] + dz Wr^T; router weight adjoint
   ph_end(s);
+  // d_xn2 = sum_k dXp[row(t,k)] + dz Wr^T; router weight adjoint
   ph_begin("unpermute_router", s);
   unpermute_router_dx<Act>(dxp, slot_row, dz, P + off.router, T, (int)E, (int)K, (int)D, dxn2, s,
-                         launches);
+                           launches);
   router_dw<Act>(mid, inv2, P + off.ffn_norm, dz, T, (int)D, (int)E, dP + off.router, part,
-               part_cap, s, launches);
-  // d_mid = rmsnorm_bwd(d_xn2) + dy
+                 part_cap, s, launches);
   ph_end(s);
+  // d_mid = rmsnorm_bwd(d_xn2) + dy (src/mixtral.rs:543-557)
   ph_begin("ffn_norm_bwd", s);
   rmsnorm_bwd<Act>(dxn2, mid, inv2, P + off.ffn_norm, dy, T, (int)D, dmid, f32 ? nullptr : dmid_,
-                 dP + off.ffn_norm, part, part_cap, s, launches);
-  const Act* dmid_op = f32 ? (const Act*)dmid : dmid_;
-  // d_mix = d_mid Wo^T (Wo is [qd, D]); dWo += mix^T d_mid
+                   dP + off.ffn_norm, part, part_cap, s, launches);
   ph_end(s);
+  const Act* dmid_op = f32 ? (const Act*)dmid : dmid_;
+  // d_mix = d_mid Wo^T (Wo is [qd, D]); dWo += mix^T d_mid (src/mixtral.rs:560-561)
   ph_begin("o_grad", s);
   {
     Gemm g7; g7.M = T; g7.N = qd; g7.K = D; g7.A = dmid_op; g7.lda = D;
@@ -354,21 +388,17 @@ void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_
   if (f32) dv_op = (const Act*)dv;
   else { convert<Act>(dv, dv_, T * kvd, s, launches); dv_op = dv_; }
   ph_end(s);
+  // d_xn = dq Wq^T + dk Wk^T + dv Wv^T (src/mixtral.rs:571-580)
   ph_begin("qkv_dgrad", s);
-  // d_xn = dq Wq^T + dk Wk^T + dv Wv^T
   {
     Gemm a1; a1.M = T; a1.N = D; a1.K = qd; a1.A = dq_; a1.lda = qd; a1.B = P + off.q;
     a1.ldb = qd; a1.b_t = true; a1.C = dxn; a1.ldc = D;
-    gemm<Act>(a1, s);
-    Gemm a2 = a1; a2.K = kvd; a2.A = dk_; a2.lda = kvd; a2.B = P + off.k; a2.ldb = kvd;
-    a2.epi = Epi::Accum;
-    gemm<Act>(a2, s);
-    Gemm a3 = a2; a3.A = dv_op; a3.B = P + off.v;
-    gemm<Act>(a3, s);
+    GemmPart kv[2] = {{dk_, kvd, P + off.k, kvd, kvd}, {dv_op, kvd, P + off.v, kvd, kvd}};
+    gemm<Act>(a1, s, kv, 2);
   }
   ph_end(s);
-  ph_begin("qkv_wgrad", s);
   // dWq += xn^T dq, dWk += xn^T dk, dWv += xn^T dv
+  ph_begin("qkv_wgrad", s);
   {
     Gemm w1; w1.M = D; w1.N = qd; w1.K = T; w1.A = xn_; w1.lda = D; w1.a_t = true; w1.B = dq_;
     w1.ldb = qd; w1.C = dP + off.q; w1.ldc = qd; w1.epi = Epi::Accum;
@@ -379,10 +409,10 @@ void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_
     gemm<Act>(w3, s);
   }
   ph_end(s);
-  // dx = rmsnorm_bwd(d_xn) + d_mid
+  // dx = rmsnorm_bwd(d_xn) + d_mid (src/mixtral.rs:581-597)
   ph_begin("attn_norm_bwd", s);
   rmsnorm_bwd<Act>(dxn, x_in, inv1, P + off.attn_norm, dmid, T, (int)D, dx, (Act*)nullptr,
-                 dP + off.attn_norm, part, part_cap, s, launches);
+                   dP + off.attn_norm, part, part_cap, s, launches);
   ph_end(s);
 }
 

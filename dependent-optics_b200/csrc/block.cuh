@@ -59,7 +59,8 @@ struct Block {
  private:
   template <typename Act> void fwd(const Act* P, const float* x, float* y, cudaStream_t s);
   template <typename Act> void bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_t s);
-  template <typename Act> void gemm(const Gemm& g, cudaStream_t s);
+  template <typename Act>
+  void gemm(const Gemm& g, cudaStream_t s, const GemmPart* extra = nullptr, int n_extra = 0);
 };
 
 }  // namespace dop

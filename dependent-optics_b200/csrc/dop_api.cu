@@ -517,6 +517,25 @@ int dop_mse_loss_grad(const float* y, const float* t, int64_t n, float* loss, fl
   });
 }
 
+int dop_gemm_bf16(int64_t M, int64_t N, int64_t K, const uint16_t* A, int64_t lda, int a_t,
+                  const uint16_t* B, int64_t ldb, int b_t, void* C, int64_t ldc, int c_f32,
+                  int accumulate, void* s) {
+  return guarded([&] {
+    DOP_REQUIRE(A && B && C && M > 0 && N > 0 && K > 0, "bad GEMM arguments");
+    DOP_REQUIRE(!accumulate || c_f32, "accumulation needs an fp32 C");
+    dop::Gemm g;
+    g.M = M; g.N = N; g.K = K;
+    g.A = A; g.lda = lda; g.a_t = a_t != 0;
+    g.B = B; g.ldb = ldb; g.b_t = b_t != 0;
+    g.C = C; g.ldc = ldc; g.c_f32 = c_f32 != 0;
+    g.epi = accumulate ? dop::Epi::Accum : dop::Epi::Store;
+    int64_t l = 0;
+    dop::gemm_tc(g, nullptr, 0, dop::TcEpilogue{}, as_stream(s), l);
+  });
+}
+
+int dop_device_status(void) { return dop::tc_error_status(); }
+
 int dop_f32_to_bf16(const float* src, uint16_t* dst, int64_t n, void* s) {
   return guarded([&] {
     DOP_REQUIRE(src && dst && n >= 0, "bad conversion arguments");

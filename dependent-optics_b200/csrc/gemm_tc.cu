@@ -1,0 +1,659 @@
+// gemm_tc.cu — bf16 x bf16 -> fp32 GEMM on the 5th-generation tensor cores.
+//
+// One persistent, warp-specialised kernel serves every contraction of the
+// bf16 block lens (dense Q/K/V/O projections and their gradients, the expert
+// SwiGLU projections grouped over expert-sorted row segments, and their
+// weight / input gradients):
+//
+//   warp 0        TMA producer: 128B-swizzled tiles of A and B into a
+//                 STAGES-deep shared-memory ring (cp.async.bulk.tensor)
+//   warp 1        allocates 512 TMEM columns; one thread issues
+//                 tcgen05.mma (M=128, N=BN, K=16) and tcgen05.commit
+//   warps 2..5    epilogue: tcgen05.ld of the fp32 accumulator (each warp
+//                 owns the 32 TMEM lanes of its quadrant), fused epilogue
+//                 math, global stores
+//
+// The accumulator is double-buffered in TMEM (2 x BN columns), so the
+// epilogue of tile i overlaps the main loop of tile i+1.  Either operand may be
+// K-major or M/N-major (the instruction descriptor's transpose bits), which
+// covers Y = X W, dX = dY W^T and dW = X^T dY on the crate's [din, dout]
+// weights without a transpose.  Every mbarrier wait is bounded; a wait that
+// runs out records an error code, stops the tile loop and drains what is in
+// flight before TMEM is freed.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "kernels.cuh"
+
+namespace dop {
+
+__device__ int g_tc_error;  // first bounded-wait failure seen by any CTA (0 = none)
+
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int THREADS = 192;
+constexpr uint64_t kWaitNs = 4000000000ull;  // 4 s of device time per wait
+
+enum EpiKind : int {
+  kStoreF32 = 0,
+  kStoreBF16 = 1,
+  kAccumF32 = 2,
+  kAddResF32 = 3,
+  kSwiGLU = 4,     // dual-B forward: cols [0,BN/2) = gate, [BN/2,BN) = up -> g, u, h
+  kSwiGLUBwd = 5,  // acc = dH; with g, u in global -> dG, dU
+};
+
+struct Params {
+  int M, N;         // output extent (rows, cols); grouped-K: per expert
+  int mode;         // 0 plain, 1 grouped rows (expert segments), 2 grouped contraction
+  int nparts;       // K segments (A_i, B_i) summed into one accumulator
+  int kb[3];        // k-blocks of each part (plain / grouped rows)
+  const int* seg_off;
+  const int* tile_expert;
+  int G;
+  int m_tiles, n_tiles;  // n_tiles counts BN-wide (dual: BN/2-wide output) tiles
+  int epi;
+  void* C;
+  int64_t ldc, c_gs;
+  const float* R;
+  int64_t ldr;
+  bf16 *g_out, *u_out, *h_out;   // SwiGLU forward outputs [rows, ldg]
+  const bf16 *g_in, *u_in;       // SwiGLU backward inputs
+  bf16 *dg_out, *du_out;
+  int64_t ldg;
+};
+
+// ------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t gtime_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait on phase `parity`: false when it ran out (kWaitNs of device
+// time; the error code is recorded and the CTA's abort flag raised) or when
+// another role of the CTA has already aborted.
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
+                                            volatile int* abort_flag, int code) {
+  const uint64_t t0 = gtime_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 127u) == 127u) {
+      if (*abort_flag) return false;
+      if (gtime_ns() - t0 > kWaitNs) break;
+    }
+  }
+  atomicCAS(&g_tc_error, 0, code);
+  *abort_flag = 1;
+  return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int code) {
+  if (mbar_try(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort_flag, code);
+}
+// Bounded wait used while draining after an abort: no error bookkeeping.
+__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = gtime_ns();
+  while (!mbar_try(bar, parity) && gtime_ns() - t0 < kWaitNs) {}
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm_100
+// version bits = 1.  Addresses and offsets are in bytes.
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+
+// Tile id -> (group, m tile, n tile).  Consecutive ids walk 16 row tiles
+// before moving to the next column tile, so a wave of CTAs shares A and B
+// tiles in L2.
+struct Tile { int g, m, n; };
+__device__ __forceinline__ Tile tile_of(int t, int m_tiles, int n_tiles) {
+  constexpr int GM = 16;
+  Tile r;
+  const int per_g = m_tiles * n_tiles;
+  r.g = t / per_g;
+  t -= r.g * per_g;
+  const int band = t / (GM * n_tiles);
+  const int rows = min(GM, m_tiles - band * GM);
+  const int in = t - band * GM * n_tiles;
+  r.m = band * GM + in % rows;
+  r.n = in / rows;
+  return r;
+}
+
+template <bool A_MN, bool B_MN, int BN, bool DUAL>
+__global__ void __launch_bounds__(THREADS, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mA1,
+              const __grid_constant__ CUtensorMap mA2, const __grid_constant__ CUtensorMap mB0,
+              const __grid_constant__ CUtensorMap mB1, const __grid_constant__ CUtensorMap mB2,
+              const Params p) {
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((A_MN ? 1u : 0u) << 15) |
+                             ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+                             ((uint32_t)(BM >> 4) << 24);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES);
+  // bars: full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 5);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  const uint32_t smem0 = smem_u32(smem);
+  const uint32_t bar0 = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto accf_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+  auto acce_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(accf_bar(a), 1);
+      mbar_init(acce_bar(a), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // work description shared by all roles
+  int rows_total = p.M;
+  if (p.mode == 1) rows_total = p.seg_off[p.G];
+  const int m_tiles = p.mode == 1 ? (rows_total + BM - 1) / BM : p.m_tiles;
+  const int groups = p.mode == 2 ? p.G : 1;
+  const int total = groups * m_tiles * p.n_tiles;
+  auto k_blocks = [&](const Tile& t, int part, int& k0) -> int {
+    if (p.mode == 2) {
+      k0 = p.seg_off[t.g];
+      return (p.seg_off[t.g + 1] - k0) / BK;
+    }
+    k0 = 0;
+    return p.kb[part];
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- producer
+    if (lane == 0) {
+      prefetch_map(&mA0);
+      prefetch_map(&mB0);
+      int s = 0;
+      uint32_t ph = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const Tile tl = tile_of(t, m_tiles, p.n_tiles);
+        const int m0 = tl.m * BM;
+        const int z = p.mode == 1 ? max(p.tile_expert[tl.m], 0) : 0;
+        for (int part = 0; part < p.nparts && ok; ++part) {
+          const CUtensorMap* ma = part == 0 ? &mA0 : (part == 1 ? &mA1 : &mA2);
+          const CUtensorMap* mb = part == 0 ? &mB0 : (part == 1 ? &mB1 : &mB2);
+          int kbase;
+          const int nk = k_blocks(tl, part, kbase);
+          for (int kb = 0; kb < nk; ++kb) {
+            if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, 1)) { ok = false; break; }
+            const uint32_t sa = smem0 + s * STAGE_BYTES, sb = sa + A_BYTES;
+            mbar_expect_tx(full_bar(s), STAGE_BYTES);
+            const int k0 = kbase + kb * BK;
+            if (!A_MN) {
+              tma_load_3d(sa, ma, full_bar(s), k0, m0, 0);
+            } else {
+              tma_load_3d(sa, ma, full_bar(s), m0, k0, 0);
+              tma_load_3d(sa + A_BYTES / 2, ma, full_bar(s), m0 + 64, k0, 0);
+            }
+            if (!DUAL) {
+              const int n0 = tl.n * BN;
+              if (!B_MN) {
+                tma_load_3d(sb, mb, full_bar(s), k0, n0, z);
+              } else {
+#pragma unroll
+                for (int j = 0; j < BN / 64; ++j)
+                  tma_load_3d(sb + j * 8192, mb, full_bar(s), n0 + 64 * j, k0, z);
+              }
+            } else {
+              // B = [gate tile | up tile], each BN/2 columns of the output
+              const int n0 = tl.n * (BN / 2);
+              const CUtensorMap* mg = &mB0;
+              const CUtensorMap* mu = &mB1;
+              if (!B_MN) {
+                tma_load_3d(sb, mg, full_bar(s), k0, n0, z);
+                tma_load_3d(sb + B_BYTES / 2, mu, full_bar(s), k0, n0, z);
+              } else {
+#pragma unroll
+                for (int j = 0; j < BN / 128; ++j) {
+                  tma_load_3d(sb + j * 8192, mg, full_bar(s), n0 + 64 * j, k0, z);
+                  tma_load_3d(sb + B_BYTES / 2 + j * 8192, mu, full_bar(s), n0 + 64 * j, k0, z);
+                }
+              }
+            }
+            ++issued;
+            if (++s == STAGES) { s = 0; ph ^= 1u; }
+          }
+        }
+      }
+      if (!ok) {
+        // drain: wait (bounded) for the copies of the stages still in flight
+        for (int q = 0; q < STAGES && q < issued; ++q) {
+          if (--s < 0) { s = STAGES - 1; ph ^= 1u; }
+          mbar_wait_drain(full_bar(s), ph);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int s = 0, a = 0;
+      uint32_t ph = 0, aph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const Tile tl = tile_of(t, m_tiles, p.n_tiles);
+        if (!mbar_wait(acce_bar(a), aph ^ 1u, abort_flag, 2)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(a * BN);
+        uint32_t accum = 0;
+        for (int part = 0; part < p.nparts && ok; ++part) {
+          int kbase;
+          const int nk = k_blocks(tl, part, kbase);
+          for (int kb = 0; kb < nk; ++kb) {
+            if (!mbar_wait(full_bar(s), ph, abort_flag, 3)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sa = smem0 + s * STAGE_BYTES, sb = sa + A_BYTES;
+#pragma unroll
+            for (int ks = 0; ks < BK / 16; ++ks) {
+              const uint64_t ad = A_MN ? sdesc(sa + ks * 2048, 8192, 1024)
+                                       : sdesc(sa + ks * 32, 16, 1024);
+              const uint64_t bd = B_MN ? sdesc(sb + ks * 2048, 8192, 1024)
+                                       : sdesc(sb + ks * 32, 16, 1024);
+              mma_bf16(d, ad, bd, IDESC, accum);
+              accum = 1;
+            }
+            mma_commit(empty_bar(s));
+            if (++s == STAGES) { s = 0; ph ^= 1u; }
+          }
+        }
+        if (!ok) break;
+        mma_commit(accf_bar(a));
+        if (++a == 2) { a = 0; aph ^= 1u; }
+      }
+      // make sure every issued MMA has finished before TMEM can be freed
+      mma_commit(drain_bar);
+      mbar_wait_drain(drain_bar, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    int a = 0;
+    uint32_t aph = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const Tile tl = tile_of(t, m_tiles, p.n_tiles);
+      if (!mbar_wait(accf_bar(a), aph, abort_flag, 4)) break;
+      tc_fence_after();
+      int kbase;
+      bool empty_k = false;
+      if (p.mode == 2) empty_k = k_blocks(tl, 0, kbase) == 0;
+      const int64_t m = (int64_t)tl.m * BM + row_in_tile;
+      const bool row_ok = m < rows_total;
+      const uint32_t tbase = tmem + (uint32_t)(a * BN) + ((uint32_t)(quad * 32) << 16);
+      if (p.epi == kSwiGLU) {
+        const int64_t nb = (int64_t)tl.n * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          float g[32], u[32];
+          tmem_ld32(tbase + c * 32, g);
+          tmem_ld32(tbase + BN / 2 + c * 32, u);
+          const int64_t n = nb + c * 32;
+          if (row_ok && n < p.N) {
+            uint32_t pg[16], pu[16], ph2[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              // g and u are rounded to bf16 first: h is computed from the
+              // stored residual, as the backward pass will see it
+              float g0 = __bfloat162float(__float2bfloat16_rn(g[2 * j]));
+              float g1 = __bfloat162float(__float2bfloat16_rn(g[2 * j + 1]));
+              float u0 = __bfloat162float(__float2bfloat16_rn(u[2 * j]));
+              float u1 = __bfloat162float(__float2bfloat16_rn(u[2 * j + 1]));
+              pg[j] = pack_bf16(g0, g1);
+              pu[j] = pack_bf16(u0, u1);
+              float h0 = g0 / (1.0f + expf(-g0)) * u0;
+              float h1 = g1 / (1.0f + expf(-g1)) * u1;
+              ph2[j] = pack_bf16(h0, h1);
+            }
+            uint4* og = (uint4*)(p.g_out + m * p.ldg + n);
+            uint4* ou = (uint4*)(p.u_out + m * p.ldg + n);
+            uint4* oh = (uint4*)(p.h_out + m * p.ldg + n);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              og[q] = make_uint4(pg[4 * q], pg[4 * q + 1], pg[4 * q + 2], pg[4 * q + 3]);
+              ou[q] = make_uint4(pu[4 * q], pu[4 * q + 1], pu[4 * q + 2], pu[4 * q + 3]);
+              oh[q] = make_uint4(ph2[4 * q], ph2[4 * q + 1], ph2[4 * q + 2], ph2[4 * q + 3]);
+            }
+          }
+        }
+      } else {
+        const int64_t nb = (int64_t)tl.n * BN;
+        char* Cb = (char*)p.C;
+        if (p.mode == 2) Cb += (int64_t)tl.g * p.c_gs * (p.epi == kStoreBF16 ? 2 : 4);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          if (!empty_k) tmem_ld32(tbase + c * 32, v);
+          else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+          const int64_t n = nb + c * 32;
+          if (!row_ok || n >= p.N) continue;
+          const bool full = n + 32 <= p.N;
+          if (p.epi == kStoreBF16) {
+            bf16* out = (bf16*)Cb + m * p.ldc + n;
+            if (full) {
+              uint4* o4 = (uint4*)out;
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                o4[q] = make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]), pack_bf16(v[8 * q + 2], v[8 * q + 3]),
+                                   pack_bf16(v[8 * q + 4], v[8 * q + 5]), pack_bf16(v[8 * q + 6], v[8 * q + 7]));
+            } else {
+              for (int j = 0; j < 32 && n + j < p.N; ++j) out[j] = __float2bfloat16_rn(v[j]);
+            }
+          } else if (p.epi == kSwiGLUBwd) {
+            // v = dH; dG = dH * u * s (1 + g (1 - s)), dU = dH * g * s
+            const bf16* gi = p.g_in + m * p.ldg + n;
+            const bf16* ui = p.u_in + m * p.ldg + n;
+            bf16* dgo = p.dg_out + m * p.ldg + n;
+            bf16* duo = p.du_out + m * p.ldg + n;
+            for (int j = 0; j < 32 && n + j < p.N; ++j) {
+              float z = __bfloat162float(gi[j]);
+              float uu = __bfloat162float(ui[j]);
+              float sg = 1.0f / (1.0f + expf(-z));
+              float dsilu = sg * (1.0f + z * (1.0f - sg));
+              dgo[j] = __float2bfloat16_rn(v[j] * uu * dsilu);
+              duo[j] = __float2bfloat16_rn(v[j] * (z * sg));
+            }
+          } else {
+            float* out = (float*)Cb + m * p.ldc + n;
+            if (p.epi == kAccumF32) {
+              if (empty_k) continue;
+              if (full) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  float4 o = ((float4*)out)[q];
+                  o.x += v[4 * q]; o.y += v[4 * q + 1]; o.z += v[4 * q + 2]; o.w += v[4 * q + 3];
+                  ((float4*)out)[q] = o;
+                }
+              } else {
+                for (int j = 0; j < 32 && n + j < p.N; ++j) out[j] += v[j];
+              }
+            } else {
+              if (p.epi == kAddResF32) {
+                const float* r = p.R + m * p.ldr + n;
+                for (int j = 0; j < 32; ++j)
+                  if (n + j < p.N) v[j] += r[j];
+              }
+              if (full) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                  ((float4*)out)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+              } else {
+                for (int j = 0; j < 32 && n + j < p.N; ++j) out[j] = v[j];
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce_bar(a));
+      if (++a == 2) { a = 0; aph ^= 1u; }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+// ------------------------------------------------------------------- host
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)f;
+  });
+  if (!fn) throw Error(-2, "cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+// 3-D bf16 tensor map: extents {inner, outer, depth}, row stride and depth
+// stride in elements, box {64, box_outer, 1}, 128-byte swizzle.
+CUtensorMap make_map(const void* base, int64_t inner, int64_t outer, int64_t depth,
+                     int64_t row_stride, int64_t depth_stride, int box_outer) {
+  DOP_REQUIRE(((uintptr_t)base & 15) == 0, "TMA base address must be 16-byte aligned");
+  DOP_REQUIRE(row_stride % 8 == 0 && depth_stride % 8 == 0,
+              "TMA strides must be multiples of 16 bytes (8 bf16)");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)depth};
+  cuuint64_t strides[2] = {(cuuint64_t)row_stride * 2, (cuuint64_t)depth_stride * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw Error(-2, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return m;
+}
+
+template <bool A_MN, bool B_MN, int BN, bool DUAL>
+void launch(const CUtensorMap* ma, const CUtensorMap* mb, const Params& p, int grid,
+            cudaStream_t s) {
+  constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+  auto kern = k_gemm_tc<A_MN, B_MN, BN, DUAL>;
+  static bool attr = false;
+  if (!attr) {
+    DOP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr = true;
+  }
+  kern<<<grid, THREADS, smem, s>>>(ma[0], ma[1], ma[2], mb[0], mb[1], mb[2], p);
+}
+
+}  // namespace tc
+
+// One tensor-core GEMM.  `parts` are (A, lda, B, ldb, K) triples summed into
+// one accumulator; all share the majors of g (a_t, b_t).
+void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue& te,
+             cudaStream_t s, int64_t& launches) {
+  using namespace tc;
+  constexpr int BN = 256;
+  DOP_REQUIRE(g.M > 0 && g.N > 0, "empty GEMM");
+  DOP_REQUIRE(g.K > 0, "GEMM contraction extent (the row extent for grouped contractions) must be > 0");
+  const bool dual = te.kind == kSwiGLU;
+  Params p{};
+  p.M = (int)g.M;
+  p.N = (int)g.N;
+  p.mode = g.group;
+  p.seg_off = g.seg_off;
+  p.tile_expert = g.tile_expert;
+  p.G = g.G;
+  if (te.kind >= 0) {
+    p.epi = te.kind;
+  } else if (g.epi == Epi::Store) {
+    p.epi = g.c_f32 ? kStoreF32 : kStoreBF16;
+  } else if (g.epi == Epi::Accum) {
+    DOP_REQUIRE(g.c_f32, "accumulation needs an fp32 C");
+    p.epi = kAccumF32;
+  } else if (g.epi == Epi::AddRes) {
+    DOP_REQUIRE(g.c_f32, "residual add needs an fp32 C");
+    p.epi = kAddResF32;
+  } else {
+    throw Error(-4, "epilogue not implemented on the tensor-core path");
+  }
+  DOP_REQUIRE(g.ldc % 8 == 0 || te.kind >= 0, "ldc must be a multiple of 8");
+  DOP_REQUIRE(te.kind < 0 || (g.N % 32 == 0 && te.ldg % 8 == 0),
+              "SwiGLU epilogues need N and ldg multiples of 32 and 8");
+  p.C = g.C;
+  p.ldc = g.ldc;
+  p.c_gs = g.c_gs;
+  p.R = g.R;
+  p.ldr = g.ldr;
+  p.g_out = te.g_out; p.u_out = te.u_out; p.h_out = te.h_out;
+  p.g_in = te.g_in; p.u_in = te.u_in; p.dg_out = te.dg_out; p.du_out = te.du_out;
+  p.ldg = te.ldg;
+  const int out_tile = dual ? BN / 2 : BN;
+  p.n_tiles = (int)ceil_div(g.N, out_tile);
+  p.m_tiles = (int)ceil_div(g.M, BM);
+  // parts
+  GemmPart parts[3];
+  parts[0] = GemmPart{g.A, g.lda, g.B, g.ldb, g.K};
+  DOP_REQUIRE(n_extra >= 0 && n_extra <= 2, "at most three K parts");
+  for (int i = 0; i < n_extra; ++i) parts[i + 1] = extra[i];
+  p.nparts = 1 + n_extra;
+  DOP_REQUIRE(g.group != 2 || p.nparts == 1, "grouped contraction takes one part");
+  CUtensorMap ma[3], mb[3];
+  const int64_t Gd = g.group == 1 ? g.G : 1;  // expert depth of B maps
+  for (int i = 0; i < p.nparts; ++i) {
+    const GemmPart& q = parts[i];
+    const int64_t Kext = g.group == 2 ? q.K : q.K;  // rows of the contraction
+    p.kb[i] = (int)ceil_div(q.K, BK);
+    // A: (M x K); K-major [M][K] or M-major [K][M]
+    if (!g.a_t) ma[i] = make_map(q.A, Kext, g.M, 1, q.lda, q.lda * g.M, BM);
+    else ma[i] = make_map(q.A, g.M, Kext, 1, q.lda, q.lda * Kext, 64);
+    // B: (K x N); N-major [K][N] (b_t = false) or K-major [N][K]
+    const int64_t Nb = dual ? g.N : g.N;
+    const int box_n = dual ? BN / 2 : BN;
+    if (!g.b_t) mb[i] = make_map(q.B, Nb, Kext, Gd, q.ldb, Gd > 1 ? g.b_gs : q.ldb * Kext, 64);
+    else mb[i] = make_map(q.B, Kext, Nb, Gd, q.ldb, Gd > 1 ? g.b_gs : q.ldb * Nb, box_n);
+  }
+  if (dual) {
+    DOP_REQUIRE(te.up_B != nullptr, "SwiGLU needs the up-projection weights");
+    if (!g.b_t) mb[1] = make_map(te.up_B, g.N, g.K, Gd, g.ldb, Gd > 1 ? g.b_gs : g.ldb * g.K, 64);
+    else mb[1] = make_map(te.up_B, g.K, g.N, Gd, g.ldb, Gd > 1 ? g.b_gs : g.ldb * g.N, BN / 2);
+    DOP_REQUIRE(p.nparts == 1, "SwiGLU GEMM takes one part");
+  }
+  for (int i = p.nparts; i < 3; ++i) ma[i] = ma[0];
+  for (int i = (dual ? 2 : p.nparts); i < 3; ++i) mb[i] = mb[0];
+  int64_t tiles = (int64_t)(g.group == 2 ? g.G : 1) * p.m_tiles * p.n_tiles;
+  int grid = (int)std::min<int64_t>(tiles, sm_count());
+  if (grid < 1) grid = 1;
+  const bool A = g.a_t, B = !g.b_t;  // MN-major flags
+  if (dual) {
+    if (!A && B) launch<false, true, BN, true>(ma, mb, p, grid, s);
+    else if (!A && !B) launch<false, false, BN, true>(ma, mb, p, grid, s);
+    else throw Error(-4, "SwiGLU GEMM needs a K-major A");
+  } else if (!A && B) launch<false, true, BN, false>(ma, mb, p, grid, s);
+  else if (!A && !B) launch<false, false, BN, false>(ma, mb, p, grid, s);
+  else if (A && B) launch<true, true, BN, false>(ma, mb, p, grid, s);
+  else launch<true, false, BN, false>(ma, mb, p, grid, s);
+  DOP_LAUNCHED(launches);
+}
+
+int tc_error_status() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int));
+  return v;
+}
+
+}  // namespace dop

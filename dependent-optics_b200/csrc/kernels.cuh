@@ -99,6 +99,28 @@ struct Gemm {
 template <typename T>
 void gemm_simt(const Gemm& g, cudaStream_t s, int64_t& launches);
 
+// Tensor-core (tcgen05) bf16 GEMM, gemm_tc.cu.  Extra K parts (A_i, B_i) are
+// summed into the same accumulator (same majors and grouping as g).  The
+// epilogue defaults to g.epi / g.c_f32; TcEpilogue selects the fused SwiGLU
+// forward (B = [gate | up], writes g, u, h) or backward (acc = dH; reads g, u,
+// writes dG, dU).
+struct GemmPart {
+  const void* A; int64_t lda; const void* B; int64_t ldb; int64_t K;
+};
+struct TcEpilogue {
+  int kind = -1;  // -1 from Gemm; 4 SwiGLU forward; 5 SwiGLU backward
+  const void* up_B = nullptr;
+  bf16 *g_out = nullptr, *u_out = nullptr, *h_out = nullptr;
+  const bf16 *g_in = nullptr, *u_in = nullptr;
+  bf16 *dg_out = nullptr, *du_out = nullptr;
+  int64_t ldg = 0;
+};
+constexpr int kTcSwiGLU = 4, kTcSwiGLUBwd = 5;
+void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue& te,
+             cudaStream_t s, int64_t& launches);
+// First bounded-wait failure recorded by a tensor-core kernel (0 = none).
+int tc_error_status();
+
 // ------------------------------------------------------------ attention
 // Sliding-window causal grouped-query attention (src/mixtral.rs:799-922),
 // flash-style: the residual is the log-sum-exp per (b, h, query), not the

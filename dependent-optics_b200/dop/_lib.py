@@ -85,6 +85,9 @@ SIGNATURES = [
     ("dop_program_backward", C.c_int, [_P, _P, _P, _P, _P, _P]),
     ("dop_program_forward_backward", C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P]),
     ("dop_mse_loss_grad", C.c_int, [_P, _P, _I64, _P, _P, _P]),
+    ("dop_gemm_bf16", C.c_int, [_I64, _I64, _I64, _P, _I64, C.c_int, _P, _I64, C.c_int, _P,
+                                _I64, C.c_int, C.c_int, _P]),
+    ("dop_device_status", C.c_int, []),
     ("dop_f32_to_bf16", C.c_int, [_P, _P, _I64, _P]),
     ("dop_sgd_step", C.c_int, [_P, _P, _I64, C.c_float, _P]),
 ]

@@ -190,6 +190,21 @@ int dop_program_forward_backward(dop_program* prog, const float* x,
 int dop_mse_loss_grad(const float* y, const float* target, int64_t n,
                       float* loss, float* dy, void* stream);
 
+/* --------------------------------------------------------------- linear
+ * The crate's `linear` contraction (src/mixtral.rs:616-659) on the tensor
+ * cores: C[m, n] (+)= sum_k A(m, k) B(k, n) with bf16 A, B and fp32
+ * accumulation.  A(m, k) = A[m*lda + k] (a_t = 0) or A[k*lda + m] (a_t = 1);
+ * B(k, n) = B[k*ldb + n] (b_t = 0, the crate's W[k*dout + n]) or
+ * B[n*ldb + k] (b_t = 1).  C is fp32 (c_f32 = 1) or bf16; accumulate = 1 adds
+ * into an fp32 C.  Leading dimensions must be multiples of 8 elements and the
+ * pointers 16-byte aligned. */
+int dop_gemm_bf16(int64_t M, int64_t N, int64_t K, const uint16_t* A, int64_t lda,
+                  int a_t, const uint16_t* B, int64_t ldb, int b_t, void* C,
+                  int64_t ldc, int c_f32, int accumulate, void* stream);
+/* First bounded-wait failure a tensor-core kernel recorded since load
+ * (0 = none); a non-zero code means a kernel gave up waiting and returned. */
+int dop_device_status(void);
+
 /* ----------------------------------------------------------- utilities */
 /* fp32 -> bf16 (round to nearest even), device arrays. */
 int dop_f32_to_bf16(const float* src, uint16_t* dst, int64_t n, void* stream);

@@ -81,7 +81,10 @@ class BlockResult:
 
     def __del__(self):
         if getattr(self, "_tape", None):
-            lib().orc_tape_free(self._tape)
+            try:
+                lib().orc_tape_free(self._tape)
+            except Exception:  # interpreter shutdown
+                pass
             self._tape = None
 
 
