@@ -1,0 +1,792 @@
+// attn_tc.cu — flash attention on the 5th-generation tensor cores (bf16,
+// head_dim 128), the bf16 lens's gqa_forward / gqa_backward
+// (src/mixtral.rs:799-922): causal sliding-window grouped-query attention,
+// visible(q, k) = k <= q && q - k < W.
+//
+// Forward, one CTA per (128-query tile, head, sequence):
+//   warp 0      TMA: the Q tile once, then K/V tiles of 128 keys into a
+//               2-stage ring (128B-swizzled, bf16)
+//   warp 1      TMEM owner; one thread issues S_j = Q K_j^T into one of two
+//               S buffers and PV_j = P_j V_j into a PV buffer (tcgen05.mma)
+//   warps 2..5  softmax, one query row per thread: online max / sum in the
+//               log2 domain, P_j written to shared memory as the bf16 A
+//               operand of the next MMA, O accumulated in registers
+//               (O = O * alpha + PV), log-sum-exp kept for the backward pass.
+// S_{j+1} runs on the tensor core while the softmax warps work on S_j.
+#include "kernels.cuh"
+#include "tc_ptx.cuh"
+
+namespace dop {
+namespace tc {
+
+constexpr int AT = 128;             // queries per CTA and keys per tile
+constexpr int HD = 128;             // head dim
+constexpr uint32_t HALF = 16384;    // [128 rows][64 cols] bf16 box
+constexpr uint32_t TILE = 2 * HALF; // [128 rows][128 cols] bf16 as two 64-col boxes
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct FwdParams {
+  int S, H, KV, group, window, n_qt;
+  float sl2;  // softmax scale * log2(e)
+  bf16* o;
+  float* lse;
+};
+
+// Write 32 bf16 values (row `r`, columns c0..c0+31 of a [128][128] K-major
+// tile stored as two 128B-swizzled 64-column boxes) to shared memory.
+__device__ __forceinline__ void st_tile_row32(uint8_t* tile, int r, int c0, const float* v) {
+  const int atom = c0 >> 6;
+  uint8_t* rowp = tile + atom * HALF + r * 128;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int chunk = ((c0 & 63) >> 3) + q;
+    const int swz = chunk ^ (r & 7);
+    uint4 val = make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]), pack_bf16(v[8 * q + 2], v[8 * q + 3]),
+                           pack_bf16(v[8 * q + 4], v[8 * q + 5]), pack_bf16(v[8 * q + 6], v[8 * q + 7]));
+    *reinterpret_cast<uint4*>(rowp + swz * 16) = val;
+  }
+}
+
+__global__ void __launch_bounds__(192, 1)
+    k_attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                  const __grid_constant__ CUtensorMap mv, const FwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + TILE;          // 2 stages
+  uint8_t* sV = smem + 3 * TILE;      // 2 stages
+  uint8_t* sP = smem + 5 * TILE;
+  uint64_t* bars = (uint64_t*)(smem + 6 * TILE);
+  uint32_t* tmem_slot = (uint32_t*)(bars + 14);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  const uint32_t b0 = smem_u32(bars);
+  const uint32_t q_full = b0, p_full = b0 + 8, pv_full = b0 + 16, pv_free = b0 + 24;
+  auto kv_full = [&](int st) { return b0 + 32 + 8u * st; };
+  auto kv_empty = [&](int st) { return b0 + 48 + 8u * st; };
+  auto s_full = [&](int st) { return b0 + 64 + 8u * st; };
+  auto s_free = [&](int st) { return b0 + 80 + 8u * st; };
+  const uint32_t drain = b0 + 96;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = p.n_qt - 1 - (int)blockIdx.x;  // longest rows first
+  const int h = blockIdx.y, b = blockIdx.z, kvh = h / p.group;
+  const int q0 = qt * AT;
+  const int lo = max(0, q0 - p.window + 1);
+  const int hi = min(p.S - 1, q0 + AT - 1);
+  const int kt0 = lo / AT, nt = hi / AT - kt0 + 1;
+  const int row0 = b * p.S;  // token row of position 0 of this sequence
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(pv_full, 1);
+    mbar_init(pv_free, 4);
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(kv_full(st), 1);
+      mbar_init(kv_empty(st), 1);
+      mbar_init(s_full(st), 1);
+      mbar_init(s_free(st), 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_map(&mq);
+      prefetch_map(&mk);
+      prefetch_map(&mv);
+      const uint32_t q_s = smem_u32(sQ);
+      mbar_expect_tx(q_full, TILE);
+      tma_load_3d(q_s, &mq, q_full, 0, h, row0 + q0);
+      tma_load_3d(q_s + HALF, &mq, q_full, 64, h, row0 + q0);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < nt; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_empty(st), ((j >> 1) & 1) ^ 1, abort_flag, 11)) { ok = false; break; }
+        const int k0 = (kt0 + j) * AT;
+        const uint32_t ks = smem_u32(sK + st * TILE), vs = smem_u32(sV + st * TILE);
+        mbar_expect_tx(kv_full(st), 2 * TILE);
+        tma_load_3d(ks, &mk, kv_full(st), 0, kvh, row0 + k0);
+        tma_load_3d(ks + HALF, &mk, kv_full(st), 64, kvh, row0 + k0);
+        tma_load_3d(vs, &mv, kv_full(st), 0, kvh, row0 + k0);
+        tma_load_3d(vs + HALF, &mv, kv_full(st), 64, kvh, row0 + k0);
+        ++issued;
+      }
+      if (!ok) {
+        mbar_wait_drain(q_full, 0);
+        for (int j = issued - 1; j >= 0 && j >= issued - 2; --j)
+          mbar_wait_drain(kv_full(j & 1), (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_bf16(128, 128, false, false);   // Q K^T
+      constexpr uint32_t ID_PV = idesc_bf16(128, 128, false, true);   // P V (V is N-major)
+      const uint32_t q_s = smem_u32(sQ), p_s = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, abort_flag, 12);
+      auto issue_pv = [&](int i) -> bool {
+        if (!mbar_wait(p_full, i & 1, abort_flag, 13)) return false;
+        if (!mbar_wait(pv_free, (i & 1) ^ 1, abort_flag, 14)) return false;
+        tc_fence_after();
+        const uint32_t vs = smem_u32(sV + (i & 1) * TILE);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + 256, kmajor_desc(p_s + (k >> 2) * HALF + (k & 3) * 32),
+                   mnmajor_desc(vs + k * 2048, HALF), ID_PV, k > 0);
+        mma_commit(pv_full);
+        mma_commit(kv_empty(i & 1));
+        return true;
+      };
+      for (int j = 0; j < nt && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_full(st), (j >> 1) & 1, abort_flag, 15)) { ok = false; break; }
+        if (!mbar_wait(s_free(st), ((j >> 1) & 1) ^ 1, abort_flag, 16)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ks = smem_u32(sK + st * TILE);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + st * 128, kmajor_desc(q_s + (k >> 2) * HALF + (k & 3) * 32),
+                   kmajor_desc(ks + (k >> 2) * HALF + (k & 3) * 32), ID_S, k > 0);
+        mma_commit(s_full(st));
+        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok) issue_pv(nt - 1);
+      mma_commit(drain);
+      mbar_wait_drain(drain, 0);
+    }
+  } else {
+    // ---------------------------------------------------------- softmax
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int qi = q0 + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    float o[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait(s_full(st), (j >> 1) & 1, abort_flag, 17)) { ok = false; break; }
+      tc_fence_after();
+      const int k0 = (kt0 + j) * AT;
+      const bool all_vis = (k0 + AT - 1 <= qi) && (qi - k0 < p.window);
+      const uint32_t ts = tmem + st * 128 + lane_off;
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(ts + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = k0 + c * 32 + i;
+          const bool vis = all_vis || (key <= qi && qi - key < p.window);
+          mx = vis ? fmaxf(mx, v[i]) : mx;
+        }
+      }
+      const float m_new = mx == -INFINITY ? m : fmaxf(m, mx * p.sl2);
+      const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_new);
+      // fold PV_{j-1} (it was computed against m_{j-1}) before P_j overwrites P
+      if (j > 0) {
+        if (!mbar_wait(pv_full, (j - 1) & 1, abort_flag, 18)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float pv[32];
+          tmem_ld32(tmem + 256 + lane_off + c * 32, pv);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha_prev + pv[i];
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pv_free);
+      }
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(ts + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = k0 + c * 32 + i;
+          const bool vis = all_vis || (key <= qi && qi - key < p.window);
+          const float e = vis ? exp2f(v[i] * p.sl2 - m_new) : 0.f;
+          v[i] = e;
+          sum += e;
+        }
+        st_tile_row32(sP, r, c * 32, v);
+      }
+      l = l * alpha + sum;
+      m = m_new;
+      alpha_prev = alpha;
+      tc_fence_before();
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(s_free(st));
+        mbar_arrive(p_full);
+      }
+    }
+    if (ok && mbar_wait(pv_full, (nt - 1) & 1, abort_flag, 19)) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float pv[32];
+        tmem_ld32(tmem + 256 + lane_off + c * 32, pv);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha_prev + pv[i];
+      }
+      if (qi < p.S) {
+        const float inv_l = 1.0f / l;
+        uint4* dst = reinterpret_cast<uint4*>(p.o + ((int64_t)(row0 + qi) * p.H + h) * HD);
+#pragma unroll
+        for (int q = 0; q < HD / 8; ++q)
+          dst[q] = make_uint4(pack_bf16(o[8 * q] * inv_l, o[8 * q + 1] * inv_l),
+                              pack_bf16(o[8 * q + 2] * inv_l, o[8 * q + 3] * inv_l),
+                              pack_bf16(o[8 * q + 4] * inv_l, o[8 * q + 5] * inv_l),
+                              pack_bf16(o[8 * q + 6] * inv_l, o[8 * q + 7] * inv_l));
+        // natural-log LSE of the scaled scores: m is max(s * scale) * log2(e)
+        p.lse[((int64_t)b * p.H + h) * p.S + qi] = m / kLog2e + logf(l);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+constexpr size_t kFwdSmem = 6 * TILE + 1024 + 256;
+
+// ------------------------------------------------------------------ backward
+// delta[b, h, i] = sum_d dO[i, d] O[i, d]  (= sum_j P_ij dA_ij of gqa_backward)
+__global__ void k_attn_delta_bf16(const bf16* __restrict__ o, const bf16* __restrict__ dout,
+                                  int64_t rows, int H, int S, float* __restrict__ delta) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;  // rows = T * H, row = t * H + h
+  const uint2 a = reinterpret_cast<const uint2*>(o + row * HD)[lane];
+  const uint2 g = reinterpret_cast<const uint2*>(dout + row * HD)[lane];
+  const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
+  float sacc = 0.f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    float2 x = __bfloat1622float2(a2[i]), y = __bfloat1622float2(g2[i]);
+    sacc += x.x * y.x + x.y * y.y;
+  }
+  sacc = warp_sum(sacc);
+  if (lane == 0) {
+    const int64_t t = row / H;
+    const int h = (int)(row % H);
+    const int64_t b = t / S, i = t % S;
+    delta[(b * H + h) * S + i] = sacc;
+  }
+}
+
+struct BwdParams {
+  int S, H, KV, group, window, n_tiles;
+  float sl2, scale;
+  const float* lse;
+  const float* delta;
+  float* dq;
+  float* dk;
+  float* dv;
+};
+
+// dQ: one CTA per (128-query tile, head, sequence).  Per key tile j:
+// S = Q K_j^T, dP = dO V_j^T (TMEM), dS = P (dP - delta) scale (bf16, smem),
+// dQ += dS K_j (TMEM accumulator across all key tiles).
+__global__ void __launch_bounds__(192, 1)
+    k_attn_dq_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                 const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
+                 const BwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sQ = smem;
+  uint8_t* sDO = smem + TILE;
+  uint8_t* sK = smem + 2 * TILE;  // 2 stages
+  uint8_t* sV = smem + 4 * TILE;  // 2 stages
+  uint8_t* sDS = smem + 6 * TILE;
+  uint64_t* bars = (uint64_t*)(smem + 7 * TILE);
+  uint32_t* tmem_slot = (uint32_t*)(bars + 12);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  const uint32_t b0 = smem_u32(bars);
+  const uint32_t q_full = b0, sd_full = b0 + 8, sd_free = b0 + 16, ds_full = b0 + 24,
+                 ds_free = b0 + 32, drain = b0 + 40;
+  auto kv_full = [&](int st) { return b0 + 48 + 8u * st; };
+  auto kv_empty = [&](int st) { return b0 + 64 + 8u * st; };
+  const uint32_t dq_done = b0 + 80;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = p.n_tiles - 1 - (int)blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z, kvh = h / p.group;
+  const int q0 = qt * AT;
+  const int lo = max(0, q0 - p.window + 1);
+  const int hi = min(p.S - 1, q0 + AT - 1);
+  const int kt0 = lo / AT, nt = hi / AT - kt0 + 1;
+  const int row0 = b * p.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(sd_full, 1);
+    mbar_init(sd_free, 4);
+    mbar_init(ds_full, 4);
+    mbar_init(ds_free, 1);
+    mbar_init(drain, 1);
+    mbar_init(dq_done, 1);
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(kv_full(st), 1);
+      mbar_init(kv_empty(st), 1);
+    }
+    *abort_flag = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t qs = smem_u32(sQ), dos = smem_u32(sDO);
+      mbar_expect_tx(q_full, 2 * TILE);
+      tma_load_3d(qs, &mq, q_full, 0, h, row0 + q0);
+      tma_load_3d(qs + HALF, &mq, q_full, 64, h, row0 + q0);
+      tma_load_3d(dos, &mdo, q_full, 0, h, row0 + q0);
+      tma_load_3d(dos + HALF, &mdo, q_full, 64, h, row0 + q0);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < nt; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_empty(st), ((j >> 1) & 1) ^ 1, abort_flag, 21)) { ok = false; break; }
+        const int k0 = (kt0 + j) * AT;
+        const uint32_t ks = smem_u32(sK + st * TILE), vs = smem_u32(sV + st * TILE);
+        mbar_expect_tx(kv_full(st), 2 * TILE);
+        tma_load_3d(ks, &mk, kv_full(st), 0, kvh, row0 + k0);
+        tma_load_3d(ks + HALF, &mk, kv_full(st), 64, kvh, row0 + k0);
+        tma_load_3d(vs, &mv, kv_full(st), 0, kvh, row0 + k0);
+        tma_load_3d(vs + HALF, &mv, kv_full(st), 64, kvh, row0 + k0);
+        ++issued;
+      }
+      if (!ok) {
+        mbar_wait_drain(q_full, 0);
+        for (int j = issued - 1; j >= 0 && j >= issued - 2; --j)
+          mbar_wait_drain(kv_full(j & 1), (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_SD = idesc_bf16(128, 128, false, false);  // Q K^T and dO V^T
+      constexpr uint32_t ID_DQ = idesc_bf16(128, 128, false, true);   // dS K (K is N-major)
+      const uint32_t qs = smem_u32(sQ), dos = smem_u32(sDO), dss = smem_u32(sDS);
+      bool ok = mbar_wait(q_full, 0, abort_flag, 22);
+      for (int j = 0; j < nt && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_full(st), (j >> 1) & 1, abort_flag, 23)) { ok = false; break; }
+        if (!mbar_wait(sd_free, (j & 1) ^ 1, abort_flag, 24)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ks = smem_u32(sK + st * TILE), vs = smem_u32(sV + st * TILE);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (k >> 2) * HALF + (k & 3) * 32;
+          mma_bf16(tmem, kmajor_desc(qs + off), kmajor_desc(ks + off), ID_SD, k > 0);
+          mma_bf16(tmem + 128, kmajor_desc(dos + off), kmajor_desc(vs + off), ID_SD, k > 0);
+        }
+        mma_commit(sd_full);
+        if (!mbar_wait(ds_full, j & 1, abort_flag, 25)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + 256, kmajor_desc(dss + (k >> 2) * HALF + (k & 3) * 32),
+                   mnmajor_desc(ks + k * 2048, HALF), ID_DQ, (j > 0 || k > 0) ? 1u : 0u);
+        mma_commit(ds_free);
+        mma_commit(kv_empty(st));
+      }
+      if (ok) mma_commit(dq_done);
+      mma_commit(drain);
+      mbar_wait_drain(drain, 0);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int qi = q0 + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const bool row_ok = qi < p.S;
+    const float lse2 = row_ok ? p.lse[((int64_t)b * p.H + h) * p.S + qi] * kLog2e : 0.f;
+    const float dlt = row_ok ? p.delta[((int64_t)b * p.H + h) * p.S + qi] : 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      if (!mbar_wait(sd_full, j & 1, abort_flag, 26)) { ok = false; break; }
+      if (j > 0 && !mbar_wait(ds_free, (j - 1) & 1, abort_flag, 27)) { ok = false; break; }
+      tc_fence_after();
+      const int k0 = (kt0 + j) * AT;
+      const bool all_vis = (k0 + AT - 1 <= qi) && (qi - k0 < p.window);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float sv[32], dp[32];
+        tmem_ld32(tmem + lane_off + c * 32, sv);
+        tmem_ld32(tmem + 128 + lane_off + c * 32, dp);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = k0 + c * 32 + i;
+          const bool vis = row_ok && (all_vis || (key <= qi && qi - key < p.window));
+          const float pr = vis ? exp2f(sv[i] * p.sl2 - lse2) : 0.f;
+          sv[i] = pr * (dp[i] - dlt) * p.scale;
+        }
+        st_tile_row32(sDS, r, c * 32, sv);
+      }
+      tc_fence_before();
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(sd_free);
+        mbar_arrive(ds_full);
+      }
+    }
+    if (ok && mbar_wait(dq_done, 0, abort_flag, 28)) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(tmem + 256 + lane_off + c * 32, v);
+        if (row_ok) {
+          float4* dst = reinterpret_cast<float4*>(p.dq + ((int64_t)(row0 + qi) * p.H + h) * HD + c * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+constexpr size_t kDqSmem = 7 * TILE + 1024 + 256;
+
+// dK, dV: one CTA per (128-key tile, kv head, sequence), looping over the
+// query heads of the group and the 64-query tiles that see the keys:
+// S^T = K Q^T, dP^T = V dO^T (TMEM, double-buffered), P^T and
+// dS^T = P^T (dP^T - delta) scale (bf16, smem), dV += P^T dO, dK += dS^T Q.
+constexpr int QB = 64;               // queries per tile
+constexpr uint32_t QHALF = 8192;     // [64 rows][64 cols] bf16 box
+constexpr uint32_t QTILE = 2 * QHALF;
+
+__global__ void __launch_bounds__(192, 1)
+    k_attn_dkdv_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                   const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
+                   const BwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + TILE;
+  uint8_t* sQ = smem + 2 * TILE;                // 2 stages of QTILE
+  uint8_t* sDO = sQ + 2 * QTILE;                // 2 stages of QTILE
+  uint8_t* sPT = sDO + 2 * QTILE;               // [128 keys][64 q] one atom
+  uint8_t* sDST = sPT + 16384;
+  float* sLD = (float*)(sDST + 16384);          // [4 warps][lse2 64 | delta 64]
+  uint64_t* bars = (uint64_t*)(sLD + 512);
+  uint32_t* tmem_slot = (uint32_t*)(bars + 16);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  const uint32_t b0 = smem_u32(bars);
+  const uint32_t kv_full = b0, pd_full = b0 + 8, pd_free = b0 + 16, drain = b0 + 24,
+                 acc_done = b0 + 32;
+  auto q_full = [&](int st) { return b0 + 40 + 8u * st; };
+  auto q_empty = [&](int st) { return b0 + 56 + 8u * st; };
+  auto s_full = [&](int st) { return b0 + 72 + 8u * st; };
+  auto s_free = [&](int st) { return b0 + 88 + 8u * st; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = (int)blockIdx.x;
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int k0 = kt * AT;
+  const int qlo = k0;
+  const int qhi = min(p.S - 1, k0 + AT - 1 + p.window - 1);
+  const int qt0 = qlo / QB, nq = qhi / QB - qt0 + 1;
+  const int total = nq * p.group;  // (head, query tile) pairs, head-major
+  const int row0 = b * p.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(pd_full, 4);
+    mbar_init(pd_free, 1);
+    mbar_init(drain, 1);
+    mbar_init(acc_done, 1);
+    for (int st = 0; st < 2; ++st) {
+      mbar_init(q_full(st), 1);
+      mbar_init(q_empty(st), 1);
+      mbar_init(s_full(st), 1);
+      mbar_init(s_free(st), 4);
+    }
+    *abort_flag = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t ks = smem_u32(sK), vs = smem_u32(sV);
+      mbar_expect_tx(kv_full, 2 * TILE);
+      tma_load_3d(ks, &mk, kv_full, 0, kvh, row0 + k0);
+      tma_load_3d(ks + HALF, &mk, kv_full, 64, kvh, row0 + k0);
+      tma_load_3d(vs, &mv, kv_full, 0, kvh, row0 + k0);
+      tma_load_3d(vs + HALF, &mv, kv_full, 64, kvh, row0 + k0);
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < total; ++i) {
+        const int st = i & 1;
+        const int h = kvh * p.group + i / nq;
+        const int qq0 = (qt0 + i % nq) * QB;
+        if (!mbar_wait(q_empty(st), ((i >> 1) & 1) ^ 1, abort_flag, 31)) { ok = false; break; }
+        const uint32_t qs = smem_u32(sQ + st * QTILE), dos = smem_u32(sDO + st * QTILE);
+        mbar_expect_tx(q_full(st), 2 * QTILE);
+        tma_load_3d(qs, &mq, q_full(st), 0, h, row0 + qq0);
+        tma_load_3d(qs + QHALF, &mq, q_full(st), 64, h, row0 + qq0);
+        tma_load_3d(dos, &mdo, q_full(st), 0, h, row0 + qq0);
+        tma_load_3d(dos + QHALF, &mdo, q_full(st), 64, h, row0 + qq0);
+        ++issued;
+      }
+      if (!ok) {
+        mbar_wait_drain(kv_full, 0);
+        for (int i = issued - 1; i >= 0 && i >= issued - 2; --i)
+          mbar_wait_drain(q_full(i & 1), (i >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t ID_ST = idesc_bf16(128, 64, false, false);   // K Q^T, V dO^T
+      constexpr uint32_t ID_ACC = idesc_bf16(128, 128, false, true);  // P^T dO, dS^T Q
+      const uint32_t ks = smem_u32(sK), vs = smem_u32(sV);
+      const uint32_t pts = smem_u32(sPT), dsts = smem_u32(sDST);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, 32);
+      auto issue_acc = [&](int i) -> bool {
+        if (!mbar_wait(pd_full, i & 1, abort_flag, 33)) return false;
+        tc_fence_after();
+        const int st = i & 1;
+        const uint32_t qs = smem_u32(sQ + st * QTILE), dos = smem_u32(sDO + st * QTILE);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          mma_bf16(tmem + 256, kmajor_desc(pts + k * 32), mnmajor_desc(dos + k * 2048, QHALF),
+                   ID_ACC, acc);
+          mma_bf16(tmem + 384, kmajor_desc(dsts + k * 32), mnmajor_desc(qs + k * 2048, QHALF),
+                   ID_ACC, acc);
+        }
+        mma_commit(pd_free);
+        mma_commit(q_empty(st));
+        return true;
+      };
+      for (int i = 0; i < total && ok; ++i) {
+        const int st = i & 1;
+        if (!mbar_wait(q_full(st), (i >> 1) & 1, abort_flag, 34)) { ok = false; break; }
+        if (!mbar_wait(s_free(st), ((i >> 1) & 1) ^ 1, abort_flag, 35)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t qs = smem_u32(sQ + st * QTILE), dos = smem_u32(sDO + st * QTILE);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t ka = (k >> 2) * HALF + (k & 3) * 32;   // K/V: two 16 KB d-boxes
+          const uint32_t kb = (k >> 2) * QHALF + (k & 3) * 32;  // Q/dO: two 8 KB d-boxes
+          mma_bf16(tmem + st * 128, kmajor_desc(ks + ka), kmajor_desc(qs + kb), ID_ST, k > 0);
+          mma_bf16(tmem + st * 128 + 64, kmajor_desc(vs + ka), kmajor_desc(dos + kb), ID_ST, k > 0);
+        }
+        mma_commit(s_full(st));
+        if (i > 0 && !issue_acc(i - 1)) { ok = false; break; }
+      }
+      if (ok && issue_acc(total - 1)) mma_commit(acc_done);
+      mma_commit(drain);
+      mbar_wait_drain(drain, 0);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;   // key row of this thread
+    const int kj = k0 + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    bool ok = true;
+    for (int i = 0; i < total; ++i) {
+      const int st = i & 1;
+      const int h = kvh * p.group + i / nq;
+      const int qq0 = (qt0 + i % nq) * QB;
+      // this warp's copy of the query tile's lse (log2 units) and delta
+      float* ld = sLD + quad * 128;
+      __syncwarp();
+      for (int e = lane; e < QB; e += 32) {
+        const int qi = qq0 + e;
+        const bool in = qi < p.S;
+        ld[e] = in ? p.lse[((int64_t)b * p.H + h) * p.S + qi] * kLog2e : 0.f;
+        ld[QB + e] = in ? p.delta[((int64_t)b * p.H + h) * p.S + qi] : 0.f;
+      }
+      __syncwarp();
+      if (!mbar_wait(s_full(st), (i >> 1) & 1, abort_flag, 36)) { ok = false; break; }
+      if (i > 0 && !mbar_wait(pd_free, (i - 1) & 1, abort_flag, 37)) { ok = false; break; }
+      tc_fence_after();
+      const bool key_ok = kj < p.S;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        float sv[32], dp[32];
+        tmem_ld32(tmem + st * 128 + lane_off + c * 32, sv);
+        tmem_ld32(tmem + st * 128 + 64 + lane_off + c * 32, dp);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int qi = qq0 + c * 32 + e;
+          const bool vis = key_ok && qi < p.S && kj <= qi && qi - kj < p.window;
+          const float pr = vis ? exp2f(sv[e] * p.sl2 - ld[c * 32 + e]) : 0.f;
+          sv[e] = pr;
+          dp[e] = pr * (dp[e] - ld[QB + c * 32 + e]) * p.scale;
+        }
+        // one 64-column atom: row r, chunks (c*4 .. c*4+3) swizzled by r & 7
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int swz = (c * 4 + q) ^ (r & 7);
+          *reinterpret_cast<uint4*>(sPT + r * 128 + swz * 16) =
+              make_uint4(pack_bf16(sv[8 * q], sv[8 * q + 1]), pack_bf16(sv[8 * q + 2], sv[8 * q + 3]),
+                         pack_bf16(sv[8 * q + 4], sv[8 * q + 5]), pack_bf16(sv[8 * q + 6], sv[8 * q + 7]));
+          *reinterpret_cast<uint4*>(sDST + r * 128 + swz * 16) =
+              make_uint4(pack_bf16(dp[8 * q], dp[8 * q + 1]), pack_bf16(dp[8 * q + 2], dp[8 * q + 3]),
+                         pack_bf16(dp[8 * q + 4], dp[8 * q + 5]), pack_bf16(dp[8 * q + 6], dp[8 * q + 7]));
+        }
+      }
+      tc_fence_before();
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(s_free(st));
+        mbar_arrive(pd_full);
+      }
+    }
+    if (ok && mbar_wait(acc_done, 0, abort_flag, 38)) {
+      tc_fence_after();
+      const bool key_ok = kj < p.S;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32], k[32];
+        tmem_ld32(tmem + 256 + lane_off + c * 32, v);
+        tmem_ld32(tmem + 384 + lane_off + c * 32, k);
+        if (key_ok) {
+          const int64_t base = ((int64_t)(row0 + kj) * p.KV + kvh) * HD + c * 32;
+          float4* dv4 = reinterpret_cast<float4*>(p.dv + base);
+          float4* dk4 = reinterpret_cast<float4*>(p.dk + base);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            dv4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            dk4[q] = make_float4(k[4 * q], k[4 * q + 1], k[4 * q + 2], k[4 * q + 3]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+constexpr size_t kDkdvSmem = 2 * TILE + 4 * QTILE + 2 * 16384 + 2048 + 1024 + 256;
+
+
+}  // namespace tc
+
+static void check_tc(const Attn& a) {
+  DOP_REQUIRE(a.hd == 128, "the tensor-core attention needs head_dim 128");
+  DOP_REQUIRE(a.causal && a.window >= 1, "the tensor-core attention is causal");
+  DOP_REQUIRE(a.H % a.KV == 0, "heads must be a multiple of kv_heads");
+  DOP_REQUIRE(a.B * a.S < (int64_t)1 << 31, "too many tokens");
+}
+
+void attn_fwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, bf16* o, float* lse,
+                 cudaStream_t s, int64_t& launches) {
+  using namespace tc;
+  check_tc(a);
+  const int64_t T = a.B * a.S;
+  const int64_t dq[3] = {HD, a.H, T}, sq[2] = {HD, (int64_t)a.H * HD};
+  const int64_t dk[3] = {HD, a.KV, T}, sk[2] = {HD, (int64_t)a.KV * HD};
+  const int box[3] = {64, 1, AT};
+  CUtensorMap mq = make_map3(q, dq, sq, box), mk = make_map3(k, dk, sk, box),
+              mv = make_map3(v, dk, sk, box);
+  FwdParams p;
+  p.S = (int)a.S; p.H = a.H; p.KV = a.KV; p.group = a.H / a.KV;
+  p.window = (int)std::min<int64_t>(a.window, a.S + 1);
+  p.n_qt = (int)ceil_div(a.S, AT);
+  p.sl2 = a.scale * kLog2e;
+  p.o = o;
+  p.lse = lse;
+  static bool attr = false;
+  if (!attr) {
+    DOP_CHECK_CUDA(cudaFuncSetAttribute(k_attn_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)kFwdSmem));
+    attr = true;
+  }
+  dim3 grid((unsigned)p.n_qt, (unsigned)a.H, (unsigned)a.B);
+  k_attn_fwd_tc<<<grid, 192, kFwdSmem, s>>>(mq, mk, mv, p);
+  DOP_LAUNCHED(launches);
+}
+
+void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, const bf16* o,
+                 const bf16* dout, const float* lse, float* delta, float* dq, float* dk, float* dv,
+                 cudaStream_t s, int64_t& launches) {
+  using namespace tc;
+  check_tc(a);
+  const int64_t T = a.B * a.S;
+  const int64_t rows = T * a.H;
+  k_attn_delta_bf16<<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(o, dout, rows, a.H, (int)a.S, delta);
+  DOP_LAUNCHED(launches);
+  const int64_t dq_[3] = {HD, a.H, T}, sq[2] = {HD, (int64_t)a.H * HD};
+  const int64_t dk_[3] = {HD, a.KV, T}, sk[2] = {HD, (int64_t)a.KV * HD};
+  const int box128[3] = {64, 1, AT}, box64[3] = {64, 1, QB};
+  BwdParams p;
+  p.S = (int)a.S; p.H = a.H; p.KV = a.KV; p.group = a.H / a.KV;
+  p.window = (int)std::min<int64_t>(a.window, a.S + 1);
+  p.sl2 = a.scale * kLog2e;
+  p.scale = a.scale;
+  p.lse = lse; p.delta = delta; p.dq = dq; p.dk = dk; p.dv = dv;
+  {
+    CUtensorMap mq = make_map3(q, dq_, sq, box128), mdo = make_map3(dout, dq_, sq, box128);
+    CUtensorMap mk = make_map3(k, dk_, sk, box128), mv = make_map3(v, dk_, sk, box128);
+    p.n_tiles = (int)ceil_div(a.S, AT);
+    static bool attr = false;
+    if (!attr) {
+      DOP_CHECK_CUDA(cudaFuncSetAttribute(k_attn_dq_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)kDqSmem));
+      attr = true;
+    }
+    dim3 grid((unsigned)p.n_tiles, (unsigned)a.H, (unsigned)a.B);
+    k_attn_dq_tc<<<grid, 192, kDqSmem, s>>>(mq, mk, mv, mdo, p);
+    DOP_LAUNCHED(launches);
+  }
+  {
+    CUtensorMap mq = make_map3(q, dq_, sq, box64), mdo = make_map3(dout, dq_, sq, box64);
+    CUtensorMap mk = make_map3(k, dk_, sk, box128), mv = make_map3(v, dk_, sk, box128);
+    p.n_tiles = (int)ceil_div(a.S, AT);
+    static bool attr = false;
+    if (!attr) {
+      DOP_CHECK_CUDA(cudaFuncSetAttribute(k_attn_dkdv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)kDkdvSmem));
+      attr = true;
+    }
+    dim3 grid((unsigned)p.n_tiles, (unsigned)a.KV, (unsigned)a.B);
+    k_attn_dkdv_tc<<<grid, 192, kDkdvSmem, s>>>(mq, mk, mv, mdo, p);
+    DOP_LAUNCHED(launches);
+  }
+}
+
+int attn_tc_error_status() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, tc::g_tc_error, sizeof(int));
+  return v;
+}
+
+}  // namespace dop

@@ -229,7 +229,11 @@ void Block::fwd(const Act* P, const float* x, float* y, cudaStream_t s) {
   at.causal = true; at.scale = 1.0f / sqrtf((float)hd);
   ph_end(s);
   ph_begin("attn_fwd", s);
-  attn_fwd_simt<Act>(at, q_, k_, v_, mix_, lse, s, launches);
+  if (std::is_same<Act, bf16>::value && hd == 128)
+    attn_fwd_tc(at, (const bf16*)q_, (const bf16*)k_, (const bf16*)v_, (bf16*)mix_, lse, s,
+                launches);
+  else
+    attn_fwd_simt<Act>(at, q_, k_, v_, mix_, lse, s, launches);
   ph_end(s);
   ph_begin("o_gemm", s);
   {
@@ -379,7 +383,11 @@ void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_
   ph_begin("attn_bwd", s);
   Attn at; at.B = B; at.S = S; at.H = H; at.KV = KV; at.hd = hd; at.window = cfg.sliding_window;
   at.causal = true; at.scale = 1.0f / sqrtf((float)hd);
-  attn_bwd_simt<Act>(at, q_, k_, v_, mix_, dmix_, lse, delta, dq, dk, dv, s, launches);
+  if (!f32 && hd == 128)
+    attn_bwd_tc(at, (const bf16*)q_, (const bf16*)k_, (const bf16*)v_, (const bf16*)mix_,
+                (const bf16*)dmix_, lse, delta, dq, dk, dv, s, launches);
+  else
+    attn_bwd_simt<Act>(at, q_, k_, v_, mix_, dmix_, lse, delta, dq, dk, dv, s, launches);
   ph_end(s);
   ph_begin("rope_bwd", s);
   rope<float, Act>(dq, dq_, T, (int)S, H, hd, rope_cos, rope_sin, -1.f, s, launches);

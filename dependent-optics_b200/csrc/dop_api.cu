@@ -35,6 +35,11 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 }  // namespace
 
 namespace dop {
+int tc_error_status() {
+  int e = gemm_tc_error_status();
+  return e ? e : attn_tc_error_status();
+}
+
 int sm_count() {
   static int cached[16] = {0};
   int dev = 0;
@@ -535,6 +540,62 @@ int dop_gemm_bf16(int64_t M, int64_t N, int64_t K, const uint16_t* A, int64_t ld
 }
 
 int dop_device_status(void) { return dop::tc_error_status(); }
+
+namespace {
+dop::Attn gqa_desc(int64_t batch, int64_t seq, int64_t heads, int64_t kv_heads, int64_t hd,
+                   int64_t window) {
+  DOP_REQUIRE(batch >= 1 && seq >= 1 && heads >= 1 && kv_heads >= 1 && heads % kv_heads == 0,
+              "bad attention shape");
+  DOP_REQUIRE(hd >= 2 && hd % 2 == 0 && window >= 1, "bad head_dim or window");
+  dop::Attn a;
+  a.B = batch; a.S = seq; a.H = (int)heads; a.KV = (int)kv_heads; a.hd = (int)hd;
+  a.window = window; a.causal = true; a.scale = 1.0f / sqrtf((float)hd);
+  return a;
+}
+}  // namespace
+
+int dop_gqa_forward(int64_t batch, int64_t seq, int64_t heads, int64_t kv_heads, int64_t hd,
+                    int64_t window, int precision, const void* q, const void* k, const void* v,
+                    void* o, float* lse, void* s) {
+  return guarded([&] {
+    DOP_REQUIRE(q && k && v && o && lse, "null pointer");
+    dop::Attn a = gqa_desc(batch, seq, heads, kv_heads, hd, window);
+    int64_t l = 0;
+    if (precision == DOP_BF16 && hd == 128)
+      dop::attn_fwd_tc(a, (const dop::bf16*)q, (const dop::bf16*)k, (const dop::bf16*)v,
+                       (dop::bf16*)o, lse, as_stream(s), l);
+    else if (precision == DOP_BF16)
+      dop::attn_fwd_simt<dop::bf16>(a, (const dop::bf16*)q, (const dop::bf16*)k,
+                                    (const dop::bf16*)v, (dop::bf16*)o, lse, as_stream(s), l);
+    else
+      dop::attn_fwd_simt<float>(a, (const float*)q, (const float*)k, (const float*)v, (float*)o,
+                                lse, as_stream(s), l);
+  });
+}
+
+int dop_gqa_backward(int64_t batch, int64_t seq, int64_t heads, int64_t kv_heads, int64_t hd,
+                     int64_t window, int precision, const void* q, const void* k, const void* v,
+                     const void* o, const void* dout, const float* lse, float* delta_ws,
+                     float* dq, float* dk, float* dv, void* s) {
+  return guarded([&] {
+    DOP_REQUIRE(q && k && v && o && dout && lse && delta_ws && dq && dk && dv, "null pointer");
+    dop::Attn a = gqa_desc(batch, seq, heads, kv_heads, hd, window);
+    int64_t l = 0;
+    if (precision == DOP_BF16 && hd == 128)
+      dop::attn_bwd_tc(a, (const dop::bf16*)q, (const dop::bf16*)k, (const dop::bf16*)v,
+                       (const dop::bf16*)o, (const dop::bf16*)dout, lse, delta_ws, dq, dk, dv,
+                       as_stream(s), l);
+    else if (precision == DOP_BF16)
+      dop::attn_bwd_simt<dop::bf16>(a, (const dop::bf16*)q, (const dop::bf16*)k,
+                                    (const dop::bf16*)v, (const dop::bf16*)o,
+                                    (const dop::bf16*)dout, lse, delta_ws, dq, dk, dv,
+                                    as_stream(s), l);
+    else
+      dop::attn_bwd_simt<float>(a, (const float*)q, (const float*)k, (const float*)v,
+                                (const float*)o, (const float*)dout, lse, delta_ws, dq, dk, dv,
+                                as_stream(s), l);
+  });
+}
 
 int dop_f32_to_bf16(const float* src, uint16_t* dst, int64_t n, void* s) {
   return guarded([&] {

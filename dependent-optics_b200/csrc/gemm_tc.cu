@@ -27,17 +27,15 @@
 
 #include "kernels.cuh"
 
+#include "tc_ptx.cuh"
+
 namespace dop {
-
-__device__ int g_tc_error;  // first bounded-wait failure seen by any CTA (0 = none)
-
 namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int STAGES = 4;
 constexpr int THREADS = 192;
-constexpr uint64_t kWaitNs = 4000000000ull;  // 4 s of device time per wait
 
 enum EpiKind : int {
   kStoreF32 = 0,
@@ -67,122 +65,6 @@ struct Params {
   bf16 *dg_out, *du_out;
   int64_t ldg;
 };
-
-// ------------------------------------------------------------ PTX wrappers
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ uint64_t gtime_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// Bounded wait on phase `parity`: false when it ran out (kWaitNs of device
-// time; the error code is recorded and the CTA's abort flag raised) or when
-// another role of the CTA has already aborted.
-__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity,
-                                            volatile int* abort_flag, int code) {
-  const uint64_t t0 = gtime_ns();
-  for (uint32_t i = 0;; ++i) {
-    if (mbar_try(bar, parity)) return true;
-    if ((i & 127u) == 127u) {
-      if (*abort_flag) return false;
-      if (gtime_ns() - t0 > kWaitNs) break;
-    }
-  }
-  atomicCAS(&g_tc_error, 0, code);
-  *abort_flag = 1;
-  return false;
-}
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int code) {
-  if (mbar_try(bar, parity)) return true;
-  return mbar_wait_slow(bar, parity, abort_flag, code);
-}
-// Bounded wait used while draining after an abort: no error bookkeeping.
-__device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
-  const uint64_t t0 = gtime_ns();
-  while (!mbar_try(bar, parity) && gtime_ns() - t0 < kWaitNs) {}
-}
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int c0, int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-      "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                         uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm_100
-// version bits = 1.  Addresses and offsets are in bytes.
-__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-  return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-  __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&t);
-}
 
 // Tile id -> (group, m tile, n tile).  Consecutive ids walk 16 row tiles
 // before moving to the next column tile, so a wave of CTAs shares A and B
@@ -526,25 +408,37 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 3-D bf16 tensor map: extents {inner, outer, depth}, row stride and depth
-// stride in elements, box {64, box_outer, 1}, 128-byte swizzle.
-CUtensorMap make_map(const void* base, int64_t inner, int64_t outer, int64_t depth,
-                     int64_t row_stride, int64_t depth_stride, int box_outer) {
+}  // namespace tc
+
+// 3-D bf16 tensor map with 128-byte swizzle: extents dims[0..2] (dims[0]
+// contiguous), strides of dims 1 and 2 in elements, box box[0..2].
+CUtensorMap make_map3(const void* base, const int64_t dims[3], const int64_t strides[2],
+                      const int box[3]) {
   DOP_REQUIRE(((uintptr_t)base & 15) == 0, "TMA base address must be 16-byte aligned");
-  DOP_REQUIRE(row_stride % 8 == 0 && depth_stride % 8 == 0,
+  DOP_REQUIRE(strides[0] % 8 == 0 && strides[1] % 8 == 0,
               "TMA strides must be multiples of 16 bytes (8 bf16)");
   CUtensorMap m;
-  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)depth};
-  cuuint64_t strides[2] = {(cuuint64_t)row_stride * 2, (cuuint64_t)depth_stride * 2};
-  cuuint32_t box[3] = {64, (cuuint32_t)box_outer, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
-                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  cuuint64_t gd[3] = {(cuuint64_t)dims[0], (cuuint64_t)dims[1], (cuuint64_t)dims[2]};
+  cuuint64_t gs[2] = {(cuuint64_t)strides[0] * 2, (cuuint64_t)strides[1] * 2};
+  cuuint32_t bx[3] = {(cuuint32_t)box[0], (cuuint32_t)box[1], (cuuint32_t)box[2]};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = tc::encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), gd,
+                               gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     throw Error(-2, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return m;
+}
+
+namespace tc {
+// 3-D map {inner, outer, depth} with box {64, box_outer, 1}.
+CUtensorMap make_map(const void* base, int64_t inner, int64_t outer, int64_t depth,
+                     int64_t row_stride, int64_t depth_stride, int box_outer) {
+  const int64_t dims[3] = {inner, outer, depth};
+  const int64_t strides[2] = {row_stride, depth_stride};
+  const int box[3] = {64, box_outer, 1};
+  return make_map3(base, dims, strides, box);
 }
 
 template <bool A_MN, bool B_MN, int BN, bool DUAL>
@@ -650,9 +544,9 @@ void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue
   DOP_LAUNCHED(launches);
 }
 
-int tc_error_status() {
+int gemm_tc_error_status() {
   int v = 0;
-  cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int));
+  cudaMemcpyFromSymbol(&v, tc::g_tc_error, sizeof(int));
   return v;
 }
 

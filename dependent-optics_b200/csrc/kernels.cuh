@@ -1,6 +1,8 @@
 // kernels.cuh — launchers of every libdop kernel, grouped by file.
 #pragma once
 
+#include <cuda.h>
+
 #include <algorithm>
 
 #include "common.cuh"
@@ -118,8 +120,14 @@ struct TcEpilogue {
 constexpr int kTcSwiGLU = 4, kTcSwiGLUBwd = 5;
 void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue& te,
              cudaStream_t s, int64_t& launches);
+// 3-D bf16 TMA descriptor, 128-byte swizzle: extents dims (dims[0]
+// contiguous), strides of dims 1 and 2 in elements, box extents.
+CUtensorMap make_map3(const void* base, const int64_t dims[3], const int64_t strides[2],
+                      const int box[3]);
 // First bounded-wait failure recorded by a tensor-core kernel (0 = none).
 int tc_error_status();
+int gemm_tc_error_status();
+int attn_tc_error_status();
 
 // ------------------------------------------------------------ attention
 // Sliding-window causal grouped-query attention (src/mixtral.rs:799-922),
@@ -133,6 +141,12 @@ struct Attn {
 template <typename T>
 void attn_fwd_simt(const Attn& a, const T* q, const T* k, const T* v, T* o, float* lse,
                    cudaStream_t s, int64_t& launches);
+// Tensor-core (tcgen05) flash attention for bf16, head_dim 128 (attn_tc.cu).
+void attn_fwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, bf16* o, float* lse,
+                 cudaStream_t s, int64_t& launches);
+void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, const bf16* o,
+                 const bf16* dout, const float* lse, float* delta, float* dq, float* dk, float* dv,
+                 cudaStream_t s, int64_t& launches);
 template <typename T>
 void attn_bwd_simt(const Attn& a, const T* q, const T* k, const T* v, const T* o, const T* dout,
                    const float* lse, float* delta, float* dq, float* dk, float* dv,

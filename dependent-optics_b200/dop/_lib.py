@@ -88,6 +88,10 @@ SIGNATURES = [
     ("dop_gemm_bf16", C.c_int, [_I64, _I64, _I64, _P, _I64, C.c_int, _P, _I64, C.c_int, _P,
                                 _I64, C.c_int, C.c_int, _P]),
     ("dop_device_status", C.c_int, []),
+    ("dop_gqa_forward", C.c_int, [_I64, _I64, _I64, _I64, _I64, _I64, C.c_int, _P, _P, _P, _P,
+                                  _P, _P]),
+    ("dop_gqa_backward", C.c_int, [_I64, _I64, _I64, _I64, _I64, _I64, C.c_int, _P, _P, _P, _P,
+                                   _P, _P, _P, _P, _P, _P, _P]),
     ("dop_f32_to_bf16", C.c_int, [_P, _P, _I64, _P]),
     ("dop_sgd_step", C.c_int, [_P, _P, _I64, C.c_float, _P]),
 ]

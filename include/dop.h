@@ -201,6 +201,23 @@ int dop_mse_loss_grad(const float* y, const float* target, int64_t n,
 int dop_gemm_bf16(int64_t M, int64_t N, int64_t K, const uint16_t* A, int64_t lda,
                   int a_t, const uint16_t* B, int64_t ldb, int b_t, void* C,
                   int64_t ldc, int c_f32, int accumulate, void* stream);
+/* ------------------------------------------------------------ attention
+ * The crate's sliding-window grouped-query attention as a lens, gqa_forward /
+ * gqa_backward (src/mixtral.rs:799-922): q [B*S, H, hd], k/v [B*S, KV, hd]
+ * (post-RoPE), key j visible from query i iff j <= i && i - j < window, scale
+ * 1/sqrt(hd).  The residual is lse [B, H, S] (log-sum-exp of the scaled
+ * scores) instead of the probabilities.  Precision DOP_BF16 takes bf16 q/k/v/o
+ * and runs on the tensor cores when hd == 128; DOP_F32 takes fp32 tensors.
+ * Backward writes fp32 dq/dk/dv and needs `delta_ws`, B*H*S floats of scratch. */
+int dop_gqa_forward(int64_t batch, int64_t seq, int64_t heads, int64_t kv_heads,
+                    int64_t head_dim, int64_t window, int precision, const void* q,
+                    const void* k, const void* v, void* o, float* lse, void* stream);
+int dop_gqa_backward(int64_t batch, int64_t seq, int64_t heads, int64_t kv_heads,
+                     int64_t head_dim, int64_t window, int precision, const void* q,
+                     const void* k, const void* v, const void* o, const void* dout,
+                     const float* lse, float* delta_ws, float* dq, float* dk, float* dv,
+                     void* stream);
+
 /* First bounded-wait failure a tensor-core kernel recorded since load
  * (0 = none); a non-zero code means a kernel gave up waiting and returned. */
 int dop_device_status(void);

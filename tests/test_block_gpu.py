@@ -165,14 +165,17 @@ def test_f32_block_c2_widths(cuda):
     compare(cfg, gpu, ref, F32_TOL)
 
 
-@pytest.mark.parametrize("kind", ["moe", "dense"])
+@pytest.mark.parametrize("kind", ["moe", "dense", "moe-hd128"])
 def test_bf16_block_matches_oracle_on_rounded_inputs(cuda, kind):
     if kind == "moe":
         cfg = small_cfg(dim=128, head_dim=32, intermediate=192)
+    elif kind == "moe-hd128":  # head_dim 128: tensor-core attention, window < seq
+        cfg = small_cfg(dim=256, heads=4, kv_heads=2, head_dim=128, intermediate=256,
+                        sliding_window=100)
     else:
         cfg = small_cfg(dim=128, heads=4, kv_heads=4, head_dim=32, intermediate=192, experts=1,
                         top_k=1, sliding_window=10_000, rope_theta=1e4)
-    batch, seq = 2, 80
+    batch, seq = (2, 200) if kind == "moe-hd128" else (2, 80)
     lp, x, dy = make_inputs(cfg, batch, seq, seed=3)
     lp, x, dy = bf16_round(lp), bf16_round(x), bf16_round(dy)
     gpu = run_gpu(cfg, batch, seq, lp, x, dy, DOP_BF16)
