@@ -53,6 +53,12 @@ WORKLOADS = {
                                  head_dim=128, intermediate=5632, experts=1, top_k=1,
                                  rms_eps=1e-5, rope_theta=1e4, sliding_window=2048),
                         batch=8, seq=2048, precision="bf16", skew=False),
+    # Mixtral-8x7B widths at batch 1, seq 1024: the small case for profiler captures
+    "mixtral8x7b_block_profile": dict(cfg=dict(vocab=32000, dim=4096, layers=1, heads=32,
+                                               kv_heads=8, head_dim=128, intermediate=14336,
+                                               experts=8, top_k=2, rms_eps=1e-5, rope_theta=1e6,
+                                               sliding_window=4096),
+                                      batch=1, seq=1024, precision="bf16", skew=False),
     # small Mixtral block, fp32
     "small_mixtral_block_f32": dict(cfg=dict(vocab=32000, dim=512, layers=1, heads=8, kv_heads=2,
                                              head_dim=64, intermediate=1408, experts=8, top_k=2,
@@ -276,14 +282,15 @@ def run_ours(a):
         ev0.record(stream)
         for _ in range(a.steps):
             step()
-            # phase events were recorded on `stream` inside the step; read them
-            # after the timed loop would overwrite them, so accumulate lazily
-            for name, ms in blk.phase_times():
-                phase_acc.setdefault(name, []).append(ms)
         ev1.record(stream)
         torch.cuda.synchronize(dev)
+    # per-phase CUDA events of the last timed step (recorded on `stream`
+    # inside it; read after the loop so the timed region has no host sync)
+    for name, pms in blk.phase_times():
+        phase_acc.setdefault(name, []).append(pms)
     launches = blk.launches() - launches0
     blk.set_timing(False)
+    clk_summary = clk.summary()
     ms = ev0.elapsed_time(ev1) / a.steps
     if world > 1:
         t = torch.tensor([ms], device=dev)
@@ -356,7 +363,7 @@ def run_ours(a):
                          "traffic": None, "peak_source": f"{src} bf16_tflops (burst)"},
             "phases_ms": phases,
             "e2e": e2e, "gpu_launches": launches // max(1, a.steps) * a.steps,
-            "clocks": clk.summary(), "cpu_baseline": cpu,
+            "clocks": clk_summary, "cpu_baseline": cpu,
         }
         print(json.dumps(out), flush=True)
     if world > 1:
@@ -373,8 +380,12 @@ def main():
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiler run: no CPU baseline, no e2e, warm-up may be < 3")
     a = ap.parse_args()
-    if a.warmup < 3 and a.impl == "ours":
+    if a.profile:
+        a.no_cpu_baseline = a.no_e2e = True
+    elif a.warmup < 3 and a.impl == "ours":
         a.warmup = 3
     if a.impl == "reference":
         run_reference(a)

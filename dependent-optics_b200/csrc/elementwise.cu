@@ -139,67 +139,77 @@ __global__ void k_rmsnorm_router(const float* __restrict__ x, const T* __restric
   }
 }
 
-// rmsnorm_bwd (src/mixtral.rs:696-723) for a chunk of rows per CTA:
-// dx = r (dy*w - xhat * mean(dy*w*xhat)) (+ res), and this chunk's partial of
-// dw[i] = sum_t dy[t,i] * xhat[t,i], written to dw_part[chunk, i].
-// blockDim.x * vec covers D; each thread owns D / blockDim.x columns.
+// rmsnorm_bwd (src/mixtral.rs:696-723), input cotangent: one warp per row,
+// dx = r (dy*w - xhat * mean(dy*w*xhat)) (+ res), xhat = x r.  Rows are read
+// twice (the second pass hits L2), float4 when D % 128 == 0.
 template <typename T>
-__global__ void k_rmsnorm_bwd(const float* __restrict__ dy, const float* __restrict__ x,
-                              const float* __restrict__ inv, const T* __restrict__ w,
-                              const float* __restrict__ res, int64_t rows, int D,
-                              int rows_per_chunk, float* __restrict__ dx, T* __restrict__ dx_act,
-                              float* __restrict__ dw_part) {
-  const int chunk = blockIdx.x;
-  const int64_t r0 = (int64_t)chunk * rows_per_chunk;
-  const int64_t r1 = ::min((int64_t)(rows), (int64_t)(r0 + rows_per_chunk));
-  __shared__ float red[32];
-  constexpr int kCols = 32;  // max columns per thread (D <= 32 * blockDim)
-  float dwacc[kCols];
-  float wv[kCols];
-  const int per = (D + blockDim.x - 1) / blockDim.x;
-#pragma unroll
-  for (int c = 0; c < kCols; ++c) {
-    dwacc[c] = 0.f;
-    int i = threadIdx.x + c * blockDim.x;
-    wv[c] = (c < per && i < D) ? ld(&w[i]) : 0.f;
+__global__ void k_rmsnorm_bwd_rows(const float* __restrict__ dy, const float* __restrict__ x,
+                                   const float* __restrict__ inv, const T* __restrict__ w,
+                                   const float* __restrict__ res, int64_t rows, int D,
+                                   float* __restrict__ dx, T* __restrict__ dx_act) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float r = inv[row];
+  const float* xr = x + row * D;
+  const float* gr = dy + row * D;
+  float dot = 0.f;
+  const bool vec = (D & 127) == 0;
+  if (vec) {
+    for (int i = lane * 4; i < D; i += 128) {
+      const float4 xv = *reinterpret_cast<const float4*>(xr + i);
+      const float4 gv = *reinterpret_cast<const float4*>(gr + i);
+      dot += (gv.x * ld(&w[i])) * (xv.x * r) + (gv.y * ld(&w[i + 1])) * (xv.y * r) +
+             (gv.z * ld(&w[i + 2])) * (xv.z * r) + (gv.w * ld(&w[i + 3])) * (xv.w * r);
+    }
+  } else {
+    for (int i = lane; i < D; i += 32) dot += (gr[i] * ld(&w[i])) * (xr[i] * r);
   }
-  for (int64_t t = r0; t < r1; ++t) {
-    const float r = inv[t];
-    float dot = 0.f;
-#pragma unroll
-    for (int c = 0; c < kCols; ++c) {
-      int i = threadIdx.x + c * blockDim.x;
-      if (c < per && i < D) {
-        float xhat = x[t * D + i] * r;
-        float g = dy[t * D + i];
-        dwacc[c] += g * xhat;
-        dot += g * wv[c] * xhat;
+  dot = warp_sum(dot);
+  const float mean = dot / (float)D;
+  if (vec) {
+    for (int i = lane * 4; i < D; i += 128) {
+      const float4 xv = *reinterpret_cast<const float4*>(xr + i);
+      const float4 gv = *reinterpret_cast<const float4*>(gr + i);
+      float4 o;
+      o.x = r * (gv.x * ld(&w[i]) - (xv.x * r) * mean);
+      o.y = r * (gv.y * ld(&w[i + 1]) - (xv.y * r) * mean);
+      o.z = r * (gv.z * ld(&w[i + 2]) - (xv.z * r) * mean);
+      o.w = r * (gv.w * ld(&w[i + 3]) - (xv.w * r) * mean);
+      if (res) {
+        const float4 rv = *reinterpret_cast<const float4*>(res + row * D + i);
+        o.x += rv.x; o.y += rv.y; o.z += rv.z; o.w += rv.w;
+      }
+      *reinterpret_cast<float4*>(dx + row * D + i) = o;
+      if (dx_act) {
+        T* da = dx_act + row * D + i;
+        st(&da[0], o.x); st(&da[1], o.y); st(&da[2], o.z); st(&da[3], o.w);
       }
     }
-    dot = warp_sum(dot);
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = dot;
-    __syncthreads();
-    float tot = 0.f;
-    for (int q = 0; q < (int)(blockDim.x >> 5); ++q) tot += red[q];
-    const float mean = tot / (float)D;
-#pragma unroll
-    for (int c = 0; c < kCols; ++c) {
-      int i = threadIdx.x + c * blockDim.x;
-      if (c < per && i < D) {
-        float xhat = x[t * D + i] * r;
-        float v = r * (dy[t * D + i] * wv[c] - xhat * mean);
-        if (res) v += res[t * D + i];
-        dx[t * D + i] = v;
-        if (dx_act) st(&dx_act[t * D + i], v);
-      }
+  } else {
+    for (int i = lane; i < D; i += 32) {
+      float v = r * (gr[i] * ld(&w[i]) - (xr[i] * r) * mean);
+      if (res) v += res[row * D + i];
+      dx[row * D + i] = v;
+      if (dx_act) st(&dx_act[row * D + i], v);
     }
   }
-#pragma unroll
-  for (int c = 0; c < kCols; ++c) {
-    int i = threadIdx.x + c * blockDim.x;
-    if (c < per && i < D) dw_part[(int64_t)chunk * D + i] = dwacc[c];
-  }
+}
+
+// Weight adjoint partials: part[c, i] = sum_{t in chunk c} dy[t,i] * x[t,i] r[t],
+// rows in increasing order (deterministic).
+__global__ void k_rmsnorm_dw_part(const float* __restrict__ dy, const float* __restrict__ x,
+                                  const float* __restrict__ inv, int64_t rows, int D,
+                                  int rows_per_chunk, float* __restrict__ part) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int c = blockIdx.y;
+  if (i >= D) return;
+  const int64_t t0 = (int64_t)c * rows_per_chunk;
+  const int64_t t1 = ::min((int64_t)rows, t0 + rows_per_chunk);
+  float acc = 0.f;
+#pragma unroll 8
+  for (int64_t t = t0; t < t1; ++t) acc += dy[t * D + i] * (x[t * D + i] * inv[t]);
+  part[(int64_t)c * D + i] = acc;
 }
 
 // out[i] += sum_{c < chunks} part[c, i] in chunk order (deterministic).
@@ -593,15 +603,15 @@ template <typename T>
 void rmsnorm_bwd(const float* dy, const float* x, const float* inv, const T* w,
                  const float* res, int64_t rows, int D, float* dx, T* dx_act, float* dw_accum,
                  float* part_buf, int64_t part_cap, cudaStream_t s, int64_t& launches) {
-  int threads = 256;
-  while (threads < 1024 && D > threads * 32) threads *= 2;
-  DOP_REQUIRE(D <= threads * 32, "dim too large for rmsnorm_bwd");
-  int64_t chunks = std::min<int64_t>(rows, (int64_t)sm_count() * 4);
+  k_rmsnorm_bwd_rows<T><<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(dy, x, inv, w, res, rows, D,
+                                                                     dx, dx_act);
+  DOP_LAUNCHED(launches);
+  int64_t chunks = std::max<int64_t>(1, std::min<int64_t>(rows, 64));
   int rows_per_chunk = (int)ceil_div(rows, chunks);
   chunks = ceil_div(rows, rows_per_chunk);
   DOP_REQUIRE(chunks * D <= part_cap, "partial buffer too small");
-  k_rmsnorm_bwd<T><<<(unsigned)chunks, threads, 0, s>>>(dy, x, inv, w, res, rows, D,
-                                                          rows_per_chunk, dx, dx_act, part_buf);
+  dim3 grid((unsigned)ceil_div(D, 128), (unsigned)chunks);
+  k_rmsnorm_dw_part<<<grid, 128, 0, s>>>(dy, x, inv, rows, D, rows_per_chunk, part_buf);
   DOP_LAUNCHED(launches);
   k_reduce_chunks<<<(unsigned)ceil_div(D, 256), 256, 0, s>>>(part_buf, (int)chunks, D, dw_accum);
   DOP_LAUNCHED(launches);

@@ -336,17 +336,28 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           } else if (p.epi == kSwiGLUBwd) {
             // v = dH; dG = dH * u * s (1 + g (1 - s)), dU = dH * g * s
-            const bf16* gi = p.g_in + m * p.ldg + n;
-            const bf16* ui = p.u_in + m * p.ldg + n;
-            bf16* dgo = p.dg_out + m * p.ldg + n;
-            bf16* duo = p.du_out + m * p.ldg + n;
-            for (int j = 0; j < 32 && n + j < p.N; ++j) {
-              float z = __bfloat162float(gi[j]);
-              float uu = __bfloat162float(ui[j]);
-              float sg = 1.0f / (1.0f + expf(-z));
-              float dsilu = sg * (1.0f + z * (1.0f - sg));
-              dgo[j] = __float2bfloat16_rn(v[j] * uu * dsilu);
-              duo[j] = __float2bfloat16_rn(v[j] * (z * sg));
+            // (N and ldg are multiples of 32 and 8: whole 16-byte vectors)
+            const uint4* gi = (const uint4*)(p.g_in + m * p.ldg + n);
+            const uint4* ui = (const uint4*)(p.u_in + m * p.ldg + n);
+            uint4* dgo = (uint4*)(p.dg_out + m * p.ldg + n);
+            uint4* duo = (uint4*)(p.du_out + m * p.ldg + n);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 g4 = gi[q], u4 = ui[q];
+              const __nv_bfloat162* g2 = (const __nv_bfloat162*)&g4;
+              const __nv_bfloat162* u2 = (const __nv_bfloat162*)&u4;
+              uint32_t rg[4], ru[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 z = __bfloat1622float2(g2[e]), uu = __bfloat1622float2(u2[e]);
+                const float s0 = 1.0f / (1.0f + __expf(-z.x)), s1 = 1.0f / (1.0f + __expf(-z.y));
+                const float d0 = v[8 * q + 2 * e], d1 = v[8 * q + 2 * e + 1];
+                rg[e] = pack_bf16(d0 * uu.x * (s0 * (1.0f + z.x * (1.0f - s0))),
+                                  d1 * uu.y * (s1 * (1.0f + z.y * (1.0f - s1))));
+                ru[e] = pack_bf16(d0 * (z.x * s0), d1 * (z.y * s1));
+              }
+              dgo[q] = make_uint4(rg[0], rg[1], rg[2], rg[3]);
+              duo[q] = make_uint4(ru[0], ru[1], ru[2], ru[3]);
             }
           } else {
             float* out = (float*)Cb + m * p.ldc + n;
