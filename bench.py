@@ -298,28 +298,59 @@ def run_ours(a):
         ms = t.item()
     value = world * T / (ms / 1e3)
 
-    # end to end through the public call: pinned host inputs in, dx out
+    # End to end through the public call: every step copies its x and dy from
+    # pinned host memory and reads its dx back.  The copies run on two copy
+    # streams and are double-buffered, so step i+1's inputs travel while step i
+    # computes and step i's dx returns during step i+1.
     e2e = None
     if not a.no_e2e:
         hx = torch.randn(T, cfg.dim, generator=torch.Generator().manual_seed(7)).pin_memory()
         hdy = torch.randn(T, cfg.dim, generator=torch.Generator().manual_seed(8)).pin_memory()
         hdx = torch.empty(T, cfg.dim).pin_memory()
+        Xb, DYb, DXb = [X, torch.empty_like(X)], [DY, torch.empty_like(DY)], [DX, torch.empty_like(DX)]
+        h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        ev = lambda: torch.cuda.Event()
+        in_ready, step_done, dx_out = [ev(), ev()], [ev(), ev()], [ev(), ev()]
 
-        def e2e_step():
-            X.copy_(hx, non_blocking=True)
-            DY.copy_(hdy, non_blocking=True)
-            step()
-            hdx.copy_(DX, non_blocking=True)
+        def e2e_run(n, start):
+            h2d.wait_event(start)
+            with torch.cuda.stream(h2d):
+                Xb[0].copy_(hx, non_blocking=True)
+                DYb[0].copy_(hdy, non_blocking=True)
+                in_ready[0].record(h2d)
+            for i in range(n):
+                b = i % 2
+                if i + 1 < n:  # prefetch step i+1 into the other buffer set
+                    with torch.cuda.stream(h2d):
+                        if i >= 1:
+                            h2d.wait_event(step_done[1 - b])
+                        Xb[1 - b].copy_(hx, non_blocking=True)
+                        DYb[1 - b].copy_(hdy, non_blocking=True)
+                        in_ready[1 - b].record(h2d)
+                stream.wait_event(in_ready[b])
+                if i >= 2:
+                    stream.wait_event(dx_out[b])
+                dP.zero_()
+                blk.forward(P, Xb[b], Y, stream=stream)
+                blk.backward(P, DYb[b], dP, DXb[b], stream=stream)
+                if world > 1:
+                    dist.all_reduce(dP)
+                step_done[b].record(stream)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(step_done[b])
+                    hdx.copy_(DXb[b], non_blocking=True)
+                    dx_out[b].record(d2h)
+            stream.wait_event(dx_out[(n - 1) % 2])
 
-        e2e_step()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        e2e_run(2, e0)  # warm-up of the copy path
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        n_e2e = max(1, min(a.steps, 5))
+        n_e2e = max(2, min(a.steps, 6))
         e0.record(stream)
-        for _ in range(n_e2e):
-            e2e_step()
+        e2e_run(n_e2e, e0)
         e1.record(stream)
         torch.cuda.synchronize(dev)
         ems = e0.elapsed_time(e1) / n_e2e
@@ -327,8 +358,9 @@ def run_ours(a):
             t = torch.tensor([ems], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ems = t.item()
-        e2e = {"value": world * T / (ems / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": 2 * T * cfg.dim * 4, "d2h_bytes_per_step": T * cfg.dim * 4}
+        e2e = {"value": world * T / (ems / 1e3), "unit": "tokens/s", "steps": n_e2e,
+               "h2d_bytes_per_step": 2 * T * cfg.dim * 4, "d2h_bytes_per_step": T * cfg.dim * 4,
+               "overlap": "double-buffered copy streams"}
 
     flops = flops_per_step(wl["cfg"], batch, seq)
     hbm, peak, peak_sus, src = measured_peaks()

@@ -47,47 +47,62 @@ __device__ __forceinline__ void st_tile_row32(uint8_t* tile, int r, int c0, cons
   }
 }
 
-__global__ void __launch_bounds__(192, 1)
+// Forward, one CTA per (256-query pair of tiles, head, sequence), 320
+// threads: warp 0 TMA, warp 1 MMA, warps 2-5 softmax of query tile A
+// (rows q0..q0+127), warps 6-9 softmax of tile B (q0+128..q0+255).
+// TMEM columns: S_A 0-127 (P_A packed bf16 in 0-63), S_B 128-255, O_A 256-383,
+// O_B 384-511.  O accumulates in TMEM (P V with accumulate); a row's running
+// max is only raised when the new max exceeds it by more than kRescale (log2
+// units), so O is rescaled in TMEM rarely.  The tensor core alternates
+// between the tiles: PV_A, S_A(next) run while B's softmax works and back.
+constexpr float kRescale = 8.0f;
+
+__global__ void __launch_bounds__(320, 1)
     k_attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                   const __grid_constant__ CUtensorMap mv, const FwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + TILE;          // 2 stages
-  uint8_t* sV = smem + 3 * TILE;      // 2 stages
-  uint8_t* sP = smem + 5 * TILE;
+  uint8_t* sQ = smem;                // tiles A and B
+  uint8_t* sK = smem + 2 * TILE;     // 2 stages
+  uint8_t* sV = smem + 4 * TILE;     // 2 stages
   uint64_t* bars = (uint64_t*)(smem + 6 * TILE);
-  uint32_t* tmem_slot = (uint32_t*)(bars + 14);
+  uint32_t* tmem_slot = (uint32_t*)(bars + 16);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   const uint32_t b0 = smem_u32(bars);
-  const uint32_t q_full = b0, p_full = b0 + 8, pv_full = b0 + 16, pv_free = b0 + 24;
-  auto kv_full = [&](int st) { return b0 + 32 + 8u * st; };
-  auto kv_empty = [&](int st) { return b0 + 48 + 8u * st; };
-  auto s_full = [&](int st) { return b0 + 64 + 8u * st; };
-  auto s_free = [&](int st) { return b0 + 80 + 8u * st; };
-  const uint32_t drain = b0 + 96;
+  const uint32_t q_full = b0, drain = b0 + 8;
+  auto kv_full = [&](int st) { return b0 + 16 + 8u * st; };
+  auto kv_empty = [&](int st) { return b0 + 32 + 8u * st; };
+  auto s_full = [&](int g) { return b0 + 48 + 8u * g; };
+  auto p_full = [&](int g) { return b0 + 64 + 8u * g; };
+  auto o_done = [&](int g) { return b0 + 80 + 8u * g; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = p.n_qt - 1 - (int)blockIdx.x;  // longest rows first
+  const int pt = p.n_qt - 1 - (int)blockIdx.x;  // longest rows first
   const int h = blockIdx.y, b = blockIdx.z, kvh = h / p.group;
-  const int q0 = qt * AT;
-  const int lo = max(0, q0 - p.window + 1);
-  const int hi = min(p.S - 1, q0 + AT - 1);
-  const int kt0 = lo / AT, nt = hi / AT - kt0 + 1;
-  const int row0 = b * p.S;  // token row of position 0 of this sequence
+  const int q0 = pt * 2 * AT;
+  const int row0 = b * p.S;
+  // key-tile ranges of the two query tiles (empty when the tile is past S)
+  int g_lo[2], g_hi[2];
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const int r0 = q0 + g * AT;
+    if (r0 >= p.S) { g_lo[g] = 1; g_hi[g] = 0; continue; }
+    g_lo[g] = max(0, r0 - p.window + 1) / AT;
+    g_hi[g] = min(p.S - 1, r0 + AT - 1) / AT;
+  }
+  const int u0 = g_lo[0];
+  const int u1 = max(g_hi[0], g_hi[1]);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(p_full, 4);
-    mbar_init(pv_full, 1);
-    mbar_init(pv_free, 4);
-    for (int st = 0; st < 2; ++st) {
-      mbar_init(kv_full(st), 1);
-      mbar_init(kv_empty(st), 1);
-      mbar_init(s_full(st), 1);
-      mbar_init(s_free(st), 4);
-    }
     mbar_init(drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(kv_full(i), 1);
+      mbar_init(kv_empty(i), 1);
+      mbar_init(s_full(i), 1);
+      mbar_init(p_full(i), 4);
+      mbar_init(o_done(i), 1);
+    }
     *abort_flag = 0;
     mbar_init_fence();
   }
@@ -103,15 +118,18 @@ __global__ void __launch_bounds__(192, 1)
       prefetch_map(&mk);
       prefetch_map(&mv);
       const uint32_t q_s = smem_u32(sQ);
-      mbar_expect_tx(q_full, TILE);
-      tma_load_3d(q_s, &mq, q_full, 0, h, row0 + q0);
-      tma_load_3d(q_s + HALF, &mq, q_full, 64, h, row0 + q0);
+      mbar_expect_tx(q_full, 2 * TILE);
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+        tma_load_3d(q_s + g * TILE, &mq, q_full, 0, h, row0 + q0 + g * AT);
+        tma_load_3d(q_s + g * TILE + HALF, &mq, q_full, 64, h, row0 + q0 + g * AT);
+      }
       int issued = 0;
       bool ok = true;
-      for (int j = 0; j < nt; ++j) {
-        const int st = j & 1;
+      for (int t = u0; t <= u1; ++t) {
+        const int j = t - u0, st = j & 1;
         if (!mbar_wait(kv_empty(st), ((j >> 1) & 1) ^ 1, abort_flag, 11)) { ok = false; break; }
-        const int k0 = (kt0 + j) * AT;
+        const int k0 = t * AT;
         const uint32_t ks = smem_u32(sK + st * TILE), vs = smem_u32(sV + st * TILE);
         mbar_expect_tx(kv_full(st), 2 * TILE);
         tma_load_3d(ks, &mk, kv_full(st), 0, kvh, row0 + k0);
@@ -128,134 +146,151 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t ID_S = idesc_bf16(128, 128, false, false);   // Q K^T
-      constexpr uint32_t ID_PV = idesc_bf16(128, 128, false, true);   // P V (V is N-major)
-      const uint32_t q_s = smem_u32(sQ), p_s = smem_u32(sP);
+      constexpr uint32_t ID_S = idesc_bf16(128, 128, false, false);  // Q K^T
+      constexpr uint32_t ID_PV = idesc_bf16(128, 128, false, true);  // P V (V N-major)
+      const uint32_t q_s = smem_u32(sQ);
       bool ok = mbar_wait(q_full, 0, abort_flag, 12);
-      auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(p_full, i & 1, abort_flag, 13)) return false;
-        if (!mbar_wait(pv_free, (i & 1) ^ 1, abort_flag, 14)) return false;
+      int nd0 = 0, nd1 = 0;     // tiles whose S was issued, per query tile
+      int pd0 = -1, pd1 = -1;   // tile whose P V is still to issue, per query tile
+      // P_g(tile) V(tile) into O_g; it must precede S_g(next), which
+      // overwrites P_g in TMEM (tcgen05 MMAs of one thread run in order)
+      auto issue_pv = [&](const int g, int& pend, const int nd, const int lo, const int hi) -> bool {
+        const int t = pend;
+        const int j = t - u0;
+        if (!mbar_wait(p_full(g), (nd - 1) & 1, abort_flag, 13 + g)) return false;
         tc_fence_after();
-        const uint32_t vs = smem_u32(sV + (i & 1) * TILE);
+        const uint32_t vs = smem_u32(sV + (j & 1) * TILE);
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + 256, kmajor_desc(p_s + (k >> 2) * HALF + (k & 3) * 32),
-                   mnmajor_desc(vs + k * 2048, HALF), ID_PV, k > 0);
-        mma_commit(pv_full);
-        mma_commit(kv_empty(i & 1));
+          mma_bf16_ts(tmem + 256 + g * 128, tmem + g * 128 + k * 8,
+                      mnmajor_desc(vs + k * 2048, HALF), ID_PV, (t > lo || k > 0) ? 1u : 0u);
+        pend = -1;
+        if (t == hi) mma_commit(o_done(g));
         return true;
       };
-      for (int j = 0; j < nt && ok; ++j) {
-        const int st = j & 1;
+      auto issue_s = [&](const int g, const uint32_t ks) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (k >> 2) * HALF + (k & 3) * 32;
+          mma_bf16(tmem + g * 128, kmajor_desc(q_s + g * TILE + off), kmajor_desc(ks + off), ID_S,
+                   k > 0);
+        }
+        mma_commit(s_full(g));
+      };
+      const int lo0 = g_lo[0], hi0 = g_hi[0], lo1 = g_lo[1], hi1 = g_hi[1];
+      for (int t = u0; t <= u1 && ok; ++t) {
+        const int j = t - u0, st = j & 1;
         if (!mbar_wait(kv_full(st), (j >> 1) & 1, abort_flag, 15)) { ok = false; break; }
-        if (!mbar_wait(s_free(st), ((j >> 1) & 1) ^ 1, abort_flag, 16)) { ok = false; break; }
         tc_fence_after();
         const uint32_t ks = smem_u32(sK + st * TILE);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + st * 128, kmajor_desc(q_s + (k >> 2) * HALF + (k & 3) * 32),
-                   kmajor_desc(ks + (k >> 2) * HALF + (k & 3) * 32), ID_S, k > 0);
-        mma_commit(s_full(st));
-        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+        if (pd0 >= 0 && !issue_pv(0, pd0, nd0, lo0, hi0)) { ok = false; break; }
+        if (t >= lo0 && t <= hi0) { issue_s(0, ks); ++nd0; pd0 = t; }
+        if (pd1 >= 0 && !issue_pv(1, pd1, nd1, lo1, hi1)) { ok = false; break; }
+        if (t >= lo1 && t <= hi1) { issue_s(1, ks); ++nd1; pd1 = t; }
+        // every P V that reads tile t-1 has been issued: release its stage
+        if (j >= 1) mma_commit(kv_empty((j - 1) & 1));
       }
-      if (ok) issue_pv(nt - 1);
+      if (ok && pd0 >= 0 && !issue_pv(0, pd0, nd0, lo0, hi0)) ok = false;
+      if (ok && pd1 >= 0 && !issue_pv(1, pd1, nd1, lo1, hi1)) ok = false;
       mma_commit(drain);
       mbar_wait_drain(drain, 0);
     }
   } else {
     // ---------------------------------------------------------- softmax
+    const int g = (warp - 2) >> 2;          // query tile of this warp group
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const int qi = q0 + r;
+    const int qi = q0 + g * AT + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    float o[HD];
-#pragma unroll
-    for (int i = 0; i < HD; ++i) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    const uint32_t ts = tmem + g * 128 + lane_off;        // S_g, then P_g
+    const uint32_t to = tmem + 256 + g * 128 + lane_off;  // O_g
+    float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < nt; ++j) {
-      const int st = j & 1;
-      if (!mbar_wait(s_full(st), (j >> 1) & 1, abort_flag, 17)) { ok = false; break; }
+    const int my_lo = g ? g_lo[1] : g_lo[0];
+    const int n = (g ? g_hi[1] : g_hi[0]) - my_lo + 1;
+    for (int it = 0; it < n; ++it) {
+      if (!mbar_wait(s_full(g), it & 1, abort_flag, 17 + g)) { ok = false; break; }
       tc_fence_after();
-      const int k0 = (kt0 + j) * AT;
+      const int k0 = (my_lo + it) * AT;
       const bool all_vis = (k0 + AT - 1 <= qi) && (qi - k0 < p.window);
-      const uint32_t ts = tmem + st * 128 + lane_off;
+      // pass 1: row max of the scaled, masked scores (S stays in TMEM)
       float mx = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(ts + c * 32, v);
+        float sv[32];
+        tmem_ld32(ts + c * 32, sv);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int key = k0 + c * 32 + i;
           const bool vis = all_vis || (key <= qi && qi - key < p.window);
-          mx = vis ? fmaxf(mx, v[i]) : mx;
+          mx = vis ? fmaxf(mx, sv[i] * p.sl2) : mx;
         }
       }
-      const float m_new = mx == -INFINITY ? m : fmaxf(m, mx * p.sl2);
-      const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_new);
-      // fold PV_{j-1} (it was computed against m_{j-1}) before P_j overwrites P
-      if (j > 0) {
-        if (!mbar_wait(pv_full, (j - 1) & 1, abort_flag, 18)) { ok = false; break; }
-        tc_fence_after();
+      if (mx > m + kRescale || (m == -INFINITY && mx > -INFINITY)) {
+        // raise the reference max; rescale O (already complete: S_g(it) was
+        // issued after P V of the previous tile) and the running sum
+        const float alpha = m == -INFINITY ? 0.f : fast_exp2(m - mx);
+        if (it > 0 && m != -INFINITY) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float ov[32];
+            tmem_ld32(to + c * 32, ov);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float pv[32];
-          tmem_ld32(tmem + 256 + lane_off + c * 32, pv);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha_prev + pv[i];
+            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+            tmem_st32(to + c * 32, ov);
+          }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(pv_free);
+        l *= alpha;
+        m = mx;
       }
       float sum = 0.f;
+      const bool none = m == -INFINITY;  // nothing visible yet in this row
+      // pass 2: P = 2^(s - m) as packed bf16 pairs over the S columns
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(ts + c * 32, v);
+      for (int hh = 0; hh < 2; ++hh) {
+        float sv[64];
+        tmem_ld32(ts + hh * 64, sv);
+        tmem_ld32(ts + hh * 64 + 32, sv + 32);
+        uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int key = k0 + c * 32 + i;
-          const bool vis = all_vis || (key <= qi && qi - key < p.window);
-          const float e = vis ? exp2f(v[i] * p.sl2 - m_new) : 0.f;
-          v[i] = e;
-          sum += e;
+          float e[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int key = k0 + hh * 64 + 2 * i + u;
+            const bool vis = !none && (all_vis || (key <= qi && qi - key < p.window));
+            e[u] = vis ? fast_exp2(sv[2 * i + u] * p.sl2 - m) : 0.f;
+          }
+          sum += e[0] + e[1];
+          pk[i] = pack_bf16(e[0], e[1]);
         }
-        st_tile_row32(sP, r, c * 32, v);
+        tmem_st32u(ts + hh * 32, pk);
       }
-      l = l * alpha + sum;
-      m = m_new;
-      alpha_prev = alpha;
+      l += sum;
+      tmem_st_wait();
       tc_fence_before();
-      fence_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(s_free(st));
-        mbar_arrive(p_full);
-      }
+      if (lane == 0) mbar_arrive(p_full(g));
     }
-    if (ok && mbar_wait(pv_full, (nt - 1) & 1, abort_flag, 19)) {
+    if (n > 0 && ok && mbar_wait(o_done(g), 0, abort_flag, 19)) {
       tc_fence_after();
-#pragma unroll
+      const float inv_l = 1.0f / l;
+#pragma unroll 1
       for (int c = 0; c < 4; ++c) {
-        float pv[32];
-        tmem_ld32(tmem + 256 + lane_off + c * 32, pv);
+        float ov[32];
+        tmem_ld32(to + c * 32, ov);
+        if (qi < p.S) {
+          uint4* dst = reinterpret_cast<uint4*>(p.o + ((int64_t)(row0 + qi) * p.H + h) * HD + c * 32);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha_prev + pv[i];
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_bf16(ov[8 * q] * inv_l, ov[8 * q + 1] * inv_l),
+                                pack_bf16(ov[8 * q + 2] * inv_l, ov[8 * q + 3] * inv_l),
+                                pack_bf16(ov[8 * q + 4] * inv_l, ov[8 * q + 5] * inv_l),
+                                pack_bf16(ov[8 * q + 6] * inv_l, ov[8 * q + 7] * inv_l));
+        }
       }
-      if (qi < p.S) {
-        const float inv_l = 1.0f / l;
-        uint4* dst = reinterpret_cast<uint4*>(p.o + ((int64_t)(row0 + qi) * p.H + h) * HD);
-#pragma unroll
-        for (int q = 0; q < HD / 8; ++q)
-          dst[q] = make_uint4(pack_bf16(o[8 * q] * inv_l, o[8 * q + 1] * inv_l),
-                              pack_bf16(o[8 * q + 2] * inv_l, o[8 * q + 3] * inv_l),
-                              pack_bf16(o[8 * q + 4] * inv_l, o[8 * q + 5] * inv_l),
-                              pack_bf16(o[8 * q + 6] * inv_l, o[8 * q + 7] * inv_l));
-        // natural-log LSE of the scaled scores: m is max(s * scale) * log2(e)
-        p.lse[((int64_t)b * p.H + h) * p.S + qi] = m / kLog2e + logf(l);
-      }
+      // natural-log LSE of the scaled scores (m is in log2 units)
+      if (qi < p.S) p.lse[((int64_t)b * p.H + h) * p.S + qi] = m / kLog2e + logf(l);
     }
   }
   tc_fence_before();
@@ -264,7 +299,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-constexpr size_t kFwdSmem = 6 * TILE + 1024 + 256;
+constexpr size_t kFwdSmem = 6 * TILE + 1024 + 256;  // Q x2, K x2, V x2
 
 // ------------------------------------------------------------------ backward
 // delta[b, h, i] = sum_d dO[i, d] O[i, d]  (= sum_j P_ij dA_ij of gqa_backward)
@@ -720,7 +755,7 @@ void attn_fwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, bf1
   FwdParams p;
   p.S = (int)a.S; p.H = a.H; p.KV = a.KV; p.group = a.H / a.KV;
   p.window = (int)std::min<int64_t>(a.window, a.S + 1);
-  p.n_qt = (int)ceil_div(a.S, AT);
+  p.n_qt = (int)ceil_div(a.S, 2 * AT);  // pairs of query tiles
   p.sl2 = a.scale * kLog2e;
   p.o = o;
   p.lse = lse;
@@ -731,7 +766,7 @@ void attn_fwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, bf1
     attr = true;
   }
   dim3 grid((unsigned)p.n_qt, (unsigned)a.H, (unsigned)a.B);
-  k_attn_fwd_tc<<<grid, 192, kFwdSmem, s>>>(mq, mk, mv, p);
+  k_attn_fwd_tc<<<grid, 320, kFwdSmem, s>>>(mq, mk, mv, p);
   DOP_LAUNCHED(launches);
 }
 
