@@ -226,6 +226,12 @@ def run_reference(a):
     }), flush=True)
 
 
+def _trace(msg):
+    if os.environ.get("DOP_BENCH_TRACE"):
+        sys.stderr.write(f"[bench {time.strftime('%H:%M:%S')}] {msg}\n")
+        sys.stderr.flush()
+
+
 def run_ours(a):
     import torch
     import torch.distributed as dist
@@ -266,9 +272,11 @@ def run_ours(a):
         if world > 1:
             dist.all_reduce(dP)
 
+    _trace("params and inputs ready")
     for _ in range(a.warmup):
         step()
     torch.cuda.synchronize(dev)
+    _trace("warm-up done")
     if world > 1:
         dist.barrier()
     blk.set_timing(True)
@@ -288,6 +296,7 @@ def run_ours(a):
     # inside it; read after the loop so the timed region has no host sync)
     for name, pms in blk.phase_times():
         phase_acc.setdefault(name, []).append(pms)
+    _trace("timed loop done")
     launches = blk.launches() - launches0
     blk.set_timing(False)
     clk_summary = clk.summary()
@@ -346,6 +355,7 @@ def run_ours(a):
         e0.record(stream)
         e2e_run(2, e0)  # warm-up of the copy path
         torch.cuda.synchronize(dev)
+        _trace("e2e warm-up done")
         if world > 1:
             dist.barrier()
         n_e2e = max(2, min(a.steps, 6))
@@ -371,6 +381,7 @@ def run_ours(a):
     achieved = gu_flops / (gu_ms / 1e3) / 1e12
     phases = {k: round(sum(v) / len(v), 3) for k, v in phase_acc.items()}
 
+    _trace("e2e done")
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         ts = cpu_oracle_sample(wl["cfg"], CPU_SAMPLE_SEQ, seed=0, repeats=1)

@@ -60,6 +60,7 @@ constexpr float kRescale = 8.0f;
 __global__ void __launch_bounds__(320, 1)
     k_attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                   const __grid_constant__ CUtensorMap mv, const FwdParams p) {
+  if (tc_failed()) return;  // an earlier wait failed: do nothing (sticky error)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sQ = smem;                // tiles A and B
@@ -344,6 +345,7 @@ __global__ void __launch_bounds__(192, 1)
     k_attn_dq_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                  const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
                  const BwdParams p) {
+  if (tc_failed()) return;  // an earlier wait failed: do nothing (sticky error)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sQ = smem;
@@ -522,6 +524,7 @@ __global__ void __launch_bounds__(192, 1)
     k_attn_dkdv_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
                    const BwdParams p) {
+  if (tc_failed()) return;  // an earlier wait failed: do nothing (sticky error)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sK = smem;

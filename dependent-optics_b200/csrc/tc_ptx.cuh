@@ -58,6 +58,11 @@ static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity
     if (mbar_try(bar, parity)) return true;
     if ((i & 127u) == 127u) {
       if (*abort_flag) return false;
+      // another CTA of this or an earlier launch already gave up: stop too
+      if (*(volatile int*)&g_tc_error) {
+        *abort_flag = 1;
+        return false;
+      }
       if (gtime_ns() - t0 > kWaitNs) break;
     }
   }
@@ -70,6 +75,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   if (mbar_try(bar, parity)) return true;
   return mbar_wait_slow(bar, parity, abort_flag, code);
 }
+// True when a tensor-core kernel has already recorded a failed wait in this
+// process; CTAs check it on entry and skip their work (the error is sticky and
+// reported by dop_device_status()).
+__device__ __forceinline__ bool tc_failed() { return *(volatile int*)&g_tc_error != 0; }
 // Bounded wait used while draining after an abort: no error bookkeeping.
 __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = gtime_ns();
