@@ -227,23 +227,26 @@ __global__ void __launch_bounds__(320, 1)
           mx = vis ? fmaxf(mx, sv[i] * p.sl2) : mx;
         }
       }
-      if (mx > m + kRescale || (m == -INFINITY && mx > -INFINITY)) {
-        // raise the reference max; rescale O (already complete: S_g(it) was
-        // issued after P V of the previous tile) and the running sum
-        const float alpha = m == -INFINITY ? 0.f : fast_exp2(m - mx);
-        if (it > 0 && m != -INFINITY) {
+      // Raise the reference max when it grew by more than kRescale.  The
+      // decision is per row, but the TMEM loads/stores that rescale O are
+      // warp-collective, so the warp rescales when any of its rows needs it
+      // (rows that do not keep alpha = 1).
+      const bool raise = mx > m + kRescale || (m == -INFINITY && mx > -INFINITY);
+      const float m_new = raise ? mx : m;
+      const float alpha = raise ? (m == -INFINITY ? 0.f : fast_exp2(m - m_new)) : 1.f;
+      if (it > 0 && __any_sync(0xffffffffu, raise && m != -INFINITY)) {
+        // O is complete: S_g(it) was issued after P V of the previous tile
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            float ov[32];
-            tmem_ld32(to + c * 32, ov);
+        for (int c = 0; c < 4; ++c) {
+          float ov[32];
+          tmem_ld32(to + c * 32, ov);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-            tmem_st32(to + c * 32, ov);
-          }
+          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+          tmem_st32(to + c * 32, ov);
         }
-        l *= alpha;
-        m = mx;
       }
+      l *= alpha;
+      m = m_new;
       float sum = 0.f;
       const bool none = m == -INFINITY;  // nothing visible yet in this row
       // pass 2: P = 2^(s - m) as packed bf16 pairs over the S columns
@@ -749,6 +752,7 @@ void attn_fwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, bf1
                  cudaStream_t s, int64_t& launches) {
   using namespace tc;
   check_tc(a);
+  bind_error_word();
   const int64_t T = a.B * a.S;
   const int64_t dq[3] = {HD, a.H, T}, sq[2] = {HD, (int64_t)a.H * HD};
   const int64_t dk[3] = {HD, a.KV, T}, sk[2] = {HD, (int64_t)a.KV * HD};
@@ -778,6 +782,7 @@ void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, con
                  cudaStream_t s, int64_t& launches) {
   using namespace tc;
   check_tc(a);
+  bind_error_word();
   const int64_t T = a.B * a.S;
   const int64_t rows = T * a.H;
   k_attn_delta_bf16<<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(o, dout, rows, a.H, (int)a.S, delta);
@@ -821,10 +826,6 @@ void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, con
   }
 }
 
-int attn_tc_error_status() {
-  int v = 0;
-  cudaMemcpyFromSymbol(&v, tc::g_tc_error, sizeof(int));
-  return v;
-}
+
 
 }  // namespace dop

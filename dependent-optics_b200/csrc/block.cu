@@ -4,6 +4,8 @@
 // backward = src/mixtral.rs:434-598 (backward_layer)
 // with the crate's per-token expert loop replaced by the deterministic
 // expert permutation and grouped GEMMs over the expert-sorted rows.
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "block.cuh"
@@ -147,6 +149,7 @@ Block::~Block() {
 }
 
 void Block::ph_begin(const char* name, cudaStream_t s) {
+  cur_phase = name;
   if (!timing) return;
   if (n_phases == phases.size()) {
     Phase p{name, nullptr, nullptr};
@@ -159,6 +162,13 @@ void Block::ph_begin(const char* name, cudaStream_t s) {
 }
 
 void Block::ph_end(cudaStream_t s) {
+  // DOP_DEBUG_SYNC=1: synchronise after every phase and report it on stderr
+  static const bool debug_sync = getenv("DOP_DEBUG_SYNC") != nullptr;
+  if (debug_sync) {
+    cudaError_t e = cudaStreamSynchronize(s);
+    fprintf(stderr, "[dop] phase %s done: %s, tensor-core status %d\n", cur_phase,
+            cudaGetErrorString(e), tc_error_status());
+  }
   if (!timing) return;
   DOP_CHECK_CUDA(cudaEventRecord(phases[n_phases].b, s));
   ++n_phases;

@@ -48,6 +48,7 @@ struct Block {
   bool timing = false;
   std::vector<Phase> phases;
   size_t n_phases = 0, n_fwd_phases = 0;
+  const char* cur_phase = "";
   void ph_begin(const char* name, cudaStream_t s);
   void ph_end(cudaStream_t s);
 

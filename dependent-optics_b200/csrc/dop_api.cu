@@ -35,11 +35,6 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 }  // namespace
 
 namespace dop {
-int tc_error_status() {
-  int e = gemm_tc_error_status();
-  return e ? e : attn_tc_error_status();
-}
-
 int sm_count() {
   static int cached[16] = {0};
   int dev = 0;

@@ -458,6 +458,7 @@ void launch(const CUtensorMap* ma, const CUtensorMap* mb, const Params& p, int g
             cudaStream_t s) {
   constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
   auto kern = k_gemm_tc<A_MN, B_MN, BN, DUAL>;
+  bind_error_word();
   static bool attr = false;
   if (!attr) {
     DOP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -556,9 +557,24 @@ void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue
   DOP_LAUNCHED(launches);
 }
 
-int gemm_tc_error_status() {
+int* tc_error_word() {
+  static int* words[16] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  DOP_CHECK_CUDA(cudaGetDevice(&dev));
+  DOP_REQUIRE(dev >= 0 && dev < 16, "device index out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!words[dev]) {
+    DOP_CHECK_CUDA(cudaMalloc(&words[dev], sizeof(int)));
+    DOP_CHECK_CUDA(cudaMemset(words[dev], 0, sizeof(int)));
+  }
+  return words[dev];
+}
+
+int tc_error_status() {
   int v = 0;
-  cudaMemcpyFromSymbol(&v, tc::g_tc_error, sizeof(int));
+  int* w = tc_error_word();
+  if (cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
   return v;
 }
 

@@ -126,8 +126,6 @@ CUtensorMap make_map3(const void* base, const int64_t dims[3], const int64_t str
                       const int box[3]);
 // First bounded-wait failure recorded by a tensor-core kernel (0 = none).
 int tc_error_status();
-int gemm_tc_error_status();
-int attn_tc_error_status();
 
 // ------------------------------------------------------------ attention
 // Sliding-window causal grouped-query attention (src/mixtral.rs:799-922),

@@ -2,8 +2,10 @@
 // mbarriers with bounded waits, TMA tile loads, tcgen05 MMA / commit / TMEM
 // loads and fences, and the shared-memory matrix descriptor.
 //
-// Include once per translation unit: each unit gets its own error word
-// (g_tc_error), which records the first bounded wait that ran out.
+// Every tensor-core kernel shares one process-wide error word per device
+// (tc_error_word(), bound to each translation unit's g_err before its first
+// launch): the first bounded wait that runs out records its code there, and
+// every CTA that sees it set skips its work.
 #pragma once
 
 #include <cuda.h>
@@ -11,13 +13,16 @@
 #include "common.cuh"
 
 namespace dop {
+// Process-wide error word of the current device (allocated and zeroed once).
+int* tc_error_word();
 namespace tc {
 
 namespace {
-__device__ int g_tc_error;  // first bounded-wait failure seen by any CTA (0 = none)
+__device__ int* g_err;  // -> the process-wide error word of this device
 }
 
-constexpr uint64_t kWaitNs = 4000000000ull;  // 4 s of device time per wait
+constexpr uint64_t kWaitNs = 4000000000ull;   // 4 s of device time per wait
+constexpr uint64_t kDrainNs = 200000000ull;   // 0.2 s per wait while draining
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -59,14 +64,14 @@ static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity
     if ((i & 127u) == 127u) {
       if (*abort_flag) return false;
       // another CTA of this or an earlier launch already gave up: stop too
-      if (*(volatile int*)&g_tc_error) {
+      if (*(volatile int*)g_err) {
         *abort_flag = 1;
         return false;
       }
       if (gtime_ns() - t0 > kWaitNs) break;
     }
   }
-  atomicCAS(&g_tc_error, 0, code);
+  atomicCAS(g_err, 0, code);
   *abort_flag = 1;
   return false;
 }
@@ -78,11 +83,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 // True when a tensor-core kernel has already recorded a failed wait in this
 // process; CTAs check it on entry and skip their work (the error is sticky and
 // reported by dop_device_status()).
-__device__ __forceinline__ bool tc_failed() { return *(volatile int*)&g_tc_error != 0; }
+__device__ __forceinline__ bool tc_failed() { return *(volatile int*)g_err != 0; }
 // Bounded wait used while draining after an abort: no error bookkeeping.
 __device__ __forceinline__ void mbar_wait_drain(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = gtime_ns();
-  while (!mbar_try(bar, parity) && gtime_ns() - t0 < kWaitNs) {}
+  while (!mbar_try(bar, parity) && gtime_ns() - t0 < kDrainNs) {}
 }
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int c0, int c1, int c2) {
@@ -218,6 +223,18 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t addr, uint32_t atom_st
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Point this translation unit's g_err at the device's error word (once per
+// device; call before the first launch of a kernel of this unit).
+static inline void bind_error_word() {
+  static int bound[16] = {0};
+  int dev = 0;
+  DOP_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 16 || bound[dev]) return;
+  int* w = tc_error_word();
+  DOP_CHECK_CUDA(cudaMemcpyToSymbol(g_err, &w, sizeof(w)));
+  bound[dev] = 1;
 }
 
 }  // namespace tc

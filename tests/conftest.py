@@ -18,3 +18,18 @@ def cuda():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda:0")
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean(request):
+    """After every GPU test: no tensor-core kernel recorded a failed bounded
+    wait (dop_device_status)."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    from dop._lib import lib
+    torch.cuda.synchronize()
+    assert lib().dop_device_status() == 0, "a tensor-core kernel gave up waiting"

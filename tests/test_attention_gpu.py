@@ -29,13 +29,16 @@ def rel(a, b):
     return ((a.double() - b.double()).abs().max() / b.double().abs().max()).item()
 
 
-@pytest.mark.parametrize("B,S,H,KV,W", [(2, 200, 4, 2, 150), (1, 256, 2, 2, 10_000),
-                                         (1, 384, 8, 2, 100), (2, 130, 4, 1, 64)],
-                         ids=["ragged-window", "causal", "gqa4", "mqa"])
-def test_gqa_tensor_core_matches_float64(cuda, B, S, H, KV, W):
+@pytest.mark.parametrize("B,S,H,KV,W,qs", [(2, 200, 4, 2, 150, 1.0), (1, 256, 2, 2, 10_000, 1.0),
+                                            (1, 384, 8, 2, 100, 1.0), (2, 130, 4, 1, 64, 1.0),
+                                            (1, 1024, 4, 2, 10_000, 3.0)],
+                         ids=["ragged-window", "causal", "gqa4", "mqa", "wide-scores"])
+def test_gqa_tensor_core_matches_float64(cuda, B, S, H, KV, W, qs):
+    """qs scales q: wide score distributions make rows of one warp raise
+    their running max at different key tiles (the divergent O rescale)."""
     hd = 128
     g = torch.Generator(device="cuda").manual_seed(S + H)
-    q = torch.randn(B * S, H, hd, generator=g, device="cuda").bfloat16()
+    q = (qs * torch.randn(B * S, H, hd, generator=g, device="cuda")).bfloat16()
     k = torch.randn(B * S, KV, hd, generator=g, device="cuda").bfloat16()
     v = torch.randn(B * S, KV, hd, generator=g, device="cuda").bfloat16()
     dout = torch.randn(B * S, H, hd, generator=g, device="cuda").bfloat16()
