@@ -341,51 +341,62 @@ struct BwdParams {
   float* dv;
 };
 
-// dQ: one CTA per (128-query tile, head, sequence).  Per key tile j:
-// S = Q K_j^T, dP = dO V_j^T (TMEM), dS = P (dP - delta) scale (bf16, smem),
-// dQ += dS K_j (TMEM accumulator across all key tiles).
-__global__ void __launch_bounds__(192, 1)
+// Backward kernels.  Both use 320 threads: warp 0 TMA, warp 1 MMA, warps
+// 2-5 and 6-9 two elementwise groups that take alternate tiles, so one
+// group's exp/shuffle work overlaps the other group's MMAs.  The bf16
+// operands the elementwise groups produce (dS, P^T, dS^T) are written back
+// into the TMEM columns they were computed from and read from there as the
+// A operand of the next MMA.
+constexpr int QB = 64;               // queries per dK/dV tile, keys per dQ tile
+constexpr uint32_t QHALF = 8192;     // [64 rows][64 cols] bf16 box
+constexpr uint32_t QTILE = 2 * QHALF;
+constexpr int BSTAGES = 4;
+
+// dQ: one CTA per (128-query tile, head, sequence), 64-key tiles.
+// TMEM: dQ 0-127; group g: S_g 128+128g (dS_g packed in its first 32
+// columns), dP_g 192+128g.  Per key tile j (group j & 1):
+// S = Q K_j^T, dP = dO V_j^T, dS = P (dP - delta) scale, dQ += dS K_j.
+__global__ void __launch_bounds__(320, 1)
     k_attn_dq_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                  const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
                  const BwdParams p) {
-  if (tc_failed()) return;  // an earlier wait failed: do nothing (sticky error)
+  if (tc_failed()) return;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sQ = smem;
   uint8_t* sDO = smem + TILE;
-  uint8_t* sK = smem + 2 * TILE;  // 2 stages
-  uint8_t* sV = smem + 4 * TILE;  // 2 stages
-  uint8_t* sDS = smem + 6 * TILE;
-  uint64_t* bars = (uint64_t*)(smem + 7 * TILE);
-  uint32_t* tmem_slot = (uint32_t*)(bars + 12);
+  uint8_t* sK = smem + 2 * TILE;              // BSTAGES x [64 keys][128 d]
+  uint8_t* sV = sK + BSTAGES * QTILE;
+  uint64_t* bars = (uint64_t*)(sV + BSTAGES * QTILE);
+  uint32_t* tmem_slot = (uint32_t*)(bars + 16);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   const uint32_t b0 = smem_u32(bars);
-  const uint32_t q_full = b0, sd_full = b0 + 8, sd_free = b0 + 16, ds_full = b0 + 24,
-                 ds_free = b0 + 32, drain = b0 + 40;
-  auto kv_full = [&](int st) { return b0 + 48 + 8u * st; };
-  auto kv_empty = [&](int st) { return b0 + 64 + 8u * st; };
-  const uint32_t dq_done = b0 + 80;
+  const uint32_t q_full = b0, dq_done = b0 + 8, drain = b0 + 16;
+  auto kv_full = [&](int st) { return b0 + 24 + 8u * st; };
+  auto kv_empty = [&](int st) { return b0 + 56 + 8u * st; };
+  auto sd_full = [&](int g) { return b0 + 88 + 8u * g; };
+  auto ds_full = [&](int g) { return b0 + 104 + 8u * g; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = p.n_tiles - 1 - (int)blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z, kvh = h / p.group;
   const int q0 = qt * AT;
-  const int lo = max(0, q0 - p.window + 1);
-  const int hi = min(p.S - 1, q0 + AT - 1);
-  const int kt0 = lo / AT, nt = hi / AT - kt0 + 1;
+  const int lo = max(0, q0 - p.window + 1) / QB;
+  const int hi = min(p.S - 1, q0 + AT - 1) / QB;
+  const int nt = hi - lo + 1;
   const int row0 = b * p.S;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(sd_full, 1);
-    mbar_init(sd_free, 4);
-    mbar_init(ds_full, 4);
-    mbar_init(ds_free, 1);
-    mbar_init(drain, 1);
     mbar_init(dq_done, 1);
-    for (int st = 0; st < 2; ++st) {
+    mbar_init(drain, 1);
+    for (int st = 0; st < BSTAGES; ++st) {
       mbar_init(kv_full(st), 1);
       mbar_init(kv_empty(st), 1);
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(sd_full(g), 1);
+      mbar_init(ds_full(g), 4);
     }
     *abort_flag = 0;
     mbar_init_fence();
@@ -407,98 +418,111 @@ __global__ void __launch_bounds__(192, 1)
       int issued = 0;
       bool ok = true;
       for (int j = 0; j < nt; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(kv_empty(st), ((j >> 1) & 1) ^ 1, abort_flag, 21)) { ok = false; break; }
-        const int k0 = (kt0 + j) * AT;
-        const uint32_t ks = smem_u32(sK + st * TILE), vs = smem_u32(sV + st * TILE);
-        mbar_expect_tx(kv_full(st), 2 * TILE);
+        const int st = j % BSTAGES;
+        if (!mbar_wait(kv_empty(st), ((j / BSTAGES) & 1) ^ 1, abort_flag, 21)) { ok = false; break; }
+        const int k0 = (lo + j) * QB;
+        const uint32_t ks = smem_u32(sK + st * QTILE), vs = smem_u32(sV + st * QTILE);
+        mbar_expect_tx(kv_full(st), 2 * QTILE);
         tma_load_3d(ks, &mk, kv_full(st), 0, kvh, row0 + k0);
-        tma_load_3d(ks + HALF, &mk, kv_full(st), 64, kvh, row0 + k0);
+        tma_load_3d(ks + QHALF, &mk, kv_full(st), 64, kvh, row0 + k0);
         tma_load_3d(vs, &mv, kv_full(st), 0, kvh, row0 + k0);
-        tma_load_3d(vs + HALF, &mv, kv_full(st), 64, kvh, row0 + k0);
+        tma_load_3d(vs + QHALF, &mv, kv_full(st), 64, kvh, row0 + k0);
         ++issued;
       }
       if (!ok) {
         mbar_wait_drain(q_full, 0);
-        for (int j = issued - 1; j >= 0 && j >= issued - 2; --j)
-          mbar_wait_drain(kv_full(j & 1), (j >> 1) & 1);
+        for (int j = issued - 1; j >= 0 && j >= issued - BSTAGES; --j)
+          mbar_wait_drain(kv_full(j % BSTAGES), (j / BSTAGES) & 1);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t ID_SD = idesc_bf16(128, 128, false, false);  // Q K^T and dO V^T
-      constexpr uint32_t ID_DQ = idesc_bf16(128, 128, false, true);   // dS K (K is N-major)
-      const uint32_t qs = smem_u32(sQ), dos = smem_u32(sDO), dss = smem_u32(sDS);
+      constexpr uint32_t ID_SD = idesc_bf16(128, 64, false, false);   // Q K^T, dO V^T
+      constexpr uint32_t ID_DQ = idesc_bf16(128, 128, false, true);   // dS K (K N-major)
+      const uint32_t qs = smem_u32(sQ), dos = smem_u32(sDO);
       bool ok = mbar_wait(q_full, 0, abort_flag, 22);
-      for (int j = 0; j < nt && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(kv_full(st), (j >> 1) & 1, abort_flag, 23)) { ok = false; break; }
-        if (!mbar_wait(sd_free, (j & 1) ^ 1, abort_flag, 24)) { ok = false; break; }
+      // dQ += dS_i K_i (dS from TMEM); it precedes S of tile i+2, which
+      // overwrites dS_i's columns
+      auto issue_dq = [&](int i) -> bool {
+        const int gi = i & 1;
+        if (!mbar_wait(ds_full(gi), (i >> 1) & 1, abort_flag, 23)) return false;
         tc_fence_after();
-        const uint32_t ks = smem_u32(sK + st * TILE), vs = smem_u32(sV + st * TILE);
+        const uint32_t ks = smem_u32(sK + (i % BSTAGES) * QTILE);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_bf16_ts(tmem, tmem + 128 + gi * 128 + k * 8, mnmajor_desc(ks + k * 2048, QHALF),
+                      ID_DQ, (i > 0 || k > 0) ? 1u : 0u);
+        mma_commit(kv_empty(i % BSTAGES));
+        return true;
+      };
+      for (int j = 0; j < nt && ok; ++j) {
+        const int g = j & 1, st = j % BSTAGES;
+        if (!mbar_wait(kv_full(st), (j / BSTAGES) & 1, abort_flag, 24)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ks = smem_u32(sK + st * QTILE), vs = smem_u32(sV + st * QTILE);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const uint32_t off = (k >> 2) * HALF + (k & 3) * 32;
-          mma_bf16(tmem, kmajor_desc(qs + off), kmajor_desc(ks + off), ID_SD, k > 0);
-          mma_bf16(tmem + 128, kmajor_desc(dos + off), kmajor_desc(vs + off), ID_SD, k > 0);
+          const uint32_t oa = (k >> 2) * HALF + (k & 3) * 32;
+          const uint32_t ob = (k >> 2) * QHALF + (k & 3) * 32;
+          mma_bf16(tmem + 128 + g * 128, kmajor_desc(qs + oa), kmajor_desc(ks + ob), ID_SD, k > 0);
+          mma_bf16(tmem + 192 + g * 128, kmajor_desc(dos + oa), kmajor_desc(vs + ob), ID_SD, k > 0);
         }
-        mma_commit(sd_full);
-        if (!mbar_wait(ds_full, j & 1, abort_flag, 25)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + 256, kmajor_desc(dss + (k >> 2) * HALF + (k & 3) * 32),
-                   mnmajor_desc(ks + k * 2048, HALF), ID_DQ, (j > 0 || k > 0) ? 1u : 0u);
-        mma_commit(ds_free);
-        mma_commit(kv_empty(st));
+        mma_commit(sd_full(g));
+        if (j >= 1 && !issue_dq(j - 1)) { ok = false; break; }
       }
-      if (ok) mma_commit(dq_done);
+      if (ok && issue_dq(nt - 1)) mma_commit(dq_done);
       mma_commit(drain);
       mbar_wait_drain(drain, 0);
     }
   } else {
+    const int g = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const int qi = q0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t ts = tmem + 128 + g * 128 + lane_off;  // S_g, then dS_g
+    const uint32_t td = tmem + 192 + g * 128 + lane_off;  // dP_g
     const bool row_ok = qi < p.S;
     const float lse2 = row_ok ? p.lse[((int64_t)b * p.H + h) * p.S + qi] * kLog2e : 0.f;
     const float dlt = row_ok ? p.delta[((int64_t)b * p.H + h) * p.S + qi] : 0.f;
     bool ok = true;
-    for (int j = 0; j < nt; ++j) {
-      if (!mbar_wait(sd_full, j & 1, abort_flag, 26)) { ok = false; break; }
-      if (j > 0 && !mbar_wait(ds_free, (j - 1) & 1, abort_flag, 27)) { ok = false; break; }
+    int cnt = 0;
+    for (int j = g; j < nt; j += 2, ++cnt) {
+      if (!mbar_wait(sd_full(g), cnt & 1, abort_flag, 26)) { ok = false; break; }
       tc_fence_after();
-      const int k0 = (kt0 + j) * AT;
-      const bool all_vis = (k0 + AT - 1 <= qi) && (qi - k0 < p.window);
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float sv[32], dp[32];
-        tmem_ld32(tmem + lane_off + c * 32, sv);
-        tmem_ld32(tmem + 128 + lane_off + c * 32, dp);
+      const int k0 = (lo + j) * QB;
+      const bool all_vis = (k0 + QB - 1 <= qi) && (qi - k0 < p.window);
+      uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = k0 + c * 32 + i;
-          const bool vis = row_ok && (all_vis || (key <= qi && qi - key < p.window));
-          const float pr = vis ? exp2f(sv[i] * p.sl2 - lse2) : 0.f;
-          sv[i] = pr * (dp[i] - dlt) * p.scale;
+      for (int hh = 0; hh < 2; ++hh) {
+        float sv[32], dp[32];
+        tmem_ld32(ts + hh * 32, sv);
+        tmem_ld32(td + hh * 32, dp);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float e[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int key = k0 + hh * 32 + 2 * i + u;
+            const bool vis = row_ok && (all_vis || (key <= qi && qi - key < p.window));
+            const float pr = vis ? fast_exp2(sv[2 * i + u] * p.sl2 - lse2) : 0.f;
+            e[u] = pr * (dp[2 * i + u] - dlt) * p.scale;
+          }
+          pk[hh * 16 + i] = pack_bf16(e[0], e[1]);
         }
-        st_tile_row32(sDS, r, c * 32, sv);
       }
+      tmem_st32u(ts, pk);
+      tmem_st_wait();
       tc_fence_before();
-      fence_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(sd_free);
-        mbar_arrive(ds_full);
-      }
+      if (lane == 0) mbar_arrive(ds_full(g));
     }
-    if (ok && mbar_wait(dq_done, 0, abort_flag, 28)) {
+    if (g == 0 && ok && mbar_wait(dq_done, 0, abort_flag, 28)) {
       tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float v[32];
-        tmem_ld32(tmem + 256 + lane_off + c * 32, v);
+        tmem_ld32(tmem + lane_off + c * 32, v);
         if (row_ok) {
           float4* dst = reinterpret_cast<float4*>(p.dq + ((int64_t)(row0 + qi) * p.H + h) * HD + c * 32);
 #pragma unroll
@@ -513,62 +537,55 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-constexpr size_t kDqSmem = 7 * TILE + 1024 + 256;
+constexpr size_t kDqSmem = 2 * TILE + 2 * BSTAGES * QTILE + 1024 + 256;
 
 // dK, dV: one CTA per (128-key tile, kv head, sequence), looping over the
-// query heads of the group and the 64-query tiles that see the keys:
-// S^T = K Q^T, dP^T = V dO^T (TMEM, double-buffered), P^T and
-// dS^T = P^T (dP^T - delta) scale (bf16, smem), dV += P^T dO, dK += dS^T Q.
-constexpr int QB = 64;               // queries per tile
-constexpr uint32_t QHALF = 8192;     // [64 rows][64 cols] bf16 box
-constexpr uint32_t QTILE = 2 * QHALF;
-
-__global__ void __launch_bounds__(192, 1)
+// query heads of the group and the 64-query tiles that see the keys (tile i
+// to group i & 1).  TMEM: dV 0-127, dK 128-255; group g: S^T_g 256+128g
+// (P^T packed in its first 32 columns), dP^T_g 320+128g (dS^T packed).
+// S^T = K Q^T, dP^T = V dO^T, dV += P^T dO, dK += dS^T Q.
+__global__ void __launch_bounds__(320, 1)
     k_attn_dkdv_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
                    const BwdParams p) {
-  if (tc_failed()) return;  // an earlier wait failed: do nothing (sticky error)
+  if (tc_failed()) return;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sK = smem;
   uint8_t* sV = smem + TILE;
-  uint8_t* sQ = smem + 2 * TILE;                // 2 stages of QTILE
-  uint8_t* sDO = sQ + 2 * QTILE;                // 2 stages of QTILE
-  uint8_t* sPT = sDO + 2 * QTILE;               // [128 keys][64 q] one atom
-  uint8_t* sDST = sPT + 16384;
-  float* sLD = (float*)(sDST + 16384);          // [4 warps][lse2 64 | delta 64]
-  uint64_t* bars = (uint64_t*)(sLD + 512);
+  uint8_t* sQ = smem + 2 * TILE;                // BSTAGES x [64 q][128 d]
+  uint8_t* sDO = sQ + BSTAGES * QTILE;
+  float* sLD = (float*)(sDO + BSTAGES * QTILE); // [8 warps][lse2 64 | delta 64]
+  uint64_t* bars = (uint64_t*)(sLD + 8 * 128);
   uint32_t* tmem_slot = (uint32_t*)(bars + 16);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   const uint32_t b0 = smem_u32(bars);
-  const uint32_t kv_full = b0, pd_full = b0 + 8, pd_free = b0 + 16, drain = b0 + 24,
-                 acc_done = b0 + 32;
-  auto q_full = [&](int st) { return b0 + 40 + 8u * st; };
+  const uint32_t kv_full = b0, acc_done = b0 + 8, drain = b0 + 16;
+  auto q_full = [&](int st) { return b0 + 24 + 8u * st; };
   auto q_empty = [&](int st) { return b0 + 56 + 8u * st; };
-  auto s_full = [&](int st) { return b0 + 72 + 8u * st; };
-  auto s_free = [&](int st) { return b0 + 88 + 8u * st; };
+  auto sd_full = [&](int g) { return b0 + 88 + 8u * g; };
+  auto pd_full = [&](int g) { return b0 + 104 + 8u * g; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = (int)blockIdx.x;
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int k0 = kt * AT;
-  const int qlo = k0;
   const int qhi = min(p.S - 1, k0 + AT - 1 + p.window - 1);
-  const int qt0 = qlo / QB, nq = qhi / QB - qt0 + 1;
+  const int qt0 = k0 / QB, nq = qhi / QB - qt0 + 1;
   const int total = nq * p.group;  // (head, query tile) pairs, head-major
   const int row0 = b * p.S;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(pd_full, 4);
-    mbar_init(pd_free, 1);
-    mbar_init(drain, 1);
     mbar_init(acc_done, 1);
-    for (int st = 0; st < 2; ++st) {
+    mbar_init(drain, 1);
+    for (int st = 0; st < BSTAGES; ++st) {
       mbar_init(q_full(st), 1);
       mbar_init(q_empty(st), 1);
-      mbar_init(s_full(st), 1);
-      mbar_init(s_free(st), 4);
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(sd_full(g), 1);
+      mbar_init(pd_full(g), 4);
     }
     *abort_flag = 0;
     mbar_init_fence();
@@ -590,10 +607,10 @@ __global__ void __launch_bounds__(192, 1)
       int issued = 0;
       bool ok = true;
       for (int i = 0; i < total; ++i) {
-        const int st = i & 1;
+        const int st = i % BSTAGES;
         const int h = kvh * p.group + i / nq;
         const int qq0 = (qt0 + i % nq) * QB;
-        if (!mbar_wait(q_empty(st), ((i >> 1) & 1) ^ 1, abort_flag, 31)) { ok = false; break; }
+        if (!mbar_wait(q_empty(st), ((i / BSTAGES) & 1) ^ 1, abort_flag, 31)) { ok = false; break; }
         const uint32_t qs = smem_u32(sQ + st * QTILE), dos = smem_u32(sDO + st * QTILE);
         mbar_expect_tx(q_full(st), 2 * QTILE);
         tma_load_3d(qs, &mq, q_full(st), 0, h, row0 + qq0);
@@ -604,8 +621,8 @@ __global__ void __launch_bounds__(192, 1)
       }
       if (!ok) {
         mbar_wait_drain(kv_full, 0);
-        for (int i = issued - 1; i >= 0 && i >= issued - 2; --i)
-          mbar_wait_drain(q_full(i & 1), (i >> 1) & 1);
+        for (int i = issued - 1; i >= 0 && i >= issued - BSTAGES; --i)
+          mbar_wait_drain(q_full(i % BSTAGES), (i / BSTAGES) & 1);
       }
     }
   } else if (warp == 1) {
@@ -613,57 +630,57 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t ID_ST = idesc_bf16(128, 64, false, false);   // K Q^T, V dO^T
       constexpr uint32_t ID_ACC = idesc_bf16(128, 128, false, true);  // P^T dO, dS^T Q
       const uint32_t ks = smem_u32(sK), vs = smem_u32(sV);
-      const uint32_t pts = smem_u32(sPT), dsts = smem_u32(sDST);
       bool ok = mbar_wait(kv_full, 0, abort_flag, 32);
       auto issue_acc = [&](int i) -> bool {
-        if (!mbar_wait(pd_full, i & 1, abort_flag, 33)) return false;
+        const int gi = i & 1, st = i % BSTAGES;
+        if (!mbar_wait(pd_full(gi), (i >> 1) & 1, abort_flag, 33)) return false;
         tc_fence_after();
-        const int st = i & 1;
         const uint32_t qs = smem_u32(sQ + st * QTILE), dos = smem_u32(sDO + st * QTILE);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-          mma_bf16(tmem + 256, kmajor_desc(pts + k * 32), mnmajor_desc(dos + k * 2048, QHALF),
-                   ID_ACC, acc);
-          mma_bf16(tmem + 384, kmajor_desc(dsts + k * 32), mnmajor_desc(qs + k * 2048, QHALF),
-                   ID_ACC, acc);
+          mma_bf16_ts(tmem, tmem + 256 + gi * 128 + k * 8, mnmajor_desc(dos + k * 2048, QHALF),
+                      ID_ACC, acc);
+          mma_bf16_ts(tmem + 128, tmem + 320 + gi * 128 + k * 8, mnmajor_desc(qs + k * 2048, QHALF),
+                      ID_ACC, acc);
         }
-        mma_commit(pd_free);
         mma_commit(q_empty(st));
         return true;
       };
       for (int i = 0; i < total && ok; ++i) {
-        const int st = i & 1;
-        if (!mbar_wait(q_full(st), (i >> 1) & 1, abort_flag, 34)) { ok = false; break; }
-        if (!mbar_wait(s_free(st), ((i >> 1) & 1) ^ 1, abort_flag, 35)) { ok = false; break; }
+        const int g = i & 1, st = i % BSTAGES;
+        if (!mbar_wait(q_full(st), (i / BSTAGES) & 1, abort_flag, 34)) { ok = false; break; }
         tc_fence_after();
         const uint32_t qs = smem_u32(sQ + st * QTILE), dos = smem_u32(sDO + st * QTILE);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t ka = (k >> 2) * HALF + (k & 3) * 32;   // K/V: two 16 KB d-boxes
           const uint32_t kb = (k >> 2) * QHALF + (k & 3) * 32;  // Q/dO: two 8 KB d-boxes
-          mma_bf16(tmem + st * 128, kmajor_desc(ks + ka), kmajor_desc(qs + kb), ID_ST, k > 0);
-          mma_bf16(tmem + st * 128 + 64, kmajor_desc(vs + ka), kmajor_desc(dos + kb), ID_ST, k > 0);
+          mma_bf16(tmem + 256 + g * 128, kmajor_desc(ks + ka), kmajor_desc(qs + kb), ID_ST, k > 0);
+          mma_bf16(tmem + 320 + g * 128, kmajor_desc(vs + ka), kmajor_desc(dos + kb), ID_ST, k > 0);
         }
-        mma_commit(s_full(st));
-        if (i > 0 && !issue_acc(i - 1)) { ok = false; break; }
+        mma_commit(sd_full(g));
+        if (i >= 1 && !issue_acc(i - 1)) { ok = false; break; }
       }
       if (ok && issue_acc(total - 1)) mma_commit(acc_done);
       mma_commit(drain);
       mbar_wait_drain(drain, 0);
     }
   } else {
+    const int g = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;   // key row of this thread
     const int kj = k0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t tsv = tmem + 256 + g * 128 + lane_off;  // S^T_g, then P^T_g
+    const uint32_t tdp = tmem + 320 + g * 128 + lane_off;  // dP^T_g, then dS^T_g
+    float* ld = sLD + (warp - 2) * 128;                    // this warp's lse2 | delta
+    const bool key_ok = kj < p.S;
     bool ok = true;
-    for (int i = 0; i < total; ++i) {
-      const int st = i & 1;
+    int cnt = 0;
+    for (int i = g; i < total; i += 2, ++cnt) {
       const int h = kvh * p.group + i / nq;
       const int qq0 = (qt0 + i % nq) * QB;
-      // this warp's copy of the query tile's lse (log2 units) and delta
-      float* ld = sLD + quad * 128;
       __syncwarp();
       for (int e = lane; e < QB; e += 32) {
         const int qi = qq0 + e;
@@ -672,51 +689,45 @@ __global__ void __launch_bounds__(192, 1)
         ld[QB + e] = in ? p.delta[((int64_t)b * p.H + h) * p.S + qi] : 0.f;
       }
       __syncwarp();
-      if (!mbar_wait(s_full(st), (i >> 1) & 1, abort_flag, 36)) { ok = false; break; }
-      if (i > 0 && !mbar_wait(pd_free, (i - 1) & 1, abort_flag, 37)) { ok = false; break; }
+      if (!mbar_wait(sd_full(g), cnt & 1, abort_flag, 36)) { ok = false; break; }
       tc_fence_after();
-      const bool key_ok = kj < p.S;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      // two halves of 32 queries: read S^T / dP^T columns 32*hh.. and write
+      // the packed P^T / dS^T to columns 16*hh.. (already-read columns)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
         float sv[32], dp[32];
-        tmem_ld32(tmem + st * 128 + lane_off + c * 32, sv);
-        tmem_ld32(tmem + st * 128 + 64 + lane_off + c * 32, dp);
+        tmem_ld32(tsv + hh * 32, sv);
+        tmem_ld32(tdp + hh * 32, dp);
+        uint32_t pp[16], pd[16];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int qi = qq0 + c * 32 + e;
-          const bool vis = key_ok && qi < p.S && kj <= qi && qi - kj < p.window;
-          const float pr = vis ? exp2f(sv[e] * p.sl2 - ld[c * 32 + e]) : 0.f;
-          sv[e] = pr;
-          dp[e] = pr * (dp[e] - ld[QB + c * 32 + e]) * p.scale;
-        }
-        // one 64-column atom: row r, chunks (c*4 .. c*4+3) swizzled by r & 7
+        for (int e = 0; e < 16; ++e) {
+          float pr[2], ds[2];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int swz = (c * 4 + q) ^ (r & 7);
-          *reinterpret_cast<uint4*>(sPT + r * 128 + swz * 16) =
-              make_uint4(pack_bf16(sv[8 * q], sv[8 * q + 1]), pack_bf16(sv[8 * q + 2], sv[8 * q + 3]),
-                         pack_bf16(sv[8 * q + 4], sv[8 * q + 5]), pack_bf16(sv[8 * q + 6], sv[8 * q + 7]));
-          *reinterpret_cast<uint4*>(sDST + r * 128 + swz * 16) =
-              make_uint4(pack_bf16(dp[8 * q], dp[8 * q + 1]), pack_bf16(dp[8 * q + 2], dp[8 * q + 3]),
-                         pack_bf16(dp[8 * q + 4], dp[8 * q + 5]), pack_bf16(dp[8 * q + 6], dp[8 * q + 7]));
+          for (int u = 0; u < 2; ++u) {
+            const int c = hh * 32 + 2 * e + u;
+            const int qi = qq0 + c;
+            const bool vis = key_ok && qi < p.S && kj <= qi && qi - kj < p.window;
+            pr[u] = vis ? fast_exp2(sv[2 * e + u] * p.sl2 - ld[c]) : 0.f;
+            ds[u] = pr[u] * (dp[2 * e + u] - ld[QB + c]) * p.scale;
+          }
+          pp[e] = pack_bf16(pr[0], pr[1]);
+          pd[e] = pack_bf16(ds[0], ds[1]);
         }
+        tmem_st16u(tsv + hh * 16, pp);
+        tmem_st16u(tdp + hh * 16, pd);
       }
+      tmem_st_wait();
       tc_fence_before();
-      fence_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(s_free(st));
-        mbar_arrive(pd_full);
-      }
+      if (lane == 0) mbar_arrive(pd_full(g));
     }
-    if (ok && mbar_wait(acc_done, 0, abort_flag, 38)) {
+    if (g == 0 && ok && mbar_wait(acc_done, 0, abort_flag, 38)) {
       tc_fence_after();
-      const bool key_ok = kj < p.S;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float v[32], k[32];
-        tmem_ld32(tmem + 256 + lane_off + c * 32, v);
-        tmem_ld32(tmem + 384 + lane_off + c * 32, k);
+        tmem_ld32(tmem + lane_off + c * 32, v);
+        tmem_ld32(tmem + 128 + lane_off + c * 32, k);
         if (key_ok) {
           const int64_t base = ((int64_t)(row0 + kj) * p.KV + kvh) * HD + c * 32;
           float4* dv4 = reinterpret_cast<float4*>(p.dv + base);
@@ -736,7 +747,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-constexpr size_t kDkdvSmem = 2 * TILE + 4 * QTILE + 2 * 16384 + 2048 + 1024 + 256;
+constexpr size_t kDkdvSmem = 2 * TILE + 2 * BSTAGES * QTILE + 8 * 128 * 4 + 1024 + 256;
 
 
 }  // namespace tc
@@ -798,7 +809,7 @@ void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, con
   p.lse = lse; p.delta = delta; p.dq = dq; p.dk = dk; p.dv = dv;
   {
     CUtensorMap mq = make_map3(q, dq_, sq, box128), mdo = make_map3(dout, dq_, sq, box128);
-    CUtensorMap mk = make_map3(k, dk_, sk, box128), mv = make_map3(v, dk_, sk, box128);
+    CUtensorMap mk = make_map3(k, dk_, sk, box64), mv = make_map3(v, dk_, sk, box64);
     p.n_tiles = (int)ceil_div(a.S, AT);
     static bool attr = false;
     if (!attr) {
@@ -807,7 +818,7 @@ void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, con
       attr = true;
     }
     dim3 grid((unsigned)p.n_tiles, (unsigned)a.H, (unsigned)a.B);
-    k_attn_dq_tc<<<grid, 192, kDqSmem, s>>>(mq, mk, mv, mdo, p);
+    k_attn_dq_tc<<<grid, 320, kDqSmem, s>>>(mq, mk, mv, mdo, p);
     DOP_LAUNCHED(launches);
   }
   {
@@ -821,7 +832,7 @@ void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, con
       attr = true;
     }
     dim3 grid((unsigned)p.n_tiles, (unsigned)a.KV, (unsigned)a.B);
-    k_attn_dkdv_tc<<<grid, 192, kDkdvSmem, s>>>(mq, mk, mv, mdo, p);
+    k_attn_dkdv_tc<<<grid, 320, kDkdvSmem, s>>>(mq, mk, mv, mdo, p);
     DOP_LAUNCHED(launches);
   }
 }
