@@ -35,6 +35,13 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 }  // namespace
 
 namespace dop {
+// Record the calling thread's error message (for entry points defined in
+// other translation units) and return its status code.
+int set_last_error(int code, const char* msg) {
+  g_last_error = msg;
+  return code;
+}
+
 int sm_count() {
   static int cached[16] = {0};
   int dev = 0;

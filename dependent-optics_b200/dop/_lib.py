@@ -92,6 +92,8 @@ SIGNATURES = [
                                   _P, _P]),
     ("dop_gqa_backward", C.c_int, [_I64, _I64, _I64, _I64, _I64, _I64, C.c_int, _P, _P, _P, _P,
                                    _P, _P, _P, _P, _P, _P, _P]),
+    ("dop_gqa_backward_f32_noalloc", C.c_int, [_I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P,
+                                               _P, _P, _P, _P, _P, _P, _P]),
     ("dop_f32_to_bf16", C.c_int, [_P, _P, _I64, _P]),
     ("dop_sgd_step", C.c_int, [_P, _P, _I64, C.c_float, _P]),
 ]

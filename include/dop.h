@@ -218,6 +218,23 @@ int dop_gqa_backward(int64_t batch, int64_t seq, int64_t heads, int64_t kv_heads
                      const float* lse, float* delta_ws, float* dq, float* dk, float* dv,
                      void* stream);
 
+/* The fp32 attention backward of dop_gqa_backward(..., DOP_F32, ...) for
+ * callers that may not allocate device memory (their memory belongs to
+ * another allocator, e.g. a framework's pool or a fixed arena): no delta_ws
+ * argument and no allocation inside the call.  It has no counterpart in the
+ * reference crate.  Its scratch is a 4 MiB array inside libdop's own device
+ * memory, held on every GPU that loads the library until exit, so it accepts
+ * batch * heads * seq <= 1,048,576 and rejects larger shapes with
+ * DOP_E_INVALID.  The first call on a device (with that device current)
+ * looks the array up with cudaGetSymbolAddress; make that first call before
+ * any stream capture.  All calls share the array: calls that overlap on the
+ * GPU race. */
+int dop_gqa_backward_f32_noalloc(int64_t batch, int64_t seq, int64_t heads,
+                                 int64_t kv_heads, int64_t head_dim, int64_t window,
+                                 const float* q, const float* k, const float* v,
+                                 const float* o, const float* dout, const float* lse,
+                                 float* dq, float* dk, float* dv, void* stream);
+
 /* First bounded-wait failure a tensor-core kernel recorded since load
  * (0 = none); a non-zero code means a kernel gave up waiting and returned. */
 int dop_device_status(void);
