@@ -141,6 +141,7 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
 }
 
 Block::~Block() {
+  if (expert_adjoint_done) cudaEventDestroy(expert_adjoint_done);
   for (auto& p : phases) {
     cudaEventDestroy(p.a);
     cudaEventDestroy(p.b);
@@ -366,6 +367,12 @@ void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_
     gemm<Act>(g6, s);
   }
   ph_end(s);
+  if (adjoint_stream) {  // the experts' adjoints are final from here on
+    if (!expert_adjoint_done)
+      DOP_CHECK_CUDA(cudaEventCreateWithFlags(&expert_adjoint_done, cudaEventDisableTiming));
+    DOP_CHECK_CUDA(cudaEventRecord(expert_adjoint_done, s));
+    DOP_CHECK_CUDA(cudaStreamWaitEvent(adjoint_stream, expert_adjoint_done, 0));
+  }
   // d_xn2 = sum_k dXp[row(t,k)] + dz Wr^T; router weight adjoint
   ph_begin("unpermute_router", s);
   unpermute_router_dx<Act>(dxp, slot_row, dz, P + off.router, T, (int)E, (int)K, (int)D, dxn2, s,

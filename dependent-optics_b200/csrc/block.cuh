@@ -29,6 +29,8 @@ struct Block {
   int64_t launches = 0;
   bool have_tape = false;
   const float* router_bias = nullptr;
+  cudaStream_t adjoint_stream = nullptr;  // waits for the experts' adjoints
+  cudaEvent_t expert_adjoint_done = nullptr;
   size_t bytes = 0;
   char* base = nullptr;   // one device allocation, carved below
 

@@ -341,6 +341,13 @@ int64_t dop_block_launches(const dop_block* blk) {
   return blk ? reinterpret_cast<const dop::Block*>(blk)->launches : -1;
 }
 
+int dop_block_set_adjoint_stream(dop_block* blk, void* stream) {
+  return guarded([&] {
+    DOP_REQUIRE(blk, "null block");
+    reinterpret_cast<dop::Block*>(blk)->adjoint_stream = as_stream(stream);
+  });
+}
+
 int dop_block_set_timing(dop_block* blk, int on) {
   return guarded([&] {
     DOP_REQUIRE(blk, "null block");

@@ -70,6 +70,7 @@ SIGNATURES = [
     ("dop_block_permutation", C.c_int, [_P, _P, _P, _P, _P]),
     ("dop_block_permuted_rows", _I64, [_P]),
     ("dop_block_launches", _I64, [_P]),
+    ("dop_block_set_adjoint_stream", C.c_int, [_P, _P]),
     ("dop_block_set_timing", C.c_int, [_P, C.c_int]),
     ("dop_block_phase_count", C.c_int, [_P]),
     ("dop_block_phase", C.c_int, [_P, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_float)]),

@@ -233,6 +233,11 @@ class Block:
         torch.cuda.synchronize()
         return sr, so, rt
 
+    def set_adjoint_stream(self, stream) -> None:
+        """Make `stream` (a torch.cuda.Stream or None) wait, in every backward,
+        until the experts' parameter adjoints are final."""
+        check(lib().dop_block_set_adjoint_stream(self._h, stream_ptr(stream)))
+
     def set_timing(self, on: bool = True) -> None:
         check(lib().dop_block_set_timing(self._h, int(on)))
 

@@ -130,6 +130,13 @@ int dop_block_permutation(const dop_block* blk, int32_t* slot_row,
 int64_t dop_block_permuted_rows(const dop_block* blk);
 /* Number of kernels the library launched on this handle since creation. */
 int64_t dop_block_launches(const dop_block* blk);
+/* Overlap of the adjoint reduction with the rest of the backward: after
+ * this call, every dop_block_backward makes `stream` (a cudaStream_t; NULL
+ * turns it off) wait until the experts' parameter adjoints — the layer slice
+ * from gate0 to the end — are final, which happens before the attention half
+ * of the backward runs.  A data-parallel caller reduces that slice on
+ * `stream` while the backward continues on its own stream. */
+int dop_block_set_adjoint_stream(dop_block* blk, void* stream);
 /* Per-phase device timing (CUDA events on the caller's stream around each
  * phase of forward/backward: "expert_gate_up", "attn_fwd", ...).  Off by
  * default; dop_block_phase() synchronises the phase's events. */
