@@ -74,6 +74,10 @@ SIGNATURES = [
     ("dop_block_set_timing", C.c_int, [_P, C.c_int]),
     ("dop_block_phase_count", C.c_int, [_P]),
     ("dop_block_phase", C.c_int, [_P, C.c_int, C.POINTER(C.c_char_p), C.POINTER(C.c_float)]),
+    ("dop_model_create", C.c_int, [C.POINTER(MixtralCfg), _I64, _I64, C.c_int, C.POINTER(_P)]),
+    ("dop_model_destroy", C.c_int, [_P]),
+    ("dop_model_forward_backward", C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P]),
+    ("dop_model_parameter_count", _I64, [_P]),
     ("dop_lens_from_block", C.c_int, [_P, _P, _P, C.POINTER(_P)]),
     ("dop_compose", C.c_int, [_P, _P, C.POINTER(_P)]),
     ("dop_lens_forward", C.c_int, [_P, _P, _P, _P]),

@@ -255,3 +255,60 @@ class Block:
 
     def workspace_bytes(self) -> int:
         return int(lib().dop_block_workspace_bytes(self._h))
+
+
+class LossGrad:
+    """`LossGrad` (src/mixtral.rs:231-235): loss, grad and logits (device tensors)."""
+
+    def __init__(self, loss, grad, logits):
+        self.loss, self.grad, self.logits = loss, grad, logits
+
+
+class Model:
+    """The whole model lens on the GPU (dop_model)."""
+
+    def __init__(self, cfg: MixtralConfig, batch: int, seq: int, precision: int = DOP_F32):
+        self.cfg, self.batch, self.seq, self.precision = cfg, batch, seq, precision
+        h = C.c_void_p()
+        check(lib().dop_model_create(C.byref(cfg.to_c()), batch, seq, precision, C.byref(h)))
+        self._h = h
+        self.n_params = int(lib().dop_model_parameter_count(h))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().dop_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def forward_backward(self, params, tokens, targets, stream=None) -> LossGrad:
+        import torch
+        dev = params.device
+        T, V = self.batch * self.seq, self.cfg.vocab
+        loss = torch.empty((), dtype=torch.float32, device=dev)
+        grad = torch.empty(self.n_params, dtype=torch.float32, device=dev)
+        logits = torch.empty(T, V, dtype=torch.float32, device=dev)
+        check(lib().dop_model_forward_backward(self._h, ptr(params), ptr(tokens), ptr(targets),
+                                               ptr(loss), ptr(grad), ptr(logits),
+                                               stream_ptr(stream)))
+        return LossGrad(loss, grad, logits)
+
+
+def forward_backward(cfg: MixtralConfig, params, tokens, targets, batch: int, seq: int,
+                     precision: int = DOP_F32) -> LossGrad:
+    """`mixtral::forward_backward` (src/mixtral.rs:245-261) on the GPU.
+    params: device tensor of the whole flat parameter vector; tokens/targets:
+    device int64 tensors of batch*seq ids."""
+    m = Model(cfg, batch, seq, precision)
+    try:
+        return m.forward_backward(params, tokens, targets)
+    finally:
+        import torch
+        torch.cuda.synchronize()
+        m.close()
+
+
+def sgd_step(params, grad, lr: float) -> None:
+    """`sgd_step` (src/mixtral.rs:994-1001) on device tensors: p -= lr * g."""
+    check(lib().dop_sgd_step(ptr(params), ptr(grad), params.numel(), lr, None))

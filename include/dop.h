@@ -144,6 +144,26 @@ int dop_block_set_timing(dop_block* blk, int on);
 int dop_block_phase_count(const dop_block* blk);
 int dop_block_phase(const dop_block* blk, int i, const char** name, float* ms);
 
+/* ---------------------------------------------------------- the model lens
+ * `mixtral::forward_backward` (src/mixtral.rs:245-261): embed, `layers`
+ * block lenses, final RMSNorm, LM head, mean next-token cross-entropy
+ * (:966-991), and the adjoint of every parameter.  `params` is the whole
+ * flat parameter vector in `layout` order (fp32 or bf16 per precision);
+ * tokens/targets are device int64 [batch*seq]; `loss` is a device float;
+ * `dparams` (fp32, dop_model_parameter_count floats) is OVERWRITTEN with a
+ * fresh adjoint, like the crate's returned `grad`; `logits` (fp32
+ * [batch*seq, vocab], may be NULL) receives the logits.  Each layer keeps its
+ * own residual, so memory grows with `layers` x the block workspace. */
+typedef struct dop_model dop_model;
+int dop_model_create(const dop_mixtral_cfg* cfg, int64_t batch, int64_t seq,
+                     int precision, dop_model** out);
+int dop_model_destroy(dop_model* m);
+int dop_model_forward_backward(dop_model* m, const void* params,
+                               const int64_t* tokens, const int64_t* targets,
+                               float* loss, float* dparams, float* logits,
+                               void* stream);
+int64_t dop_model_parameter_count(const dop_model* m);
+
 /* ------------------------------------------------------- lens composition
  * `compose(g, f)` means g after f (src/dlens.rs:74-113; README "compose(g, f)
  * always means g ∘ f").  Forward runs f then g; backward runs g's put then
