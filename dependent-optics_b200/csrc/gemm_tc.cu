@@ -9,9 +9,9 @@
 //                 STAGES-deep shared-memory ring (cp.async.bulk.tensor)
 //   warp 1        allocates 512 TMEM columns; one thread issues
 //                 tcgen05.mma (M=128, N=BN, K=16) and tcgen05.commit
-//   warps 2..5    epilogue: tcgen05.ld of the fp32 accumulator (each warp
-//                 owns the 32 TMEM lanes of its quadrant), fused epilogue
-//                 math, global stores
+//   warps 2..9    epilogue: tcgen05.ld of the fp32 accumulator (two warps
+//                 per 32-lane TMEM quadrant, each owning half the columns),
+//                 fused epilogue math, global stores
 //
 // The accumulator is double-buffered in TMEM (2 x BN columns), so the
 // epilogue of tile i overlaps the main loop of tile i+1.  Either operand may be
@@ -35,7 +35,7 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int STAGES = 4;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;  // TMA warp, MMA warp, 8 epilogue warps
 
 enum EpiKind : int {
   kStoreF32 = 0,
@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(accf_bar(a), 1);
-      mbar_init(acce_bar(a), 4);
+      mbar_init(acce_bar(a), 8);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -260,7 +260,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // two warps per TMEM lane quadrant (warp & 3), each owning half of the
+    // tile's columns
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int chalf = (warp - 2) >> 2;
     const int row_in_tile = quad * 32 + lane;
     int a = 0;
     uint32_t aph = 0;
@@ -277,7 +280,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (p.epi == kSwiGLU) {
         const int64_t nb = (int64_t)tl.n * (BN / 2);
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+        for (int c = chalf * (BN / 128); c < (chalf + 1) * (BN / 128); ++c) {
           float g[32], u[32];
           tmem_ld32(tbase + c * 32, g);
           tmem_ld32(tbase + BN / 2 + c * 32, u);
@@ -314,7 +317,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         char* Cb = (char*)p.C;
         if (p.mode == 2) Cb += (int64_t)tl.g * p.c_gs * (p.epi == kStoreBF16 ? 2 : 4);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = chalf * (BN / 64); c < (chalf + 1) * (BN / 64); ++c) {
           float v[32];
           if (!empty_k) tmem_ld32(tbase + c * 32, v);
           else {
