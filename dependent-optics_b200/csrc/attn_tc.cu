@@ -3,16 +3,18 @@
 // (src/mixtral.rs:799-922): causal sliding-window grouped-query attention,
 // visible(q, k) = k <= q && q - k < W.
 //
-// Forward, one CTA per (128-query tile, head, sequence):
-//   warp 0      TMA: the Q tile once, then K/V tiles of 128 keys into a
-//               2-stage ring (128B-swizzled, bf16)
-//   warp 1      TMEM owner; one thread issues S_j = Q K_j^T into one of two
-//               S buffers and PV_j = P_j V_j into a PV buffer (tcgen05.mma)
-//   warps 2..5  softmax, one query row per thread: online max / sum in the
-//               log2 domain, P_j written to shared memory as the bf16 A
-//               operand of the next MMA, O accumulated in registers
-//               (O = O * alpha + PV), log-sum-exp kept for the backward pass.
-// S_{j+1} runs on the tensor core while the softmax warps work on S_j.
+// Forward, one CTA per (pair of 128-query tiles, head, sequence):
+//   warp 0      TMA: the two Q tiles once, then K and V tiles of 128 keys,
+//               each into its own 2-stage ring (128B-swizzled, bf16)
+//   warp 1      TMEM owner; one thread issues S_g = Q_g K^T into S_g and
+//               O_g += P_g V (P_g read from TMEM) for both query tiles g
+//   warps 2..9  softmax, one query row per thread, warps 2-5 for tile A and
+//               6-9 for tile B: online max / sum in the log2 domain, P_g
+//               written back over S_g in TMEM as packed bf16, O_g rescaled
+//               in TMEM only when the row max grows by more than 2^8, and
+//               the log-sum-exp kept for the backward pass.
+// The tensor core alternates between the tiles: while one tile's softmax
+// runs, the other tile's P V and next S run.
 #include "kernels.cuh"
 #include "tc_ptx.cuh"
 
@@ -71,11 +73,16 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   const uint32_t b0 = smem_u32(bars);
   const uint32_t q_full = b0, drain = b0 + 8;
-  auto kv_full = [&](int st) { return b0 + 16 + 8u * st; };
-  auto kv_empty = [&](int st) { return b0 + 32 + 8u * st; };
+  // K and V stages are released separately: K(t) once both S MMAs of tile t
+  // are issued, V(t) once both P V MMAs are, so K(t+2) streams in while
+  // tile t+1 is still on the tensor core.
+  auto k_full = [&](int st) { return b0 + 16 + 8u * st; };
+  auto k_empty = [&](int st) { return b0 + 32 + 8u * st; };
   auto s_full = [&](int g) { return b0 + 48 + 8u * g; };
   auto p_full = [&](int g) { return b0 + 64 + 8u * g; };
   auto o_done = [&](int g) { return b0 + 80 + 8u * g; };
+  auto v_full = [&](int st) { return b0 + 96 + 8u * st; };
+  auto v_empty = [&](int st) { return b0 + 112 + 8u * st; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pt = p.n_qt - 1 - (int)blockIdx.x;  // longest rows first
@@ -98,8 +105,10 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(q_full, 1);
     mbar_init(drain, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(kv_full(i), 1);
-      mbar_init(kv_empty(i), 1);
+      mbar_init(k_full(i), 1);
+      mbar_init(k_empty(i), 1);
+      mbar_init(v_full(i), 1);
+      mbar_init(v_empty(i), 1);
       mbar_init(s_full(i), 1);
       mbar_init(p_full(i), 4);
       mbar_init(o_done(i), 1);
@@ -125,24 +134,27 @@ __global__ void __launch_bounds__(320, 1)
         tma_load_3d(q_s + g * TILE, &mq, q_full, 0, h, row0 + q0 + g * AT);
         tma_load_3d(q_s + g * TILE + HALF, &mq, q_full, 64, h, row0 + q0 + g * AT);
       }
-      int issued = 0;
+      int nk = 0, nv = 0;  // K and V tiles issued
       bool ok = true;
       for (int t = u0; t <= u1; ++t) {
-        const int j = t - u0, st = j & 1;
-        if (!mbar_wait(kv_empty(st), ((j >> 1) & 1) ^ 1, abort_flag, 11)) { ok = false; break; }
+        const int j = t - u0, st = j & 1, ph = ((j >> 1) & 1) ^ 1;
         const int k0 = t * AT;
+        if (!mbar_wait(k_empty(st), ph, abort_flag, 11)) { ok = false; break; }
         const uint32_t ks = smem_u32(sK + st * TILE), vs = smem_u32(sV + st * TILE);
-        mbar_expect_tx(kv_full(st), 2 * TILE);
-        tma_load_3d(ks, &mk, kv_full(st), 0, kvh, row0 + k0);
-        tma_load_3d(ks + HALF, &mk, kv_full(st), 64, kvh, row0 + k0);
-        tma_load_3d(vs, &mv, kv_full(st), 0, kvh, row0 + k0);
-        tma_load_3d(vs + HALF, &mv, kv_full(st), 64, kvh, row0 + k0);
-        ++issued;
+        mbar_expect_tx(k_full(st), TILE);
+        tma_load_3d(ks, &mk, k_full(st), 0, kvh, row0 + k0);
+        tma_load_3d(ks + HALF, &mk, k_full(st), 64, kvh, row0 + k0);
+        ++nk;
+        if (!mbar_wait(v_empty(st), ph, abort_flag, 10)) { ok = false; break; }
+        mbar_expect_tx(v_full(st), TILE);
+        tma_load_3d(vs, &mv, v_full(st), 0, kvh, row0 + k0);
+        tma_load_3d(vs + HALF, &mv, v_full(st), 64, kvh, row0 + k0);
+        ++nv;
       }
       if (!ok) {
         mbar_wait_drain(q_full, 0);
-        for (int j = issued - 1; j >= 0 && j >= issued - 2; --j)
-          mbar_wait_drain(kv_full(j & 1), (j >> 1) & 1);
+        for (int j = nk - 1; j >= 0 && j >= nk - 2; --j) mbar_wait_drain(k_full(j & 1), (j >> 1) & 1);
+        for (int j = nv - 1; j >= 0 && j >= nv - 2; --j) mbar_wait_drain(v_full(j & 1), (j >> 1) & 1);
       }
     }
   } else if (warp == 1) {
@@ -181,15 +193,25 @@ __global__ void __launch_bounds__(320, 1)
       const int lo0 = g_lo[0], hi0 = g_hi[0], lo1 = g_lo[1], hi1 = g_hi[1];
       for (int t = u0; t <= u1 && ok; ++t) {
         const int j = t - u0, st = j & 1;
-        if (!mbar_wait(kv_full(st), (j >> 1) & 1, abort_flag, 15)) { ok = false; break; }
+        // P V of tile t-1 needs V(t-1)
+        if ((pd0 >= 0 || pd1 >= 0) &&
+            !mbar_wait(v_full((j - 1) & 1), ((j - 1) >> 1) & 1, abort_flag, 16)) { ok = false; break; }
+        tc_fence_after();
+        if (pd0 >= 0 && !issue_pv(0, pd0, nd0, lo0, hi0)) { ok = false; break; }
+        if (!mbar_wait(k_full(st), (j >> 1) & 1, abort_flag, 15)) { ok = false; break; }
         tc_fence_after();
         const uint32_t ks = smem_u32(sK + st * TILE);
-        if (pd0 >= 0 && !issue_pv(0, pd0, nd0, lo0, hi0)) { ok = false; break; }
         if (t >= lo0 && t <= hi0) { issue_s(0, ks); ++nd0; pd0 = t; }
         if (pd1 >= 0 && !issue_pv(1, pd1, nd1, lo1, hi1)) { ok = false; break; }
+        // every P V that reads V(t-1) has been issued: release its stage
+        if (j >= 1) mma_commit(v_empty((j - 1) & 1));
         if (t >= lo1 && t <= hi1) { issue_s(1, ks); ++nd1; pd1 = t; }
-        // every P V that reads tile t-1 has been issued: release its stage
-        if (j >= 1) mma_commit(kv_empty((j - 1) & 1));
+        mma_commit(k_empty(st));  // both S MMAs that read K(t) are issued
+      }
+      if (ok && (pd0 >= 0 || pd1 >= 0)) {
+        const int j = u1 - u0;
+        ok = mbar_wait(v_full(j & 1), (j >> 1) & 1, abort_flag, 16);
+        tc_fence_after();
       }
       if (ok && pd0 >= 0 && !issue_pv(0, pd0, nd0, lo0, hi0)) ok = false;
       if (ok && pd1 >= 0 && !issue_pv(1, pd1, nd1, lo1, hi1)) ok = false;
@@ -198,10 +220,16 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ---------------------------------------------------------- softmax
+    // One query row per thread.  S is read from TMEM once (128 columns);
+    // masks are applied only on tiles that cross the diagonal or the
+    // window edge; the row max and sum use independent accumulators and
+    // paired fp32 instructions so that a single warp per SM sub-partition
+    // keeps its pipelines busy.
     const int g = (warp - 2) >> 2;          // query tile of this warp group
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const int qi = q0 + g * AT + r;
+    const int r0 = q0 + g * AT;
+    const int qi = r0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t ts = tmem + g * 128 + lane_off;        // S_g, then P_g
     const uint32_t to = tmem + 256 + g * 128 + lane_off;  // O_g
@@ -209,24 +237,35 @@ __global__ void __launch_bounds__(320, 1)
     bool ok = true;
     const int my_lo = g ? g_lo[1] : g_lo[0];
     const int n = (g ? g_hi[1] : g_hi[0]) - my_lo + 1;
+    const float2 sl2v = make_float2(p.sl2, p.sl2);
     for (int it = 0; it < n; ++it) {
       if (!mbar_wait(s_full(g), it & 1, abort_flag, 17 + g)) { ok = false; break; }
       tc_fence_after();
       const int k0 = (my_lo + it) * AT;
-      const bool all_vis = (k0 + AT - 1 <= qi) && (qi - k0 < p.window);
-      // pass 1: row max of the scaled, masked scores (S stays in TMEM)
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float sv[32];
-        tmem_ld32(ts + c * 32, sv);
+      // every (query, key) pair of the tile is visible: no masks
+      const bool full = (k0 + AT - 1 <= r0) && (r0 + AT - 1 - k0 < p.window);
+      float sv[128];
+      tmem_ld128(ts, sv);
+      if (!full) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = k0 + c * 32 + i;
-          const bool vis = all_vis || (key <= qi && qi - key < p.window);
-          mx = vis ? fmaxf(mx, sv[i] * p.sl2) : mx;
+        for (int i = 0; i < 128; ++i) {
+          const int key = k0 + i;
+          if (!(key <= qi && qi - key < p.window)) sv[i] = -INFINITY;
         }
       }
+      // row max of the raw scores (scaling by sl2 > 0 after the max gives
+      // the same value as the max of the scaled scores)
+      float a[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) a[u] = fmax3(sv[u], sv[8 + u], sv[16 + u]);
+#pragma unroll
+      for (int i = 24; i < 120; i += 16)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) a[u] = fmax3(a[u], sv[i + u], sv[i + 8 + u]);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) a[u] = fmaxf(a[u], sv[120 + u]);
+      const float mx = fmaxf(fmax3(a[0], a[1], a[2]), fmax3(fmax3(a[3], a[4], a[5]), a[6], a[7])) *
+                       p.sl2;
       // Raise the reference max when it grew by more than kRescale.  The
       // decision is per row, but the TMEM loads/stores that rescale O are
       // warp-collective, so the warp rescales when any of its rows needs it
@@ -234,8 +273,33 @@ __global__ void __launch_bounds__(320, 1)
       const bool raise = mx > m + kRescale || (m == -INFINITY && mx > -INFINITY);
       const float m_new = raise ? mx : m;
       const float alpha = raise ? (m == -INFINITY ? 0.f : fast_exp2(m - m_new)) : 1.f;
-      if (it > 0 && __any_sync(0xffffffffu, raise && m != -INFINITY)) {
-        // O is complete: S_g(it) was issued after P V of the previous tile
+      const bool rescale = it > 0 && __any_sync(0xffffffffu, raise && m != -INFINITY);
+      m = m_new;
+      // P = 2^(s sl2 - m); a row with nothing visible yet (m = -inf) has
+      // every score masked to -inf, and 2^(-inf) = 0
+      const float nm = m == -INFINITY ? 0.f : -m;
+      const float2 nmv = make_float2(nm, nm);
+      float2 acc[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[u] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int qq = 0; qq < 4; ++qq) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 x = ffma2(make_float2(sv[qq * 32 + 2 * i], sv[qq * 32 + 2 * i + 1]), sl2v, nmv);
+          const float2 e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          acc[i & 3] = fadd2(acc[i & 3], e);
+          pk[i] = pack_bf16(e.x, e.y);
+        }
+        tmem_st16u(ts + qq * 16, pk);
+      }
+      const float2 s01 = fadd2(acc[0], acc[1]), s23 = fadd2(acc[2], acc[3]);
+      const float2 s4 = fadd2(s01, s23);
+      l = l * alpha + (s4.x + s4.y);
+      if (rescale) {
+        // O is complete (S_g(it) was issued after P V of the previous tile)
+        // and stays so until p_full is signalled below
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           float ov[32];
@@ -245,32 +309,6 @@ __global__ void __launch_bounds__(320, 1)
           tmem_st32(to + c * 32, ov);
         }
       }
-      l *= alpha;
-      m = m_new;
-      float sum = 0.f;
-      const bool none = m == -INFINITY;  // nothing visible yet in this row
-      // pass 2: P = 2^(s - m) as packed bf16 pairs over the S columns
-#pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
-        float sv[64];
-        tmem_ld32(ts + hh * 64, sv);
-        tmem_ld32(ts + hh * 64 + 32, sv + 32);
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float e[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int key = k0 + hh * 64 + 2 * i + u;
-            const bool vis = !none && (all_vis || (key <= qi && qi - key < p.window));
-            e[u] = vis ? fast_exp2(sv[2 * i + u] * p.sl2 - m) : 0.f;
-          }
-          sum += e[0] + e[1];
-          pk[i] = pack_bf16(e[0], e[1]);
-        }
-        tmem_st32u(ts + hh * 32, pk);
-      }
-      l += sum;
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
