@@ -523,30 +523,37 @@ __global__ void __launch_bounds__(320, 1)
     const bool row_ok = qi < p.S;
     const float lse2 = row_ok ? p.lse[((int64_t)b * p.H + h) * p.S + qi] * kLog2e : 0.f;
     const float dlt = row_ok ? p.delta[((int64_t)b * p.H + h) * p.S + qi] : 0.f;
+    // P = 2^(s sl2 - lse2), dS = P (dP scale - delta scale), as paired FMAs
+    const float2 sl2v = make_float2(p.sl2, p.sl2), scv = make_float2(p.scale, p.scale);
+    const float2 nl2 = make_float2(-lse2, -lse2);
+    const float2 nd2 = make_float2(-dlt * p.scale, -dlt * p.scale);
     bool ok = true;
     int cnt = 0;
     for (int j = g; j < nt; j += 2, ++cnt) {
       if (!mbar_wait(sd_full(g), cnt & 1, abort_flag, 26)) { ok = false; break; }
       tc_fence_after();
       const int k0 = (lo + j) * QB;
-      const bool all_vis = (k0 + QB - 1 <= qi) && (qi - k0 < p.window);
+      // every (query, key) pair of the 128 x 64 tile is visible: no masks
+      const bool full = (k0 + QB - 1 <= q0) && (q0 + AT - 1 - k0 < p.window) && (q0 + AT <= p.S);
       uint32_t pk[32];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         float sv[32], dp[32];
-        tmem_ld32(ts + hh * 32, sv);
-        tmem_ld32(td + hh * 32, dp);
+        tmem_ld32x2(ts + hh * 32, td + hh * 32, sv, dp);
+        if (!full) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int key = k0 + hh * 32 + i;
+            if (!(row_ok && key <= qi && qi - key < p.window)) sv[i] = -INFINITY;
+          }
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float e[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int key = k0 + hh * 32 + 2 * i + u;
-            const bool vis = row_ok && (all_vis || (key <= qi && qi - key < p.window));
-            const float pr = vis ? fast_exp2(sv[2 * i + u] * p.sl2 - lse2) : 0.f;
-            e[u] = pr * (dp[2 * i + u] - dlt) * p.scale;
-          }
-          pk[hh * 16 + i] = pack_bf16(e[0], e[1]);
+          const float2 x = ffma2(make_float2(sv[2 * i], sv[2 * i + 1]), sl2v, nl2);
+          const float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          const float2 d = ffma2(make_float2(dp[2 * i], dp[2 * i + 1]), scv, nd2);
+          const float2 ds = fmul2(pr, d);
+          pk[hh * 16 + i] = pack_bf16(ds.x, ds.y);
         }
       }
       tmem_st32u(ts, pk);
@@ -593,7 +600,7 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* sV = smem + TILE;
   uint8_t* sQ = smem + 2 * TILE;                // BSTAGES x [64 q][128 d]
   uint8_t* sDO = sQ + BSTAGES * QTILE;
-  float* sLD = (float*)(sDO + BSTAGES * QTILE); // [8 warps][lse2 64 | delta 64]
+  float* sLD = (float*)(sDO + BSTAGES * QTILE); // [8 warps][-lse2 64 | -delta scale 64]
   uint64_t* bars = (uint64_t*)(sLD + 8 * 128);
   uint32_t* tmem_slot = (uint32_t*)(bars + 16);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
@@ -712,8 +719,9 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t tsv = tmem + 256 + g * 128 + lane_off;  // S^T_g, then P^T_g
     const uint32_t tdp = tmem + 320 + g * 128 + lane_off;  // dP^T_g, then dS^T_g
-    float* ld = sLD + (warp - 2) * 128;                    // this warp's lse2 | delta
+    float* ld = sLD + (warp - 2) * 128;                    // this warp's -lse2 | -delta scale
     const bool key_ok = kj < p.S;
+    const float2 sl2v = make_float2(p.sl2, p.sl2), scv = make_float2(p.scale, p.scale);
     bool ok = true;
     int cnt = 0;
     for (int i = g; i < total; i += 2, ++cnt) {
@@ -723,33 +731,47 @@ __global__ void __launch_bounds__(320, 1)
       for (int e = lane; e < QB; e += 32) {
         const int qi = qq0 + e;
         const bool in = qi < p.S;
-        ld[e] = in ? p.lse[((int64_t)b * p.H + h) * p.S + qi] * kLog2e : 0.f;
-        ld[QB + e] = in ? p.delta[((int64_t)b * p.H + h) * p.S + qi] : 0.f;
+        const int64_t at = ((int64_t)b * p.H + h) * p.S + qi;
+        ld[e] = in ? -p.lse[at] * kLog2e : 0.f;           // -lse2
+        ld[QB + e] = in ? -p.delta[at] * p.scale : 0.f;    // -delta scale
       }
       __syncwarp();
       if (!mbar_wait(sd_full(g), cnt & 1, abort_flag, 36)) { ok = false; break; }
       tc_fence_after();
+      // every (key, query) pair of the 128 x 64 tile is visible: no masks
+      const bool full = (k0 + AT <= p.S) && (qq0 + QB <= p.S) && (k0 + AT - 1 <= qq0) &&
+                        (qq0 + QB - 1 - k0 < p.window);
       // two halves of 32 queries: read S^T / dP^T columns 32*hh.. and write
       // the packed P^T / dS^T to columns 16*hh.. (already-read columns)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         float sv[32], dp[32];
-        tmem_ld32(tsv + hh * 32, sv);
-        tmem_ld32(tdp + hh * 32, dp);
+        tmem_ld32x2(tsv + hh * 32, tdp + hh * 32, sv, dp);
+        if (!full) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int qi = qq0 + hh * 32 + e;
+            if (!(key_ok && qi < p.S && kj <= qi && qi - kj < p.window)) sv[e] = -INFINITY;
+          }
+        }
         uint32_t pp[16], pd[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float pr[2], ds[2];
+        for (int e4 = 0; e4 < 8; ++e4) {
+          const int c = hh * 32 + 4 * e4;
+          const float4 nl = *reinterpret_cast<const float4*>(ld + c);
+          const float4 nd = *reinterpret_cast<const float4*>(ld + QB + c);
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
-            const int c = hh * 32 + 2 * e + u;
-            const int qi = qq0 + c;
-            const bool vis = key_ok && qi < p.S && kj <= qi && qi - kj < p.window;
-            pr[u] = vis ? fast_exp2(sv[2 * e + u] * p.sl2 - ld[c]) : 0.f;
-            ds[u] = pr[u] * (dp[2 * e + u] - ld[QB + c]) * p.scale;
+            const int e = 2 * e4 + u;
+            const float2 nlu = u ? make_float2(nl.z, nl.w) : make_float2(nl.x, nl.y);
+            const float2 ndu = u ? make_float2(nd.z, nd.w) : make_float2(nd.x, nd.y);
+            const float2 x = ffma2(make_float2(sv[2 * e], sv[2 * e + 1]), sl2v, nlu);
+            const float2 pr = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+            const float2 d = ffma2(make_float2(dp[2 * e], dp[2 * e + 1]), scv, ndu);
+            const float2 ds = fmul2(pr, d);
+            pp[e] = pack_bf16(pr.x, pr.y);
+            pd[e] = pack_bf16(ds.x, ds.y);
           }
-          pp[e] = pack_bf16(pr[0], pr[1]);
-          pd[e] = pack_bf16(ds[0], ds[1]);
         }
         tmem_st16u(tsv + hh * 16, pp);
         tmem_st16u(tdp + hh * 16, pd);
