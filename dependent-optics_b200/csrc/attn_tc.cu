@@ -377,7 +377,43 @@ struct BwdParams {
   float* dq;
   float* dk;
   float* dv;
+  AttnBwdBf16 o16;  // bf16 outputs (o16.dq set) instead of dq, dk, dv
 };
+
+// Row `pos` of a head's gradient, columns d and d + 64 (d in c0..c0+31) in
+// a[] and b[]: rotate back by the RoPE adjoint (rope_qkv_transpose,
+// src/mixtral.rs:777-797) when cs is set, round to bf16 and store.
+__device__ __forceinline__ void store_grad_bf16(bf16* dst, int c0, const float* a, const float* b,
+                                                const float* cs, const float* sn, int pos) {
+  float o1[32], o2[32];
+  if (cs) {
+    const float4* c4 = reinterpret_cast<const float4*>(cs + (int64_t)pos * (HD / 2) + c0);
+    const float4* s4 = reinterpret_cast<const float4*>(sn + (int64_t)pos * (HD / 2) + c0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 cv = c4[q], sv = s4[q];
+      const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = 4 * q + u;
+        o1[i] = a[i] * cc[u] + b[i] * ss[u];
+        o2[i] = b[i] * cc[u] - a[i] * ss[u];
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) { o1[i] = a[i]; o2[i] = b[i]; }
+  }
+  uint4* d1 = reinterpret_cast<uint4*>(dst + c0);
+  uint4* d2 = reinterpret_cast<uint4*>(dst + c0 + HD / 2);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    d1[q] = make_uint4(pack_bf16(o1[8 * q], o1[8 * q + 1]), pack_bf16(o1[8 * q + 2], o1[8 * q + 3]),
+                       pack_bf16(o1[8 * q + 4], o1[8 * q + 5]), pack_bf16(o1[8 * q + 6], o1[8 * q + 7]));
+    d2[q] = make_uint4(pack_bf16(o2[8 * q], o2[8 * q + 1]), pack_bf16(o2[8 * q + 2], o2[8 * q + 3]),
+                       pack_bf16(o2[8 * q + 4], o2[8 * q + 5]), pack_bf16(o2[8 * q + 6], o2[8 * q + 7]));
+  }
+}
 
 // Backward kernels.  Both use 320 threads: warp 0 TMA, warp 1 MMA, warps
 // 2-5 and 6-9 two elementwise groups that take alternate tiles, so one
@@ -562,8 +598,18 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_full(g));
     }
-    if (g == 0 && ok && mbar_wait(dq_done, 0, abort_flag, 28)) {
-      tc_fence_after();
+    const bool done = g == 0 && ok && mbar_wait(dq_done, 0, abort_flag, 28);
+    if (done) tc_fence_after();
+    if (done && p.o16.dq) {
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        float a[32], bb[32];
+        tmem_ld32x2(tmem + lane_off + c * 32, tmem + lane_off + (c + 2) * 32, a, bb);
+        if (row_ok)
+          store_grad_bf16(p.o16.dq + ((int64_t)(row0 + qi) * p.H + h) * HD, c * 32, a, bb,
+                          p.o16.cs, p.o16.sn, qi);
+      }
+    } else if (done) {
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float v[32];
@@ -781,8 +827,19 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(pd_full(g));
     }
-    if (g == 0 && ok && mbar_wait(acc_done, 0, abort_flag, 38)) {
-      tc_fence_after();
+    const bool done = g == 0 && ok && mbar_wait(acc_done, 0, abort_flag, 38);
+    if (done) tc_fence_after();
+    if (done && p.o16.dq) {
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        float a[32], bb[32];
+        const int64_t base = ((int64_t)(row0 + kj) * p.KV + kvh) * HD;
+        tmem_ld32x2(tmem + lane_off + c * 32, tmem + lane_off + (c + 2) * 32, a, bb);
+        if (key_ok) store_grad_bf16(p.o16.dv + base, c * 32, a, bb, nullptr, nullptr, kj);
+        tmem_ld32x2(tmem + 128 + lane_off + c * 32, tmem + 128 + lane_off + (c + 2) * 32, a, bb);
+        if (key_ok) store_grad_bf16(p.o16.dk + base, c * 32, a, bb, p.o16.cs, p.o16.sn, kj);
+      }
+    } else if (done) {
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float v[32], k[32];
@@ -850,7 +907,7 @@ void attn_fwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, bf1
 
 void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, const bf16* o,
                  const bf16* dout, const float* lse, float* delta, float* dq, float* dk, float* dv,
-                 cudaStream_t s, int64_t& launches) {
+                 cudaStream_t s, int64_t& launches, const AttnBwdBf16* out16) {
   using namespace tc;
   check_tc(a);
   bind_error_word();
@@ -867,6 +924,13 @@ void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, con
   p.sl2 = a.scale * kLog2e;
   p.scale = a.scale;
   p.lse = lse; p.delta = delta; p.dq = dq; p.dk = dk; p.dv = dv;
+  if (out16) {
+    DOP_REQUIRE(out16->dq && out16->dk && out16->dv, "bf16 gradient outputs need dq, dk and dv");
+    DOP_REQUIRE(!out16->cs || out16->sn, "RoPE adjoint needs both tables");
+    p.o16 = *out16;
+  } else {
+    DOP_REQUIRE(dq && dk && dv, "null gradient output");
+  }
   {
     CUtensorMap mq = make_map3(q, dq_, sq, box128), mdo = make_map3(dout, dq_, sq, box128);
     CUtensorMap mk = make_map3(k, dk_, sk, box64), mv = make_map3(v, dk_, sk, box64);

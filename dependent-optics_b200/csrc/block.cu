@@ -400,19 +400,27 @@ void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_
   ph_begin("attn_bwd", s);
   Attn at; at.B = B; at.S = S; at.H = H; at.KV = KV; at.hd = hd; at.window = cfg.sliding_window;
   at.causal = true; at.scale = 1.0f / sqrtf((float)hd);
-  if (!f32 && hd == 128)
-    attn_bwd_tc(at, (const bf16*)q_, (const bf16*)k_, (const bf16*)v_, (const bf16*)mix_,
-                (const bf16*)dmix_, lse, delta, dq, dk, dv, s, launches);
-  else
-    attn_bwd_simt<Act>(at, q_, k_, v_, mix_, dmix_, lse, delta, dq, dk, dv, s, launches);
-  ph_end(s);
-  ph_begin("rope_bwd", s);
-  rope<float, Act>(dq, dq_, T, (int)S, H, hd, rope_cos, rope_sin, -1.f, s, launches);
-  rope<float, Act>(dk, dk_, T, (int)S, KV, hd, rope_cos, rope_sin, -1.f, s, launches);
   const Act* dv_op;
-  if (f32) dv_op = (const Act*)dv;
-  else { convert<Act>(dv, dv_, T * kvd, s, launches); dv_op = dv_; }
-  ph_end(s);
+  if (!f32 && hd == 128) {
+    // the attention backward writes bf16 dq, dk (rotated back by the RoPE
+    // adjoint) and dv straight from its accumulators
+    AttnBwdBf16 o16;
+    o16.dq = (bf16*)dq_; o16.dk = (bf16*)dk_; o16.dv = (bf16*)dv_;
+    o16.cs = rope_cos; o16.sn = rope_sin;
+    attn_bwd_tc(at, (const bf16*)q_, (const bf16*)k_, (const bf16*)v_, (const bf16*)mix_,
+                (const bf16*)dmix_, lse, delta, nullptr, nullptr, nullptr, s, launches, &o16);
+    dv_op = dv_;
+    ph_end(s);
+  } else {
+    attn_bwd_simt<Act>(at, q_, k_, v_, mix_, dmix_, lse, delta, dq, dk, dv, s, launches);
+    ph_end(s);
+    ph_begin("rope_bwd", s);
+    rope<float, Act>(dq, dq_, T, (int)S, H, hd, rope_cos, rope_sin, -1.f, s, launches);
+    rope<float, Act>(dk, dk_, T, (int)S, KV, hd, rope_cos, rope_sin, -1.f, s, launches);
+    if (f32) dv_op = (const Act*)dv;
+    else { convert<Act>(dv, dv_, T * kvd, s, launches); dv_op = dv_; }
+    ph_end(s);
+  }
   // d_xn = dq Wq^T + dk Wk^T + dv Wv^T (src/mixtral.rs:571-580)
   ph_begin("qkv_dgrad", s);
   {

@@ -45,6 +45,49 @@ __global__ void k_rmsnorm_fwd(const float* __restrict__ x, const T* __restrict__
   }
 }
 
+// Router tail for one token, run by one thread: logits z = sum of the
+// per-warp partials (+ bias), softmax (src/mixtral.rs:924-929), top-k by
+// (probability desc, index asc) and renormalisation (:931-939).
+__device__ void router_select(const float* lg, int nw, const float* bias, int E, int K,
+                              int64_t row, float* probs, int* top_i, float* top_p, float* top_w) {
+  float z[kMaxExperts], p[kMaxExperts];
+  float m = -INFINITY;
+  for (int e = 0; e < E; ++e) {
+    float v = 0.f;
+    for (int q = 0; q < nw; ++q) v += lg[q * kMaxExperts + e];
+    if (bias) v += bias[e];
+    z[e] = v;
+    m = fmaxf(m, v);
+  }
+  float s = 0.f;
+  for (int e = 0; e < E; ++e) p[e] = expf(z[e] - m);
+  for (int e = 0; e < E; ++e) s += p[e];
+  for (int e = 0; e < E; ++e) {
+    p[e] = p[e] / s;
+    probs[row * E + e] = p[e];
+  }
+  uint64_t taken = 0;
+  int idx[kMaxTopK];
+  float pk[kMaxTopK];
+  for (int k = 0; k < K; ++k) {
+    int best = -1;
+    for (int e = 0; e < E; ++e) {
+      if (taken >> e & 1) continue;
+      if (best < 0 || p[e] > p[best]) best = e;
+    }
+    taken |= 1ull << best;
+    idx[k] = best;
+    pk[k] = p[best];
+  }
+  float sk = 0.f;
+  for (int k = 0; k < K; ++k) sk += pk[k];
+  for (int k = 0; k < K; ++k) {
+    top_i[row * K + k] = idx[k];
+    top_p[row * K + k] = pk[k];
+    top_w[row * K + k] = pk[k] / sk;
+  }
+}
+
 // RMSNorm of the feed-forward input fused with the router (src/mixtral.rs:
 // 311-327, softmax :924-929, topk_renorm :931-939).  Router logits are
 // computed in fp32 from the fp32 normalised row (not from its rounded copy),
@@ -96,57 +139,215 @@ __global__ void k_rmsnorm_router(const float* __restrict__ x, const T* __restric
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const int nw = blockDim.x >> 5;
-    float z[kMaxExperts], p[kMaxExperts];
-    float m = -INFINITY;
-    for (int e = 0; e < E; ++e) {
-      float v = 0.f;
-      for (int q = 0; q < nw; ++q) v += lg[q * kMaxExperts + e];
-      if (bias) v += bias[e];
-      z[e] = v;
-      m = fmaxf(m, v);
+  if (threadIdx.x == 0)
+    router_select(lg, blockDim.x >> 5, bias, E, K, row, probs, top_i, top_p, top_w);
+}
+
+// ------------------------------------------- vectorised row kernels
+// The kernels below are the row kernels above with 4-wide accesses (float4
+// for fp32, 8-byte bf16 quads) and the row held in registers between the
+// reduction and the write.  The host launchers pick them when D % 4 == 0 and
+// every pointer is aligned for the wide access; the per-element arithmetic is
+// the same, only the order of the partial sums inside a row differs.
+
+// Sum of v over the CTA (blockDim.x a multiple of 32); every thread gets it.
+__device__ __forceinline__ float block_sum(float v, float* red /* [33] */) {
+  v = warp_sum(v);
+  __syncthreads();  // red may still be read from a previous call
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[32] = t;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// The router's E weights of model row i (wr is [D, E] row-major), E == 8.
+__device__ __forceinline__ void ld_row8(const float* p, float* v) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void ld_row8(const bf16* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[q]));
+    v[2 * q] = f.x;
+    v[2 * q + 1] = f.y;
+  }
+}
+
+// RMSNorm forward, NV quads per thread (256 threads, D / 4 <= 256 NV).
+template <typename T, int NV>
+__global__ void __launch_bounds__(256) k_rmsnorm_fwd_v(const float* __restrict__ x,
+                                                       const T* __restrict__ w, int D, float eps,
+                                                       T* __restrict__ y, float* __restrict__ inv,
+                                                       float* __restrict__ x_copy) {
+  const int64_t row = blockIdx.x;
+  const int D4 = D >> 2;
+  const float* xr = x + row * D;
+  __shared__ float red[33];
+  float4 xv[NV];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * 256;
+    if (i < D4) {
+      xv[j] = ld4(xr + 4 * i);
+      ss += xv[j].x * xv[j].x + xv[j].y * xv[j].y + xv[j].z * xv[j].z + xv[j].w * xv[j].w;
     }
-    float s = 0.f;
-    for (int e = 0; e < E; ++e) {
-      p[e] = expf(z[e] - m);
+  }
+  ss = block_sum(ss, red);
+  const float r = 1.0f / sqrtf(ss / (float)D + eps);
+  if (threadIdx.x == 0) inv[row] = r;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * 256;
+    if (i < D4) {
+      const float4 wv = ld4(w + 4 * i);
+      const float4 v = xv[j];
+      st4(y + row * D + 4 * i, make_float4(v.x * r * wv.x, v.y * r * wv.y, v.z * r * wv.z,
+                                           v.w * r * wv.w));
+      if (x_copy) st4(x_copy + row * D + 4 * i, v);
     }
-    for (int e = 0; e < E; ++e) s += p[e];
-    for (int e = 0; e < E; ++e) {
-      p[e] = p[e] / s;
-      probs[row * E + e] = p[e];
+  }
+}
+
+// RMSNorm of the feed-forward input fused with the router, NV quads per
+// thread; E8: the router has 8 experts and its rows are read 16 or 32
+// bytes at a time.
+template <typename T, int NV, bool E8>
+__global__ void __launch_bounds__(256) k_rmsnorm_router_v(
+    const float* __restrict__ x, const T* __restrict__ w, const T* __restrict__ wr,
+    const float* __restrict__ bias, int D, int E, int K, float eps, T* __restrict__ y,
+    float* __restrict__ inv, float* __restrict__ probs, int* __restrict__ top_i,
+    float* __restrict__ top_p, float* __restrict__ top_w) {
+  const int64_t row = blockIdx.x;
+  const int D4 = D >> 2;
+  const float* xr = x + row * D;
+  __shared__ float red[33];
+  __shared__ float lg[kMaxExperts * 8];  // per-warp partial logits (8 warps)
+  float4 xv[NV];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * 256;
+    if (i < D4) {
+      xv[j] = ld4(xr + 4 * i);
+      ss += xv[j].x * xv[j].x + xv[j].y * xv[j].y + xv[j].z * xv[j].z + xv[j].w * xv[j].w;
     }
-    uint64_t taken = 0;
-    int idx[kMaxTopK];
-    float pk[kMaxTopK];
-    for (int k = 0; k < K; ++k) {
-      int best = -1;
-      for (int e = 0; e < E; ++e) {
-        if (taken >> e & 1) continue;
-        if (best < 0 || p[e] > p[best]) best = e;
+  }
+  ss = block_sum(ss, red);
+  const float r = 1.0f / sqrtf(ss / (float)D + eps);
+  if (threadIdx.x == 0) inv[row] = r;
+  float part[kMaxExperts];
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) part[e] = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * 256;
+    if (i < D4) {
+      const float4 wv = ld4(w + 4 * i);
+      const float xn[4] = {xv[j].x * r * wv.x, xv[j].y * r * wv.y, xv[j].z * r * wv.z,
+                           xv[j].w * r * wv.w};
+      st4(y + row * D + 4 * i, make_float4(xn[0], xn[1], xn[2], xn[3]));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const T* wrow = wr + (int64_t)(4 * i + u) * E;
+        if (E8) {
+          float wv8[8];
+          ld_row8(wrow, wv8);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) part[e] += xn[u] * wv8[e];
+        } else {
+#pragma unroll
+          for (int e = 0; e < kMaxExperts; ++e)
+            if (e < E) part[e] += xn[u] * ld(&wrow[e]);
+        }
       }
-      taken |= 1ull << best;
-      idx[k] = best;
-      pk[k] = p[best];
     }
-    float sk = 0.f;
-    for (int k = 0; k < K; ++k) sk += pk[k];
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) {
+    if (e < E) {
+      float v = warp_sum(part[e]);
+      if (lane == 0) lg[warp * kMaxExperts + e] = v;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) router_select(lg, 8, bias, E, K, row, probs, top_i, top_p, top_w);
+}
+
+// Xp[r] = xn[row_token[r]] in 16-byte words (zero rows for padding).
+__global__ void k_gather_rows16(const uint4* __restrict__ src, const int* __restrict__ row_token,
+                                const int* __restrict__ seg_off, int E, int n16,
+                                uint4* __restrict__ dst) {
+  const int64_t r = blockIdx.x;
+  if (r >= seg_off[E]) return;
+  const int t = row_token[r];
+  for (int i = threadIdx.x; i < n16; i += blockDim.x)
+    dst[r * n16 + i] = t >= 0 ? src[(int64_t)t * n16 + i] : make_uint4(0u, 0u, 0u, 0u);
+}
+
+// dO[r] = row_w[r] * dy[row_token[r]], 4 elements per access.
+template <typename T>
+__global__ void k_gather_scale_rows_v(const float* __restrict__ src,
+                                      const int* __restrict__ row_token,
+                                      const float* __restrict__ row_w,
+                                      const int* __restrict__ seg_off, int E, int D,
+                                      T* __restrict__ dst) {
+  const int64_t r = blockIdx.x;
+  if (r >= seg_off[E]) return;
+  const int t = row_token[r];
+  const float w = t >= 0 ? row_w[r] : 0.f;
+  for (int i = threadIdx.x * 4; i < D; i += blockDim.x * 4) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (t >= 0) {
+      const float4 a = ld4(src + (int64_t)t * D + i);
+      v = make_float4(w * a.x, w * a.y, w * a.z, w * a.w);
+    }
+    st4(dst + r * D + i, v);
+  }
+}
+
+// y[t] = mid[t] + sum_k w_k * out[row(t,k)], 4 elements per access; the slot
+// sum is taken in slot order from zero, as in k_combine.
+__global__ void k_combine_v(const float* __restrict__ mid, const float* __restrict__ out,
+                            const int* __restrict__ slot_row, const float* __restrict__ top_w,
+                            int K, int D, float* __restrict__ y) {
+  const int64_t t = blockIdx.x;
+  __shared__ int64_t rows[kMaxTopK];
+  __shared__ float ws[kMaxTopK];
+  if (threadIdx.x < K) {
+    rows[threadIdx.x] = slot_row[t * K + threadIdx.x];
+    ws[threadIdx.x] = top_w[t * K + threadIdx.x];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x * 4; i < D; i += blockDim.x * 4) {
+    float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < K; ++k) {
-      top_i[row * K + k] = idx[k];
-      top_p[row * K + k] = pk[k];
-      top_w[row * K + k] = pk[k] / sk;
+      const float4 o = ld4(out + rows[k] * D + i);
+      m.x += ws[k] * o.x; m.y += ws[k] * o.y; m.z += ws[k] * o.z; m.w += ws[k] * o.w;
     }
+    const float4 a = ld4(mid + t * D + i);
+    st4(y + t * D + i, make_float4(a.x + m.x, a.y + m.y, a.z + m.z, a.w + m.w));
   }
 }
 
 // rmsnorm_bwd (src/mixtral.rs:696-723), input cotangent: one warp per row,
 // dx = r (dy*w - xhat * mean(dy*w*xhat)) (+ res), xhat = x r.  Rows are read
-// twice (the second pass hits L2), float4 when D % 128 == 0.
+// twice (the second pass hits L2), float4 when D % 128 == 0 and every
+// pointer is 16-byte (fp32) or 8-byte (bf16) aligned.
 template <typename T>
 __global__ void k_rmsnorm_bwd_rows(const float* __restrict__ dy, const float* __restrict__ x,
                                    const float* __restrict__ inv, const T* __restrict__ w,
                                    const float* __restrict__ res, int64_t rows, int D,
-                                   float* __restrict__ dx, T* __restrict__ dx_act) {
+                                   float* __restrict__ dx, T* __restrict__ dx_act, bool vec) {
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -154,13 +355,13 @@ __global__ void k_rmsnorm_bwd_rows(const float* __restrict__ dy, const float* __
   const float* xr = x + row * D;
   const float* gr = dy + row * D;
   float dot = 0.f;
-  const bool vec = (D & 127) == 0;
   if (vec) {
     for (int i = lane * 4; i < D; i += 128) {
-      const float4 xv = *reinterpret_cast<const float4*>(xr + i);
-      const float4 gv = *reinterpret_cast<const float4*>(gr + i);
-      dot += (gv.x * ld(&w[i])) * (xv.x * r) + (gv.y * ld(&w[i + 1])) * (xv.y * r) +
-             (gv.z * ld(&w[i + 2])) * (xv.z * r) + (gv.w * ld(&w[i + 3])) * (xv.w * r);
+      const float4 xv = ld4(xr + i);
+      const float4 gv = ld4(gr + i);
+      const float4 wv = ld4(w + i);
+      dot += (gv.x * wv.x) * (xv.x * r) + (gv.y * wv.y) * (xv.y * r) +
+             (gv.z * wv.z) * (xv.z * r) + (gv.w * wv.w) * (xv.w * r);
     }
   } else {
     for (int i = lane; i < D; i += 32) dot += (gr[i] * ld(&w[i])) * (xr[i] * r);
@@ -169,22 +370,20 @@ __global__ void k_rmsnorm_bwd_rows(const float* __restrict__ dy, const float* __
   const float mean = dot / (float)D;
   if (vec) {
     for (int i = lane * 4; i < D; i += 128) {
-      const float4 xv = *reinterpret_cast<const float4*>(xr + i);
-      const float4 gv = *reinterpret_cast<const float4*>(gr + i);
+      const float4 xv = ld4(xr + i);
+      const float4 gv = ld4(gr + i);
+      const float4 wv = ld4(w + i);
       float4 o;
-      o.x = r * (gv.x * ld(&w[i]) - (xv.x * r) * mean);
-      o.y = r * (gv.y * ld(&w[i + 1]) - (xv.y * r) * mean);
-      o.z = r * (gv.z * ld(&w[i + 2]) - (xv.z * r) * mean);
-      o.w = r * (gv.w * ld(&w[i + 3]) - (xv.w * r) * mean);
+      o.x = r * (gv.x * wv.x - (xv.x * r) * mean);
+      o.y = r * (gv.y * wv.y - (xv.y * r) * mean);
+      o.z = r * (gv.z * wv.z - (xv.z * r) * mean);
+      o.w = r * (gv.w * wv.w - (xv.w * r) * mean);
       if (res) {
-        const float4 rv = *reinterpret_cast<const float4*>(res + row * D + i);
+        const float4 rv = ld4(res + row * D + i);
         o.x += rv.x; o.y += rv.y; o.z += rv.z; o.w += rv.w;
       }
-      *reinterpret_cast<float4*>(dx + row * D + i) = o;
-      if (dx_act) {
-        T* da = dx_act + row * D + i;
-        st(&da[0], o.x); st(&da[1], o.y); st(&da[2], o.z); st(&da[3], o.w);
-      }
+      st4(dx + row * D + i, o);
+      if (dx_act) st4(dx_act + row * D + i, o);
     }
   } else {
     for (int i = lane; i < D; i += 32) {
@@ -476,6 +675,97 @@ __global__ void k_unpermute_router_dx(const float* __restrict__ dxp,
   }
 }
 
+// k_router_bwd with 4-wide dot products (D % 4 == 0, aligned rows).
+__global__ void k_router_bwd_v(const float* __restrict__ dy, const float* __restrict__ out,
+                               const int* __restrict__ slot_row, const int* __restrict__ top_i,
+                               const float* __restrict__ top_p, const float* __restrict__ top_w,
+                               const float* __restrict__ probs, int E, int K, int D,
+                               float* __restrict__ dz) {
+  const int64_t t = blockIdx.x;
+  __shared__ float red[kMaxTopK][32];
+  __shared__ float dv[kMaxTopK];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float acc[kMaxTopK];
+  int64_t rows[kMaxTopK];
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) {
+    acc[k] = 0.f;
+    rows[k] = k < K ? slot_row[t * K + k] : 0;
+  }
+  for (int i = threadIdx.x * 4; i < D; i += blockDim.x * 4) {
+    const float4 g = ld4(dy + t * D + i);
+#pragma unroll
+    for (int k = 0; k < kMaxTopK; ++k) {
+      if (k < K) {
+        const float4 o = ld4(out + rows[k] * D + i);
+        acc[k] += g.x * o.x + g.y * o.y + g.z * o.z + g.w * o.w;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) {
+    if (k < K) {
+      const float v = warp_sum(acc[k]);
+      if (lane == 0) red[k][warp] = v;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f, wdot = 0.f;
+    for (int k = 0; k < K; ++k) s += top_p[t * K + k];
+    for (int k = 0; k < K; ++k) {
+      float v = 0.f;
+      for (int q = 0; q < (int)(blockDim.x >> 5); ++q) v += red[k][q];
+      dv[k] = v;
+      wdot += v * top_w[t * K + k];
+    }
+    float dp[kMaxExperts];
+    for (int e = 0; e < E; ++e) dp[e] = 0.f;
+    for (int k = 0; k < K; ++k) dp[top_i[t * K + k]] = dv[k] / s - wdot / s;
+    float dot = 0.f;
+    for (int e = 0; e < E; ++e) dot += probs[t * E + e] * dp[e];
+    for (int e = 0; e < E; ++e) dz[t * E + e] = probs[t * E + e] * (dp[e] - dot);
+  }
+}
+
+// k_unpermute_router_dx with 4-wide accesses; E8: 8 experts, router rows
+// read 16 or 32 bytes at a time.
+template <typename T, bool E8>
+__global__ void k_unpermute_router_dx_v(const float* __restrict__ dxp,
+                                        const int* __restrict__ slot_row,
+                                        const float* __restrict__ dz, const T* __restrict__ wr,
+                                        int E, int K, int D, float* __restrict__ dxn) {
+  const int64_t t = blockIdx.x;
+  __shared__ float dzs[kMaxExperts];
+  __shared__ int64_t rows[kMaxTopK];
+  if (threadIdx.x < E) dzs[threadIdx.x] = dz[t * E + threadIdx.x];
+  if (threadIdx.x < K) rows[threadIdx.x] = slot_row[t * K + threadIdx.x];
+  __syncthreads();
+  for (int i = threadIdx.x * 4; i < D; i += blockDim.x * 4) {
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < K; ++k) {
+      const float4 v = ld4(dxp + rows[k] * D + i);
+      a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+    }
+    float rr[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const T* wrow = wr + (int64_t)(i + u) * E;
+      float acc = 0.f;
+      if (E8) {
+        float wv8[8];
+        ld_row8(wrow, wv8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc += dzs[e] * wv8[e];
+      } else {
+        for (int e = 0; e < E; ++e) acc += dzs[e] * ld(&wrow[e]);
+      }
+      rr[u] = acc;
+    }
+    st4(dxn + t * D + i, make_float4(a.x + rr[0], a.y + rr[1], a.z + rr[2], a.w + rr[3]));
+  }
+}
+
 // Router weight adjoint partials: part[c, i, e] = sum_{t in chunk c}
 // xn2[t,i] * dz[t,e] with xn2 recomputed in fp32 from (mid, inv, w).
 template <typename T>
@@ -582,10 +872,25 @@ static int grid_for(int64_t n, int block) {
   return (int)(g < cap ? (g > 0 ? g : 1) : cap);
 }
 
+// Quads per thread of the vectorised row kernels (256 threads): 1, 2, 4 or 8,
+// or 0 when D is not a multiple of 4 or too wide for registers.
+static int row_quads(int D) {
+  if (D % 4 != 0 || D > 4 * 256 * 8) return 0;
+  const int need = (int)ceil_div(D / 4, 256);
+  return need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : 8;
+}
+
 template <typename T>
 void rmsnorm_fwd(const float* x, const T* w, int64_t rows, int D, float eps, T* y, float* inv,
                  float* x_copy, cudaStream_t s, int64_t& launches) {
-  k_rmsnorm_fwd<T><<<(unsigned)rows, 256, 0, s>>>(x, w, D, eps, y, inv, x_copy);
+  const int nv = row_quads(D);
+  if (nv && aligned4(x) && aligned4(w) && aligned4(y) && (!x_copy || aligned4(x_copy))) {
+    auto k = nv == 1 ? k_rmsnorm_fwd_v<T, 1> : nv == 2 ? k_rmsnorm_fwd_v<T, 2>
+           : nv == 4 ? k_rmsnorm_fwd_v<T, 4> : k_rmsnorm_fwd_v<T, 8>;
+    k<<<(unsigned)rows, 256, 0, s>>>(x, w, D, eps, y, inv, x_copy);
+  } else {
+    k_rmsnorm_fwd<T><<<(unsigned)rows, 256, 0, s>>>(x, w, D, eps, y, inv, x_copy);
+  }
   DOP_LAUNCHED(launches);
 }
 
@@ -594,8 +899,20 @@ void rmsnorm_router(const float* x, const T* w, const T* wr, const float* bias, 
                     int D, int E, int K, float eps, T* y, float* inv, float* probs, int* top_i,
                     float* top_p, float* top_w, cudaStream_t s, int64_t& launches) {
   DOP_REQUIRE(E <= kMaxExperts && K <= kMaxTopK && K <= E, "experts/top_k out of range");
-  k_rmsnorm_router<T><<<(unsigned)rows, 256, 0, s>>>(x, w, wr, bias, D, E, K, eps, y, inv, probs,
-                                                     top_i, top_p, top_w);
+  const int nv = row_quads(D);
+  if (nv && aligned4(x) && aligned4(w) && aligned4(y)) {
+    const bool e8 = E == 8 && (uintptr_t)wr % 16 == 0;
+#define DOP_ROUTER_V(NV)                                                              \
+  (e8 ? k_rmsnorm_router_v<T, NV, true> : k_rmsnorm_router_v<T, NV, false>)
+    auto k = nv == 1 ? DOP_ROUTER_V(1) : nv == 2 ? DOP_ROUTER_V(2)
+           : nv == 4 ? DOP_ROUTER_V(4) : DOP_ROUTER_V(8);
+#undef DOP_ROUTER_V
+    k<<<(unsigned)rows, 256, 0, s>>>(x, w, wr, bias, D, E, K, eps, y, inv, probs, top_i, top_p,
+                                     top_w);
+  } else {
+    k_rmsnorm_router<T><<<(unsigned)rows, 256, 0, s>>>(x, w, wr, bias, D, E, K, eps, y, inv,
+                                                       probs, top_i, top_p, top_w);
+  }
   DOP_LAUNCHED(launches);
 }
 
@@ -603,8 +920,10 @@ template <typename T>
 void rmsnorm_bwd(const float* dy, const float* x, const float* inv, const T* w,
                  const float* res, int64_t rows, int D, float* dx, T* dx_act, float* dw_accum,
                  float* part_buf, int64_t part_cap, cudaStream_t s, int64_t& launches) {
+  const bool vec = D % 128 == 0 && aligned4(dy) && aligned4(x) && aligned4(w) &&
+                   (!res || aligned4(res)) && aligned4(dx) && (!dx_act || aligned4(dx_act));
   k_rmsnorm_bwd_rows<T><<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(dy, x, inv, w, res, rows, D,
-                                                                     dx, dx_act);
+                                                                     dx, dx_act, vec);
   DOP_LAUNCHED(launches);
   int64_t chunks = std::max<int64_t>(1, std::min<int64_t>(rows, 64));
   int rows_per_chunk = (int)ceil_div(rows, chunks);
@@ -653,7 +972,12 @@ void permute(const int* top_i, const float* top_w, int64_t T, int E, int K, int*
 template <typename T>
 void gather_rows(const T* src, const int* row_token, const int* seg_off, int E, int D,
                  int64_t rows_cap, T* dst, cudaStream_t s, int64_t& launches) {
-  k_gather_rows<T><<<(unsigned)rows_cap, 256, 0, s>>>(src, row_token, seg_off, E, D, dst);
+  const int64_t bytes = (int64_t)D * sizeof(T);
+  if (bytes % 16 == 0 && (uintptr_t)src % 16 == 0 && (uintptr_t)dst % 16 == 0)
+    k_gather_rows16<<<(unsigned)rows_cap, 128, 0, s>>>((const uint4*)src, row_token, seg_off, E,
+                                                        (int)(bytes / 16), (uint4*)dst);
+  else
+    k_gather_rows<T><<<(unsigned)rows_cap, 256, 0, s>>>(src, row_token, seg_off, E, D, dst);
   DOP_LAUNCHED(launches);
 }
 
@@ -661,8 +985,12 @@ template <typename T>
 void gather_scale_rows(const float* src, const int* row_token, const float* row_w,
                        const int* seg_off, int E, int D, int64_t rows_cap, T* dst, cudaStream_t s,
                        int64_t& launches) {
-  k_gather_scale_rows<T><<<(unsigned)rows_cap, 256, 0, s>>>(src, row_token, row_w, seg_off, E, D,
-                                                            dst);
+  if (D % 4 == 0 && aligned4(src) && aligned4(dst))
+    k_gather_scale_rows_v<T><<<(unsigned)rows_cap, 256, 0, s>>>(src, row_token, row_w, seg_off, E,
+                                                                D, dst);
+  else
+    k_gather_scale_rows<T><<<(unsigned)rows_cap, 256, 0, s>>>(src, row_token, row_w, seg_off, E,
+                                                              D, dst);
   DOP_LAUNCHED(launches);
 }
 
@@ -682,15 +1010,22 @@ void silu_mul_bwd(const float* dh, const T* g, const T* u, const int* seg_off, i
 
 void combine(const float* mid, const float* out, const int* slot_row, const float* top_w,
              int64_t T, int K, int D, float* y, cudaStream_t s, int64_t& launches) {
-  k_combine<<<(unsigned)T, 256, 0, s>>>(mid, out, slot_row, top_w, K, D, y);
+  if (D % 4 == 0 && aligned4(mid) && aligned4(out) && aligned4(y))
+    k_combine_v<<<(unsigned)T, 256, 0, s>>>(mid, out, slot_row, top_w, K, D, y);
+  else
+    k_combine<<<(unsigned)T, 256, 0, s>>>(mid, out, slot_row, top_w, K, D, y);
   DOP_LAUNCHED(launches);
 }
 
 void router_bwd(const float* dy, const float* out, const int* slot_row, const int* top_i,
                 const float* top_p, const float* top_w, const float* probs, int64_t Tn, int E,
                 int K, int D, float* dz, cudaStream_t s, int64_t& launches) {
-  k_router_bwd<<<(unsigned)Tn, 256, 0, s>>>(dy, out, slot_row, top_i, top_p, top_w, probs, E, K,
-                                            D, dz);
+  if (D % 4 == 0 && aligned4(dy) && aligned4(out))
+    k_router_bwd_v<<<(unsigned)Tn, 256, 0, s>>>(dy, out, slot_row, top_i, top_p, top_w, probs, E,
+                                                K, D, dz);
+  else
+    k_router_bwd<<<(unsigned)Tn, 256, 0, s>>>(dy, out, slot_row, top_i, top_p, top_w, probs, E, K,
+                                              D, dz);
   DOP_LAUNCHED(launches);
 }
 
@@ -698,7 +1033,16 @@ template <typename T>
 void unpermute_router_dx(const float* dxp, const int* slot_row, const float* dz, const T* wr,
                          int64_t Tn, int E, int K, int D, float* dxn, cudaStream_t s,
                          int64_t& launches) {
-  k_unpermute_router_dx<T><<<(unsigned)Tn, 256, 0, s>>>(dxp, slot_row, dz, wr, E, K, D, dxn);
+  if (D % 4 == 0 && aligned4(dxp) && aligned4(dxn)) {
+    if (E == 8 && (uintptr_t)wr % 16 == 0)
+      k_unpermute_router_dx_v<T, true><<<(unsigned)Tn, 256, 0, s>>>(dxp, slot_row, dz, wr, E, K, D,
+                                                                    dxn);
+    else
+      k_unpermute_router_dx_v<T, false><<<(unsigned)Tn, 256, 0, s>>>(dxp, slot_row, dz, wr, E, K,
+                                                                     D, dxn);
+  } else {
+    k_unpermute_router_dx<T><<<(unsigned)Tn, 256, 0, s>>>(dxp, slot_row, dz, wr, E, K, D, dxn);
+  }
   DOP_LAUNCHED(launches);
 }
 

@@ -142,9 +142,17 @@ void attn_fwd_simt(const Attn& a, const T* q, const T* k, const T* v, T* o, floa
 // Tensor-core (tcgen05) flash attention for bf16, head_dim 128 (attn_tc.cu).
 void attn_fwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, bf16* o, float* lse,
                  cudaStream_t s, int64_t& launches);
+// Optional bf16 outputs of attn_bwd_tc: dq, dk, dv rounded once from the fp32
+// accumulators, dq and dk rotated back by the RoPE adjoint (tables cs, sn of
+// [S][hd/2], position = index within the sequence) when cs is set.  With
+// them the fp32 dq, dk, dv are not written.
+struct AttnBwdBf16 {
+  bf16* dq = nullptr; bf16* dk = nullptr; bf16* dv = nullptr;
+  const float* cs = nullptr; const float* sn = nullptr;
+};
 void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, const bf16* o,
                  const bf16* dout, const float* lse, float* delta, float* dq, float* dk, float* dv,
-                 cudaStream_t s, int64_t& launches);
+                 cudaStream_t s, int64_t& launches, const AttnBwdBf16* out16 = nullptr);
 template <typename T>
 void attn_bwd_simt(const Attn& a, const T* q, const T* k, const T* v, const T* o, const T* dout,
                    const float* lse, float* delta, float* dq, float* dk, float* dv,
