@@ -248,7 +248,14 @@ def run_ours(a):
     T = batch * seq
     cfg, ll, P = make_params(wl["cfg"], wl["precision"], seed=0, device=dev)  # same weights on every rank
     prec = DOP_BF16 if wl["precision"] == "bf16" else DOP_F32
-    blk = Block(cfg, batch, seq, prec)
+    # expert parallel when the experts split over the ranks (the contract's
+    # partitioning of the Mixtral block), else data parallel
+    ep = world > 1 and a.parallel != "dp" and parallel.ep_mode(world, cfg.experts, prec == DOP_BF16)
+    if a.parallel == "ep" and world > 1 and not ep:
+        raise SystemExit(f"--parallel ep needs bf16 and experts % {world} == 0")
+    blk = Block(cfg, batch, seq, prec, ep=(rank, world) if ep else None)
+    if ep:
+        parallel.connect_expert_parallel(blk, device=dev)
     bias = None
     if wl["skew"]:
         bias = zipf_bias(cfg.experts).to(dev)
@@ -261,17 +268,21 @@ def run_ours(a):
     dP = torch.zeros(ll.total, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
     # data parallel: the experts' adjoints (the slice from gate0 on) are
-    # reduced on a side stream while the attention half of the backward runs
-    side = torch.cuda.Stream(dev) if world > 1 else None
+    # reduced on a side stream while the attention half of the backward runs.
+    # Expert parallel: each rank's experts' adjoints are complete on that
+    # rank; only the shared slice is summed.
+    side = torch.cuda.Stream(dev) if world > 1 and not ep else None
     if side is not None:
         blk.set_adjoint_stream(side)
     x0 = ll.gate0
 
     def reduce_dp():
-        with torch.cuda.stream(side):
-            parallel.reduce_adjoint(dP[x0:])
+        if side is not None:
+            with torch.cuda.stream(side):
+                parallel.reduce_adjoint(dP[x0:])
         parallel.reduce_adjoint(dP[:x0])
-        stream.wait_stream(side)
+        if side is not None:
+            stream.wait_stream(side)
 
     def step():
         dP.zero_()
@@ -397,8 +408,12 @@ def run_ours(a):
             "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) x and dy)",
             "config": {"workload": a.workload, "batch_per_gpu": batch, "seq": seq,
                        "global_batch": batch * world, **wl["cfg"],
-                       "parallelism": (f"dp{world}, expert adjoints reduced during the "
-                                       "attention backward") if world > 1 else "single",
+                       "parallelism": ("single" if world == 1 else
+                                       f"ep{world} ({cfg.experts // world} experts per rank, "
+                                       "exchange over NVLink peer reads, shared adjoint "
+                                       "all-reduced)" if ep else
+                                       f"dp{world}, expert adjoints reduced during the "
+                                       "attention backward"),
                        "l2": "inputs larger than L2 (x, dy are 4 B x T x D each)"},
             "tflops": flops / (ms / 1e3) / 1e12,
             "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / peak,
@@ -415,7 +430,11 @@ def run_ours(a):
         }
         print(json.dumps(out), flush=True)
     if world > 1:
+        # every rank's kernels are done before any rank unmaps or frees a
+        # workspace its peers read
+        torch.cuda.synchronize(dev)
         dist.barrier()
+        blk.close()
         dist.destroy_process_group()
 
 
@@ -427,6 +446,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--parallel", default="auto", choices=["auto", "dp", "ep"],
+                    help="N > 1: expert parallel (auto when the experts split evenly over "
+                         "the ranks, bf16) or data parallel")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="profiler run: no CPU baseline, no e2e, warm-up may be < 3")

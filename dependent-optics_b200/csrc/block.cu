@@ -43,8 +43,9 @@ struct Carver {
 };
 }  // namespace
 
-Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision)
-    : cfg(c), B(batch), S(seq), T(batch * seq), prec(precision) {
+Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision, int rank,
+             int world)
+    : cfg(c), B(batch), S(seq), T(batch * seq), prec(precision), ep_rank(rank), ep_world(world) {
   DOP_REQUIRE(batch >= 1 && seq >= 1, "batch and seq must be >= 1");
   DOP_REQUIRE(c.dim >= 1 && c.heads >= 1 && c.kv_heads >= 1 && c.head_dim >= 2,
               "bad model widths");
@@ -64,11 +65,22 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
                 "the bf16 lens needs dim, heads*head_dim and kv_heads*head_dim multiples of 8");
     DOP_REQUIRE(c.intermediate % 32 == 0, "the bf16 lens needs intermediate % 32 == 0");
   }
+  DOP_REQUIRE(world >= 1 && world <= kEpMaxWorld && rank >= 0 && rank < world,
+              "expert-parallel rank/world out of range");
+  if (world > 1) {
+    DOP_REQUIRE(precision == DOP_BF16, "expert parallelism runs the bf16 lens");
+    DOP_REQUIRE(c.experts % world == 0, "experts must be a multiple of the expert-parallel world");
+  }
   off = layer_offsets(c);
   const int64_t D = c.dim, E = c.experts, K = c.top_k, I = c.intermediate;
   const int64_t qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim;
   rows_cap = round_up(T * K + E * (kRowAlign - 1), kRowAlign);
   max_tiles = (int)(rows_cap / kRowAlign);
+  const bool ep = world > 1;
+  ep_local = (int)(E / world);
+  recv_cap = ep ? world * rows_cap : 0;
+  const int recv_tiles = (int)(recv_cap / kRowAlign);
+  const int64_t xe = ep ? 0 : 1;  // the local expert buffers exist without EP only
   const size_t a = prec == DOP_F32 ? 4 : 2;  // activation element size
   const int64_t chunks = ceil_div(T * K, kPermChunk);
   part_cap = std::max<int64_t>((int64_t)sm_count() * 4 * D, 64 * D * E);
@@ -98,17 +110,17 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
     cv.take(v, a * T * kvd, base_);
     cv.take(mix, a * T * qd, base_);
     cv.take(xn2, a * T * D, base_);
-    cv.take(xp, a * rows_cap * D, base_);
-    cv.take(g, a * rows_cap * I, base_);
-    cv.take(u, a * rows_cap * I, base_);
-    cv.take(h, a * rows_cap * I, base_);
+    cv.take(xp, xe * a * rows_cap * D, base_);
+    cv.take(g, xe * a * rows_cap * I, base_);
+    cv.take(u, xe * a * rows_cap * I, base_);
+    cv.take(h, xe * a * rows_cap * I, base_);
     cv.take(qpre, 4 * T * qd, base_);
     cv.take(kpre, 4 * T * kvd, base_);
     cv.take(rope_cos, 4 * S * (c.head_dim / 2), base_);
     cv.take(rope_sin, 4 * S * (c.head_dim / 2), base_);
     cv.take(dz, 4 * T * E, base_);
     cv.take(dh, prec == DOP_F32 ? 4 * rows_cap * I : 0, base_);
-    cv.take(dxp, 4 * rows_cap * D, base_);
+    cv.take(dxp, xe * 4 * rows_cap * D, base_);
     cv.take(dxn2, 4 * T * D, base_);
     cv.take(dmid, 4 * T * D, base_);
     cv.take(dxn, 4 * T * D, base_);
@@ -118,13 +130,28 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
     cv.take(delta, 4 * T * c.heads, base_);
     cv.take(part, 4 * part_cap, base_);
     cv.take(dO, a * rows_cap * D, base_);
-    cv.take(dg, a * rows_cap * I, base_);
-    cv.take(du, a * rows_cap * I, base_);
+    cv.take(dg, xe * a * rows_cap * I, base_);
+    cv.take(du, xe * a * rows_cap * I, base_);
     cv.take(dmid_a, a * T * D, base_);
     cv.take(dmix, a * T * qd, base_);
     cv.take(dq_a, a * T * qd, base_);
     cv.take(dk_a, a * T * kvd, base_);
     cv.take(dv_a, a * T * kvd, base_);
+    if (ep) {
+      cv.take(ep_flags, 4 * kEpBarriers * kEpMaxWorld, base_);
+      cv.take(send_off, 4 * E, base_);
+      cv.take(recv_seg_off, 4 * (ep_local + 1), base_);
+      cv.take(recv_tile_expert, 4 * recv_tiles, base_);
+      cv.take(recv_tile_src, 4 * recv_tiles, base_);
+      cv.take(recv_tile_row0, 4 * recv_tiles, base_);
+      cv.take(xr, 2 * recv_cap * D, base_);
+      cv.take(gr, 2 * recv_cap * I, base_);
+      cv.take(ur, 2 * recv_cap * I, base_);
+      cv.take(hr, 2 * recv_cap * I, base_);
+      cv.take(dOr, 2 * recv_cap * D, base_);
+      cv.take(outr, 4 * recv_cap * D, base_);
+      cv.take(dxpr, 4 * recv_cap * D, base_);
+    }
     return cv.at;
   };
   bytes = carve(nullptr);
@@ -135,18 +162,150 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
                                  cudaGetErrorString(e));
   }
   carve(base);
+  if (ep) {
+    DOP_CHECK_CUDA(cudaMemset(ep_flags, 0, 4 * kEpBarriers * kEpMaxWorld));
+    ep_peer_base.assign(world, nullptr);
+    ep_peer_base[rank] = base;
+  }
   // RoPE table (positions 0..S-1) once per handle.
   rope_table((int)S, (int)c.head_dim, c.rope_theta, rope_cos, rope_sin, 0, launches);
   DOP_CHECK_CUDA(cudaStreamSynchronize(0));
 }
 
 Block::~Block() {
+  for (int r = 0; r < (int)ep_peer_base.size(); ++r)
+    if (r != ep_rank && ep_peer_base[r]) cudaIpcCloseMemHandle(ep_peer_base[r]);
+  if (ep_peers_dev) cudaFree(ep_peers_dev);
   if (expert_adjoint_done) cudaEventDestroy(expert_adjoint_done);
   for (auto& p : phases) {
     cudaEventDestroy(p.a);
     cudaEventDestroy(p.b);
   }
   if (base) cudaFree(base);
+}
+
+// ------------------------------------------------------ expert parallelism
+EpView Block::ep_view() const {
+  EpView v;
+  v.rank = ep_rank; v.world = ep_world; v.local = ep_local;
+  v.recv_tiles = (int)(recv_cap / kRowAlign);
+  v.recv_cap = recv_cap;
+  v.peers = ep_peers_dev; v.flags = ep_flags;
+  v.seg_off = seg_off; v.row_token = row_token; v.send_off = send_off;
+  v.recv_seg_off = recv_seg_off; v.recv_tile_expert = recv_tile_expert;
+  v.recv_tile_src = recv_tile_src; v.recv_tile_row0 = recv_tile_row0;
+  v.xr = (bf16*)xr; v.outr = outr; v.dxpr = dxpr;
+  return v;
+}
+
+void Block::ep_connect(const cudaIpcMemHandle_t* handles) {
+  DOP_REQUIRE(ep_world > 1, "not an expert-parallel block");
+  DOP_REQUIRE(!ep_peers_dev, "expert-parallel block already connected");
+  for (int r = 0; r < ep_world; ++r) {
+    if (r == ep_rank) continue;
+    void* p = nullptr;
+    DOP_CHECK_CUDA(cudaIpcOpenMemHandle(&p, handles[r], cudaIpcMemLazyEnablePeerAccess));
+    ep_peer_base[r] = (char*)p;
+  }
+  DOP_CHECK_CUDA(cudaMalloc(&ep_peers_dev, sizeof(char*) * ep_world));
+  DOP_CHECK_CUDA(cudaMemcpy(ep_peers_dev, ep_peer_base.data(), sizeof(char*) * ep_world,
+                            cudaMemcpyHostToDevice));
+}
+
+void Block::ep_barrier_next(int k, cudaStream_t s) {
+  DOP_REQUIRE(ep_peers_dev, "expert-parallel block is not connected (dop_block_ep_connect)");
+  ep_barrier(ep_view(), k, ++ep_epoch, s, launches);
+}
+
+// Forward experts of an expert-parallel block, after the permutation:
+// gather the receive rows from the sources, gate/up (SwiGLU) and down over
+// this rank's experts, then combine the owners' outputs into y.
+void Block::ep_fwd_experts(const bf16* P, float* y, cudaStream_t s) {
+  const int64_t D = cfg.dim, I = cfg.intermediate, K = cfg.top_k;
+  const int64_t ex0 = (int64_t)ep_rank * ep_local * off.expert_stride;  // first local expert
+  const EpView v = ep_view();
+  ph_begin("ep_dispatch", s);
+  ep_barrier_next(0, s);  // every rank's xn2, row_token, seg_off are written
+  ep_layout(v, (int)cfg.experts, s, launches);
+  ep_gather_tokens(v, (const bf16*)xn2, (int)D, s, launches);
+  ph_end(s);
+  ph_begin("expert_gate_up", s);
+  {
+    Gemm gg; gg.M = recv_cap; gg.N = I; gg.K = D; gg.A = xr; gg.lda = D;
+    gg.B = P + off.gate0 + ex0; gg.ldb = I; gg.C = gr; gg.ldc = I; gg.c_f32 = false;
+    gg.group = 1; gg.seg_off = recv_seg_off; gg.tile_expert = recv_tile_expert; gg.G = ep_local;
+    gg.b_gs = off.expert_stride;
+    TcEpilogue te; te.kind = kTcSwiGLU; te.up_B = P + off.up0 + ex0;
+    te.g_out = (bf16*)gr; te.u_out = (bf16*)ur; te.h_out = (bf16*)hr; te.ldg = I;
+    gemm_tc(gg, nullptr, 0, te, s, launches);
+  }
+  ph_end(s);
+  ph_begin("expert_down", s);
+  {
+    Gemm gd; gd.M = recv_cap; gd.N = D; gd.K = I; gd.A = hr; gd.lda = I;
+    gd.B = P + off.down0 + ex0; gd.ldb = D; gd.C = outr; gd.ldc = D;
+    gd.group = 1; gd.seg_off = recv_seg_off; gd.tile_expert = recv_tile_expert; gd.G = ep_local;
+    gd.b_gs = off.expert_stride;
+    gemm<bf16>(gd, s);
+  }
+  ph_end(s);
+  ph_begin("combine", s);
+  ep_barrier_next(1, s);  // every owner's expert outputs are written
+  ep_combine(v, mid, top_i, slot_row, top_w, T, (int)K, (int)D, out, y, s, launches);
+  ph_end(s);
+}
+
+// Backward experts of an expert-parallel block, after the output cotangent
+// rows dO are written: gather them at the owners, dH with the SwiGLU
+// adjoint, this rank's expert weight adjoints, and dXp for the sources.
+void Block::ep_bwd_experts(const bf16* P, float* dP, cudaStream_t s) {
+  const int64_t D = cfg.dim, I = cfg.intermediate;
+  const int64_t ex0 = (int64_t)ep_rank * ep_local * off.expert_stride;
+  const EpView v = ep_view();
+  ph_begin("ep_dispatch_bwd", s);
+  ep_barrier_next(2, s);  // every rank's dO is written
+  ep_gather_rows(v, (const bf16*)dO, (bf16*)dOr, (int)D, s, launches);
+  ph_end(s);
+  ph_begin("expert_dh", s);
+  {
+    Gemm g1; g1.M = recv_cap; g1.N = I; g1.K = D; g1.A = dOr; g1.lda = D;
+    g1.B = P + off.down0 + ex0; g1.ldb = D; g1.b_t = true; g1.C = dh; g1.ldc = I;
+    g1.group = 1; g1.seg_off = recv_seg_off; g1.tile_expert = recv_tile_expert; g1.G = ep_local;
+    g1.b_gs = off.expert_stride;
+    // dg, du overwrite g, u in place (each element is read before it is written)
+    TcEpilogue te; te.kind = kTcSwiGLUBwd; te.g_in = (const bf16*)gr; te.u_in = (const bf16*)ur;
+    te.dg_out = (bf16*)gr; te.du_out = (bf16*)ur; te.ldg = I;
+    gemm_tc(g1, nullptr, 0, te, s, launches);
+  }
+  ph_end(s);
+  ph_begin("expert_dw_down", s);
+  {
+    Gemm g2; g2.M = I; g2.N = D; g2.K = recv_cap; g2.A = hr; g2.lda = I; g2.a_t = true;
+    g2.B = dOr; g2.ldb = D; g2.C = dP + off.down0 + ex0; g2.ldc = D; g2.epi = Epi::Accum;
+    g2.group = 2; g2.seg_off = recv_seg_off; g2.G = ep_local; g2.c_gs = off.expert_stride;
+    gemm<bf16>(g2, s);
+  }
+  ph_end(s);
+  ph_begin("expert_dx", s);
+  {
+    Gemm g3; g3.M = recv_cap; g3.N = D; g3.K = I; g3.A = gr; g3.lda = I;
+    g3.B = P + off.gate0 + ex0; g3.ldb = I; g3.b_t = true; g3.C = dxpr; g3.ldc = D;
+    g3.group = 1; g3.seg_off = recv_seg_off; g3.tile_expert = recv_tile_expert; g3.G = ep_local;
+    g3.b_gs = off.expert_stride;
+    GemmPart up{ur, I, P + off.up0 + ex0, I, I};
+    gemm<bf16>(g3, s, &up, 1);
+  }
+  ph_end(s);
+  ph_begin("expert_dw_gate_up", s);
+  {
+    Gemm g5; g5.M = D; g5.N = I; g5.K = recv_cap; g5.A = xr; g5.lda = D; g5.a_t = true;
+    g5.B = gr; g5.ldb = I; g5.C = dP + off.gate0 + ex0; g5.ldc = I; g5.epi = Epi::Accum;
+    g5.group = 2; g5.seg_off = recv_seg_off; g5.G = ep_local; g5.c_gs = off.expert_stride;
+    gemm<bf16>(g5, s);
+    Gemm g6 = g5; g6.B = ur; g6.C = dP + off.up0 + ex0;
+    gemm<bf16>(g6, s);
+  }
+  ph_end(s);
 }
 
 void Block::ph_begin(const char* name, cudaStream_t s) {
@@ -261,6 +420,13 @@ void Block::fwd(const Act* P, const float* x, float* y, cudaStream_t s) {
   ph_begin("permute", s);
   permute(top_i, top_w, T, (int)E, (int)K, chunk_counts, seg_off, tile_expert, max_tiles,
           slot_row, row_token, row_w, rows_cap, s, launches);
+  if constexpr (std::is_same<Act, bf16>::value) {
+    if (ep_world > 1) {  // the owners gather the rows themselves
+      ph_end(s);
+      ep_fwd_experts(P, y, s);
+      return;
+    }
+  }
   gather_rows<Act>(xn2_, row_token, seg_off, (int)E, (int)D, rows_cap, xp_, s, launches);
   ph_end(s);
   ph_begin("expert_gate_up", s);
@@ -317,56 +483,65 @@ void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_
              launches);
   gather_scale_rows<Act>(dy, row_token, row_w, seg_off, (int)E, (int)D, rows_cap, dO_, s, launches);
   ph_end(s);
-  // dH = dO Wd^T (Wd_e is [I, D]) and the SwiGLU adjoint (src/mixtral.rs:478-486)
-  ph_begin("expert_dh", s);
-  {
-    Gemm g1; g1.M = rows_cap; g1.N = I; g1.K = D; g1.A = dO_; g1.lda = D;
-    g1.B = P + off.down0; g1.ldb = D; g1.b_t = true; g1.C = dh; g1.ldc = I;
-    g1.group = 1; g1.seg_off = seg_off; g1.tile_expert = tile_expert; g1.G = (int)E;
-    g1.b_gs = off.expert_stride;
-    if (!f32) {
-      TcEpilogue te; te.kind = kTcSwiGLUBwd; te.g_in = (const bf16*)g_; te.u_in = (const bf16*)u_;
-      te.dg_out = (bf16*)dg_; te.du_out = (bf16*)du_; te.ldg = I;
-      gemm_tc(g1, nullptr, 0, te, s, launches);
-    } else {
-      gemm<Act>(g1, s);
-      ph_end(s);
-      ph_begin("swiglu_bwd", s);
-      silu_mul_bwd<Act>(dh, g_, u_, seg_off, (int)E, I, rows_cap, dg_, du_, s, launches);
+  bool ep = false;
+  if constexpr (std::is_same<Act, bf16>::value) {
+    if (ep_world > 1) {
+      ep_bwd_experts(P, dP, s);
+      ep = true;
     }
   }
-  ph_end(s);
-  // dWd_e += H^T dO over expert e's rows (src/mixtral.rs:478-480)
-  ph_begin("expert_dw_down", s);
-  {
-    Gemm g2; g2.M = I; g2.N = D; g2.K = rows_cap; g2.A = h_; g2.lda = I; g2.a_t = true;
-    g2.B = dO_; g2.ldb = D; g2.C = dP + off.down0; g2.ldc = D; g2.epi = Epi::Accum;
-    g2.group = 2; g2.seg_off = seg_off; g2.G = (int)E; g2.c_gs = off.expert_stride;
-    gemm<Act>(g2, s);
+  if (!ep) {
+    // dH = dO Wd^T (Wd_e is [I, D]) and the SwiGLU adjoint (src/mixtral.rs:478-486)
+    ph_begin("expert_dh", s);
+    {
+      Gemm g1; g1.M = rows_cap; g1.N = I; g1.K = D; g1.A = dO_; g1.lda = D;
+      g1.B = P + off.down0; g1.ldb = D; g1.b_t = true; g1.C = dh; g1.ldc = I;
+      g1.group = 1; g1.seg_off = seg_off; g1.tile_expert = tile_expert; g1.G = (int)E;
+      g1.b_gs = off.expert_stride;
+      if (!f32) {
+        TcEpilogue te; te.kind = kTcSwiGLUBwd; te.g_in = (const bf16*)g_; te.u_in = (const bf16*)u_;
+        te.dg_out = (bf16*)dg_; te.du_out = (bf16*)du_; te.ldg = I;
+        gemm_tc(g1, nullptr, 0, te, s, launches);
+      } else {
+        gemm<Act>(g1, s);
+        ph_end(s);
+        ph_begin("swiglu_bwd", s);
+        silu_mul_bwd<Act>(dh, g_, u_, seg_off, (int)E, I, rows_cap, dg_, du_, s, launches);
+      }
+    }
+    ph_end(s);
+    // dWd_e += H^T dO over expert e's rows (src/mixtral.rs:478-480)
+    ph_begin("expert_dw_down", s);
+    {
+      Gemm g2; g2.M = I; g2.N = D; g2.K = rows_cap; g2.A = h_; g2.lda = I; g2.a_t = true;
+      g2.B = dO_; g2.ldb = D; g2.C = dP + off.down0; g2.ldc = D; g2.epi = Epi::Accum;
+      g2.group = 2; g2.seg_off = seg_off; g2.G = (int)E; g2.c_gs = off.expert_stride;
+      gemm<Act>(g2, s);
+    }
+    ph_end(s);
+    // dXp = dG Wg^T + dU Wu^T (Wg_e, Wu_e are [D, I]; src/mixtral.rs:488-516)
+    ph_begin("expert_dx", s);
+    {
+      Gemm g3; g3.M = rows_cap; g3.N = D; g3.K = I; g3.A = dg_; g3.lda = I;
+      g3.B = P + off.gate0; g3.ldb = I; g3.b_t = true; g3.C = dxp; g3.ldc = D;
+      g3.group = 1; g3.seg_off = seg_off; g3.tile_expert = tile_expert; g3.G = (int)E;
+      g3.b_gs = off.expert_stride;
+      GemmPart up{du_, I, P + off.up0, I, I};
+      gemm<Act>(g3, s, &up, 1);
+    }
+    ph_end(s);
+    // dWg_e += Xp^T dG, dWu_e += Xp^T dU
+    ph_begin("expert_dw_gate_up", s);
+    {
+      Gemm g5; g5.M = D; g5.N = I; g5.K = rows_cap; g5.A = xp_; g5.lda = D; g5.a_t = true;
+      g5.B = dg_; g5.ldb = I; g5.C = dP + off.gate0; g5.ldc = I; g5.epi = Epi::Accum;
+      g5.group = 2; g5.seg_off = seg_off; g5.G = (int)E; g5.c_gs = off.expert_stride;
+      gemm<Act>(g5, s);
+      Gemm g6 = g5; g6.B = du_; g6.C = dP + off.up0;
+      gemm<Act>(g6, s);
+    }
+    ph_end(s);
   }
-  ph_end(s);
-  // dXp = dG Wg^T + dU Wu^T (Wg_e, Wu_e are [D, I]; src/mixtral.rs:488-516)
-  ph_begin("expert_dx", s);
-  {
-    Gemm g3; g3.M = rows_cap; g3.N = D; g3.K = I; g3.A = dg_; g3.lda = I;
-    g3.B = P + off.gate0; g3.ldb = I; g3.b_t = true; g3.C = dxp; g3.ldc = D;
-    g3.group = 1; g3.seg_off = seg_off; g3.tile_expert = tile_expert; g3.G = (int)E;
-    g3.b_gs = off.expert_stride;
-    GemmPart up{du_, I, P + off.up0, I, I};
-    gemm<Act>(g3, s, &up, 1);
-  }
-  ph_end(s);
-  // dWg_e += Xp^T dG, dWu_e += Xp^T dU
-  ph_begin("expert_dw_gate_up", s);
-  {
-    Gemm g5; g5.M = D; g5.N = I; g5.K = rows_cap; g5.A = xp_; g5.lda = D; g5.a_t = true;
-    g5.B = dg_; g5.ldb = I; g5.C = dP + off.gate0; g5.ldc = I; g5.epi = Epi::Accum;
-    g5.group = 2; g5.seg_off = seg_off; g5.G = (int)E; g5.c_gs = off.expert_stride;
-    gemm<Act>(g5, s);
-    Gemm g6 = g5; g6.B = du_; g6.C = dP + off.up0;
-    gemm<Act>(g6, s);
-  }
-  ph_end(s);
   if (adjoint_stream) {  // the experts' adjoints are final from here on
     if (!expert_adjoint_done)
       DOP_CHECK_CUDA(cudaEventCreateWithFlags(&expert_adjoint_done, cudaEventDisableTiming));
@@ -375,8 +550,16 @@ void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_
   }
   // d_xn2 = sum_k dXp[row(t,k)] + dz Wr^T; router weight adjoint
   ph_begin("unpermute_router", s);
-  unpermute_router_dx<Act>(dxp, slot_row, dz, P + off.router, T, (int)E, (int)K, (int)D, dxn2, s,
-                           launches);
+  if (ep) {
+    if constexpr (std::is_same<Act, bf16>::value) {
+      ep_barrier_next(3, s);  // every owner's dXp is written
+      ep_unpermute_router_dx<bf16>(ep_view(), top_i, slot_row, dz, P + off.router, T, (int)E,
+                                   (int)K, (int)D, dxn2, s, launches);
+    }
+  } else {
+    unpermute_router_dx<Act>(dxp, slot_row, dz, P + off.router, T, (int)E, (int)K, (int)D, dxn2, s,
+                             launches);
+  }
   router_dw<Act>(mid, inv2, P + off.ffn_norm, dz, T, (int)D, (int)E, dP + off.router, part,
                  part_cap, s, launches);
   ph_end(s);

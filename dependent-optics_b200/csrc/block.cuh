@@ -5,6 +5,7 @@
 #include "../../include/dop.h"
 #include <vector>
 
+#include "ep.cuh"
 #include "kernels.cuh"
 
 namespace dop {
@@ -45,6 +46,27 @@ struct Block {
   int64_t part_cap;
   void *dO, *dg, *du, *dmid_a, *dmix, *dq_a, *dk_a, *dv_a;
 
+  // expert parallelism (ep_world > 1, bf16 only; ep.cu): this rank owns
+  // experts [ep_rank * ep_local, (ep_rank + 1) * ep_local) and holds the
+  // receive rows of every rank routed to them (capacity recv_cap =
+  // ep_world * rows_cap, the most any routing can send).  The receive
+  // buffers of g and u are reused for dg and du (the SwiGLU adjoint reads
+  // each element before it writes it).
+  int ep_rank = 0, ep_world = 1, ep_local = 0;
+  int64_t recv_cap = 0;
+  unsigned ep_epoch = 0;
+  std::vector<char*> ep_peer_base;  // workspace bases as mapped here, [ep_world]
+  char** ep_peers_dev = nullptr;    // device copy of ep_peer_base
+  unsigned* ep_flags = nullptr;
+  int *send_off = nullptr, *recv_seg_off = nullptr, *recv_tile_expert = nullptr;
+  int *recv_tile_src = nullptr, *recv_tile_row0 = nullptr;
+  void *xr = nullptr, *gr = nullptr, *ur = nullptr, *hr = nullptr, *dOr = nullptr;
+  float *outr = nullptr, *dxpr = nullptr;
+  EpView ep_view() const;
+  void ep_barrier_next(int k, cudaStream_t s);
+  // Map the peers' workspaces (handles in rank order; own entry ignored).
+  void ep_connect(const cudaIpcMemHandle_t* handles);
+
   // per-phase CUDA-event timing (dop_block_set_timing)
   struct Phase { const char* name; cudaEvent_t a, b; };
   bool timing = false;
@@ -54,7 +76,8 @@ struct Block {
   void ph_begin(const char* name, cudaStream_t s);
   void ph_end(cudaStream_t s);
 
-  Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision);
+  Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision, int rank = 0,
+        int world = 1);
   ~Block();
   void forward(const void* params, const float* x, float* y, cudaStream_t s);
   void backward(const void* params, const float* dy, float* dx, float* dparams, cudaStream_t s);
@@ -64,6 +87,8 @@ struct Block {
   template <typename Act> void bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_t s);
   template <typename Act>
   void gemm(const Gemm& g, cudaStream_t s, const GemmPart* extra = nullptr, int n_extra = 0);
+  void ep_fwd_experts(const bf16* P, float* y, cudaStream_t s);
+  void ep_bwd_experts(const bf16* P, float* dP, cudaStream_t s);
 };
 
 }  // namespace dop

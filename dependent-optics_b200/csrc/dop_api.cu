@@ -307,6 +307,38 @@ int dop_block_create(const dop_mixtral_cfg* cfg, int64_t batch, int64_t seq, int
   });
 }
 
+int dop_block_create_ep(const dop_mixtral_cfg* cfg, int64_t batch, int64_t seq, int precision,
+                        int rank, int world, dop_block** out) {
+  return guarded([&] {
+    DOP_REQUIRE(cfg && out, "null pointer");
+    DOP_REQUIRE(world >= 2, "an expert-parallel block needs world >= 2");
+    *out = reinterpret_cast<dop_block*>(new dop::Block(*cfg, batch, seq, precision, rank, world));
+  });
+}
+
+int dop_block_ep_handle(const dop_block* blk, void* handle) {
+  return guarded([&] {
+    DOP_REQUIRE(blk && handle, "null pointer");
+    auto* b = reinterpret_cast<const dop::Block*>(blk);
+    DOP_REQUIRE(b->ep_world > 1, "not an expert-parallel block");
+    static_assert(sizeof(cudaIpcMemHandle_t) == DOP_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    DOP_CHECK_CUDA(cudaIpcGetMemHandle(&h, b->base));
+    std::memcpy(handle, &h, sizeof(h));
+  });
+}
+
+int dop_block_ep_connect(dop_block* blk, const void* handles) {
+  return guarded([&] {
+    DOP_REQUIRE(blk && handles, "null pointer");
+    auto* b = reinterpret_cast<dop::Block*>(blk);
+    DOP_REQUIRE(b->ep_world > 1, "not an expert-parallel block");
+    std::vector<cudaIpcMemHandle_t> hs(b->ep_world);
+    std::memcpy(hs.data(), handles, sizeof(cudaIpcMemHandle_t) * b->ep_world);
+    b->ep_connect(hs.data());
+  });
+}
+
 int dop_block_destroy(dop_block* blk) {
   return guarded([&] { delete reinterpret_cast<dop::Block*>(blk); });
 }

@@ -1,0 +1,302 @@
+// ep.cu — expert parallelism for the Mixtral block lens: each rank owns
+// experts [rank * Ed, (rank + 1) * Ed) (Ed = E / world) and runs their
+// grouped GEMMs over the expert-sorted rows that every rank routed to them.
+//
+// The exchange is fused with the permutation and the combine: there is no
+// separate all-to-all and no send buffer.  Every rank's block workspace is
+// one cudaMalloc shared with the other ranks through CUDA IPC, so a rank
+// reads a peer's buffer at (peer base + the same offset as its own):
+//   dispatch (fwd)   the owner gathers its receive rows straight from the
+//                    sources' normalised activations xn2, through the
+//                    sources' row -> token maps (k_ep_gather_tokens);
+//   combine (fwd)    each source reads the expert outputs of its (token,
+//                    slot) pairs from the owners and sums them into y
+//                    (k_ep_combine), keeping a local copy for the backward;
+//   dispatch (bwd)   the owner copies the sources' output cotangent rows
+//                    (k_ep_gather_rows);
+//   combine (bwd)    each source sums the expert-input cotangents of its
+//                    pairs from the owners (k_ep_unpermute_router_dx).
+// Receive buffers are expert-major: local expert j's rows from source 0, 1,
+// ...; each (expert, source) piece keeps the source's 128-row padding, so a
+// GEMM row tile belongs to one expert and the weight-gradient contraction of
+// expert j runs over one contiguous range.
+//
+// Ordering between ranks uses four flag barriers per step (k_ep_barrier):
+// after the permutation (sources' rows readable), after the down projection
+// (expert outputs readable), after the output-cotangent gather source is
+// written (dO readable), after the expert-input cotangent GEMM (dXp
+// readable).  Every buffer a peer reads is next overwritten only after the
+// following barrier, which the reader can only pass after its reads.  Waits
+// are bounded; a wait that runs out records a code in the device error word
+// and the kernels that follow skip their work.
+#include "ep.cuh"
+#include "tc_ptx.cuh"
+
+namespace dop {
+namespace ep {
+
+using tc::g_err;
+using tc::gtime_ns;
+
+constexpr uint64_t kBarrierNs = 20000000000ull;  // 20 s per barrier
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Peer copy of a workspace pointer: same offset from the peer's base.
+template <typename P>
+__device__ __forceinline__ P* peer(const EpView& v, int s, P* mine) {
+  return reinterpret_cast<P*>(v.peers[s] + (reinterpret_cast<const char*>(mine) - v.peers[v.rank]));
+}
+
+// Barrier `k` of epoch `epoch`: thread s tells rank s that this rank
+// arrived (flags[k][rank] on rank s), then waits until rank s arrived here.
+__global__ void k_ep_barrier(EpView v, int k, unsigned epoch) {
+  const int s = threadIdx.x;
+  if (s < v.world) {
+    __threadfence_system();
+    st_release_sys(peer(v, s, v.flags) + k * kEpMaxWorld + v.rank, epoch);
+    const unsigned* mine = v.flags + k * kEpMaxWorld + s;
+    const uint64_t t0 = gtime_ns();
+    bool ok = true;
+    for (uint32_t i = 0;; ++i) {
+      if ((int)(ld_acquire_sys(mine) - epoch) >= 0) break;
+      if ((i & 255u) == 255u) {
+        if (*(volatile int*)g_err) { ok = false; break; }
+        if (gtime_ns() - t0 > kBarrierNs) {
+          atomicCAS(g_err, 0, 60 + k);
+          ok = false;
+          break;
+        }
+      }
+    }
+    (void)ok;
+    __threadfence_system();
+  }
+}
+
+// Receive layout (one CTA): reads every rank's padded segment offsets and
+// writes this rank's receive segments, its tile -> (expert, source, source
+// row) map and, for this rank as a source, where its piece of each expert
+// starts in the owner's receive buffer.
+__global__ void k_ep_layout(EpView v, int E) {
+  if (tc::tc_failed()) return;  // an earlier wait gave up: skip (sticky error)
+  __shared__ int so[kEpMaxWorld][kMaxExperts + 1];
+  const int W = v.world, Ed = E / W;
+  for (int i = threadIdx.x; i < W * (E + 1); i += blockDim.x) {
+    const int s = i / (E + 1), e = i % (E + 1);
+    so[s][e] = __ldcv(peer(v, s, v.seg_off) + e);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // start of piece (local expert j, source s) in owner d's receive buffer
+    auto start = [&](int d, int j, int s) {
+      int at = 0;
+      for (int jj = 0; jj < j; ++jj)
+        for (int ss = 0; ss < W; ++ss) at += so[ss][d * Ed + jj + 1] - so[ss][d * Ed + jj];
+      for (int ss = 0; ss < s; ++ss) at += so[ss][d * Ed + j + 1] - so[ss][d * Ed + j];
+      return at;
+    };
+    for (int e = 0; e < E; ++e) v.send_off[e] = start(e / Ed, e % Ed, v.rank);
+    for (int j = 0; j < Ed; ++j) v.recv_seg_off[j] = start(v.rank, j, 0);
+    v.recv_seg_off[Ed] = start(v.rank, Ed - 1, W);  // every piece of every local expert
+  }
+  __syncthreads();
+  // tile map of this rank's receive buffer
+  const int d = v.rank;
+  for (int t = threadIdx.x; t < v.recv_tiles; t += blockDim.x) {
+    const int row = t * kRowAlign;
+    int ex = -1, src = -1, srow = 0;
+    int at = 0;
+    for (int j = 0; j < Ed && ex < 0; ++j)
+      for (int s = 0; s < W; ++s) {
+        const int e = d * Ed + j, n = so[s][e + 1] - so[s][e];
+        if (row >= at && row < at + n) {
+          ex = j; src = s; srow = so[s][e] + (row - at);
+          break;
+        }
+        at += n;
+      }
+    v.recv_tile_expert[t] = ex;
+    v.recv_tile_src[t] = src;
+    v.recv_tile_row0[t] = srow;
+  }
+}
+
+// Owner side of the forward dispatch: receive row r (a row of source s's
+// expert-sorted buffer) = xn2_s[row_token_s[row]], or zeros for padding.
+// One warp per row, 16-byte words.
+__global__ void k_ep_gather_tokens(EpView v, const bf16* xn2, int D) {
+  if (tc::tc_failed()) return;
+  const int n16 = D * 2 / 16;
+  const int rows = v.recv_seg_off[v.local];
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+       r += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    const int tile = (int)(r / kRowAlign);
+    const int s = v.recv_tile_src[tile];
+    if (s < 0 || s >= v.world) continue;
+    const int srow = v.recv_tile_row0[tile] + (int)(r % kRowAlign);
+    const int tok = __ldcv(peer(v, s, v.row_token) + srow);
+    uint4* dst = reinterpret_cast<uint4*>(v.xr) + r * n16;
+    if (tok >= 0) {
+      const uint4* src = reinterpret_cast<const uint4*>(peer(v, s, xn2)) + (int64_t)tok * n16;
+      for (int i = lane; i < n16; i += 32) dst[i] = __ldcv(src + i);
+    } else {
+      for (int i = lane; i < n16; i += 32) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
+// Owner side of the backward dispatch: receive row r = row srow of source
+// s's expert-sorted output cotangent dO.
+__global__ void k_ep_gather_rows(EpView v, const bf16* dO, bf16* dst_rows, int D) {
+  if (tc::tc_failed()) return;
+  const int n16 = D * 2 / 16;
+  const int rows = v.recv_seg_off[v.local];
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+       r += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+    const int tile = (int)(r / kRowAlign);
+    const int s = v.recv_tile_src[tile];
+    if (s < 0 || s >= v.world) continue;
+    const int srow = v.recv_tile_row0[tile] + (int)(r % kRowAlign);
+    const uint4* src = reinterpret_cast<const uint4*>(peer(v, s, dO)) + (int64_t)srow * n16;
+    uint4* dst = reinterpret_cast<uint4*>(dst_rows) + r * n16;
+    for (int i = lane; i < n16; i += 32) dst[i] = __ldcv(src + i);
+  }
+}
+
+// Where (token, slot) pair p's row sits in its owner's receive buffer,
+// clamped into the buffer (it is inside whenever the barriers held).
+__device__ __forceinline__ int64_t owner_row(const EpView& v, int e, int slot_row) {
+  const int64_t r = (int64_t)v.send_off[e] + (slot_row - v.seg_off[e]);
+  return r < 0 ? 0 : (r >= v.recv_cap ? v.recv_cap - 1 : r);
+}
+
+// Source side of the forward combine: y[t] = mid[t] + sum_k w_k out_k, with
+// out_k read from the owner of expert top_i[t, k] (slot order, from zero, as
+// src/mixtral.rs:330-359) and copied to this rank's `out` at slot_row for
+// the router Jacobian of the backward.
+__global__ void k_ep_combine(EpView v, const float* __restrict__ mid, const int* __restrict__ top_i,
+                             const int* __restrict__ slot_row, const float* __restrict__ top_w,
+                             int K, int D, float* __restrict__ out, float* __restrict__ y) {
+  if (tc::tc_failed()) return;
+  const int64_t t = blockIdx.x;
+  __shared__ const float4* src[kMaxTopK];
+  __shared__ float4* stash[kMaxTopK];
+  __shared__ float ws[kMaxTopK];
+  if (threadIdx.x < K) {
+    const int k = threadIdx.x;
+    const int e = top_i[t * K + k], sr = slot_row[t * K + k];
+    const int d = e / v.local;
+    src[k] = reinterpret_cast<const float4*>(peer(v, d, v.outr) + owner_row(v, e, sr) * D);
+    stash[k] = reinterpret_cast<float4*>(out + (int64_t)sr * D);
+    ws[k] = top_w[t * K + k];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < D / 4; i += blockDim.x) {
+    float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < K; ++k) {
+      const float4 o = __ldcv(src[k] + i);
+      stash[k][i] = o;
+      m.x += ws[k] * o.x; m.y += ws[k] * o.y; m.z += ws[k] * o.z; m.w += ws[k] * o.w;
+    }
+    const float4 a = reinterpret_cast<const float4*>(mid + t * D)[i];
+    reinterpret_cast<float4*>(y + t * D)[i] = make_float4(a.x + m.x, a.y + m.y, a.z + m.z, a.w + m.w);
+  }
+}
+
+// Source side of the backward combine: d_xn2[t] = sum_k dXp_k + dz[t] Wr^T,
+// dXp_k read from the owners (src/mixtral.rs:516, 535-540).
+template <typename T>
+__global__ void k_ep_unpermute_router_dx(EpView v, const int* __restrict__ top_i,
+                                         const int* __restrict__ slot_row,
+                                         const float* __restrict__ dz, const T* __restrict__ wr,
+                                         int E, int K, int D, float* __restrict__ dxn) {
+  if (tc::tc_failed()) return;
+  const int64_t t = blockIdx.x;
+  __shared__ float dzs[kMaxExperts];
+  __shared__ const float4* src[kMaxTopK];
+  if (threadIdx.x < E) dzs[threadIdx.x] = dz[t * E + threadIdx.x];
+  if (threadIdx.x < K) {
+    const int k = threadIdx.x;
+    const int e = top_i[t * K + k], sr = slot_row[t * K + k];
+    src[k] = reinterpret_cast<const float4*>(peer(v, e / v.local, v.dxpr) + owner_row(v, e, sr) * D);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < D / 4; i += blockDim.x) {
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < K; ++k) {
+      const float4 o = __ldcv(src[k] + i);
+      a.x += o.x; a.y += o.y; a.z += o.z; a.w += o.w;
+    }
+    float rr[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float acc = 0.f;
+      for (int e = 0; e < E; ++e) acc += dzs[e] * ld(&wr[(int64_t)(4 * i + u) * E + e]);
+      rr[u] = acc;
+    }
+    reinterpret_cast<float4*>(dxn + t * D)[i] =
+        make_float4(a.x + rr[0], a.y + rr[1], a.z + rr[2], a.w + rr[3]);
+  }
+}
+
+}  // namespace ep
+
+using namespace ep;
+
+void ep_barrier(const EpView& v, int k, unsigned epoch, cudaStream_t s, int64_t& launches) {
+  tc::bind_error_word();
+  k_ep_barrier<<<1, 32, 0, s>>>(v, k, epoch);
+  DOP_LAUNCHED(launches);
+}
+
+void ep_layout(const EpView& v, int E, cudaStream_t s, int64_t& launches) {
+  tc::bind_error_word();
+  k_ep_layout<<<1, 256, 0, s>>>(v, E);
+  DOP_LAUNCHED(launches);
+}
+
+void ep_gather_tokens(const EpView& v, const bf16* xn2, int D, cudaStream_t s, int64_t& launches) {
+  tc::bind_error_word();
+  k_ep_gather_tokens<<<sm_count() * 8, 256, 0, s>>>(v, xn2, D);
+  DOP_LAUNCHED(launches);
+}
+
+void ep_gather_rows(const EpView& v, const bf16* dO, bf16* dst, int D, cudaStream_t s,
+                    int64_t& launches) {
+  tc::bind_error_word();
+  k_ep_gather_rows<<<sm_count() * 8, 256, 0, s>>>(v, dO, dst, D);
+  DOP_LAUNCHED(launches);
+}
+
+void ep_combine(const EpView& v, const float* mid, const int* top_i, const int* slot_row,
+                const float* top_w, int64_t T, int K, int D, float* out, float* y, cudaStream_t s,
+                int64_t& launches) {
+  tc::bind_error_word();
+  k_ep_combine<<<(unsigned)T, 256, 0, s>>>(v, mid, top_i, slot_row, top_w, K, D, out, y);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename T>
+void ep_unpermute_router_dx(const EpView& v, const int* top_i, const int* slot_row,
+                            const float* dz, const T* wr, int64_t Tn, int E, int K, int D,
+                            float* dxn, cudaStream_t s, int64_t& launches) {
+  tc::bind_error_word();
+  k_ep_unpermute_router_dx<T><<<(unsigned)Tn, 256, 0, s>>>(v, top_i, slot_row, dz, wr, E, K, D,
+                                                           dxn);
+  DOP_LAUNCHED(launches);
+}
+template void ep_unpermute_router_dx<bf16>(const EpView&, const int*, const int*, const float*,
+                                           const bf16*, int64_t, int, int, int, float*,
+                                           cudaStream_t, int64_t&);
+
+}  // namespace dop

@@ -17,6 +17,7 @@ DOP_BF16 = 1
 DOP_STAGE_GEMM = 0
 DOP_STAGE_ATTENTION = 1
 DOP_STAGE_ADD = 2
+DOP_IPC_HANDLE_BYTES = 64
 
 ERRORS = {
     -1: "DOP_E_INVALID", -2: "DOP_E_CUDA", -3: "DOP_E_NOMEM", -4: "DOP_E_UNSUPPORTED",
@@ -70,6 +71,10 @@ SIGNATURES = [
     ("dop_block_permutation", C.c_int, [_P, _P, _P, _P, _P]),
     ("dop_block_permuted_rows", _I64, [_P]),
     ("dop_block_launches", _I64, [_P]),
+    ("dop_block_create_ep", C.c_int, [C.POINTER(MixtralCfg), _I64, _I64, C.c_int, C.c_int,
+                                      C.c_int, C.POINTER(_P)]),
+    ("dop_block_ep_handle", C.c_int, [_P, _P]),
+    ("dop_block_ep_connect", C.c_int, [_P, _P]),
     ("dop_block_set_adjoint_stream", C.c_int, [_P, _P]),
     ("dop_block_set_timing", C.c_int, [_P, C.c_int]),
     ("dop_block_phase_count", C.c_int, [_P]),

@@ -11,7 +11,7 @@ import ctypes as C
 from dataclasses import dataclass, field
 
 from . import _lib
-from ._lib import DOP_BF16, DOP_F32, check, lib, ptr, stream_ptr
+from ._lib import DOP_BF16, DOP_F32, DOP_IPC_HANDLE_BYTES, check, lib, ptr, stream_ptr
 
 
 @dataclass
@@ -169,12 +169,34 @@ class Block:
     fp32 [batch*seq, dim], dparams is fp32.
     """
 
-    def __init__(self, cfg: MixtralConfig, batch: int, seq: int, precision: int = DOP_F32):
+    def __init__(self, cfg: MixtralConfig, batch: int, seq: int, precision: int = DOP_F32,
+                 ep: tuple | None = None):
+        """`ep = (rank, world)` makes an expert-parallel block (bf16; rank owns
+        experts [rank*E/world, (rank+1)*E/world)); connect it to its peers
+        with `dop.parallel.connect_expert_parallel` before the first forward."""
         self.cfg, self.batch, self.seq, self.precision = cfg, batch, seq, precision
+        self.ep = ep
         h = C.c_void_p()
-        check(lib().dop_block_create(C.byref(cfg.to_c()), batch, seq, precision, C.byref(h)))
+        if ep is None:
+            check(lib().dop_block_create(C.byref(cfg.to_c()), batch, seq, precision, C.byref(h)))
+        else:
+            rank, world = ep
+            check(lib().dop_block_create_ep(C.byref(cfg.to_c()), batch, seq, precision, rank,
+                                            world, C.byref(h)))
         self._h = h
         self._bias = None
+
+    def ep_handle(self) -> bytes:
+        """This rank's workspace IPC handle (DOP_IPC_HANDLE_BYTES bytes)."""
+        buf = C.create_string_buffer(DOP_IPC_HANDLE_BYTES)
+        check(lib().dop_block_ep_handle(self._h, buf))
+        return buf.raw
+
+    def ep_connect(self, handles: bytes) -> None:
+        """Map the peers' workspaces (world handles concatenated in rank order)."""
+        assert len(handles) == DOP_IPC_HANDLE_BYTES * self.ep[1]
+        buf = C.create_string_buffer(handles, len(handles))
+        check(lib().dop_block_ep_connect(self._h, buf))
 
     def close(self) -> None:
         if getattr(self, "_h", None):

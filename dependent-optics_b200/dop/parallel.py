@@ -3,7 +3,11 @@ torch.distributed.
 
 Data parallelism over the batch: every rank runs the block lens on its own
 batch with the same parameters, then the ranks sum their parameter adjoints
-(`reduce_adjoint`).  The crate has no parallel execution (its cluster plan
+(`reduce_adjoint`).  Expert parallelism: every rank still runs attention
+and the router on its own batch, but owns E / world experts and runs them
+for every rank's tokens (the exchange is inside the block, over CUDA IPC
+mappings set up by `connect_expert_parallel`); only the shared slice of the
+adjoint (before the first expert) is summed over ranks.  The crate has no parallel execution (its cluster plan
 runs windows one at a time, src/dist.rs:243-275); this is the exchange the
 data-parallel workloads need.
 """
@@ -58,6 +62,28 @@ def reduce_adjoint(dparams, bucket: int = 1 << 28, async_op: bool = False):
         if async_op:
             works.append(w)
     return works
+
+
+def ep_mode(world: int, experts: int, bf16: bool) -> bool:
+    """Whether a block of `experts` experts runs expert-parallel on `world`
+    ranks: bf16, more than one rank, and the experts split evenly."""
+    return bf16 and 1 < world <= 8 and experts % world == 0
+
+
+def connect_expert_parallel(block, device=None) -> None:
+    """All-gather every rank's workspace IPC handle over the process group
+    and map the peers' workspaces into `block` (an expert-parallel
+    dop.mixtral.Block).  Every rank calls it once, before the first
+    forward."""
+    import torch
+    import torch.distributed as dist
+    h = block.ep_handle()
+    world = dist.get_world_size()
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    mine = torch.tensor(list(h), dtype=torch.uint8, device=dev)
+    every = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine)
+    block.ep_connect(b"".join(bytes(t.cpu().tolist()) for t in every))
 
 
 def heartbeat(step: int) -> None:

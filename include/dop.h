@@ -137,6 +137,30 @@ int64_t dop_block_launches(const dop_block* blk);
  * of the backward runs.  A data-parallel caller reduces that slice on
  * `stream` while the backward continues on its own stream. */
 int dop_block_set_adjoint_stream(dop_block* blk, void* stream);
+/* ---------------------------------------------- expert-parallel block lens
+ * One process per GPU, `world` ranks (2..8, experts % world == 0), bf16
+ * only.  Rank r owns experts [r*E/world, (r+1)*E/world): it runs their
+ * grouped GEMMs over the expert-sorted rows that EVERY rank routed to them
+ * and accumulates only their slices of dparams (the other experts' slices
+ * are left untouched; the shared slice [0, gate0) is this rank's own
+ * adjoint and is summed over ranks by the caller, as in data parallelism).
+ * The exchange has no counterpart in the crate (its experts run in one
+ * process, src/mixtral.rs:330-357, 456-542): the owners read the sources'
+ * rows and the sources read the owners' outputs through CUDA IPC mappings
+ * of each other's workspaces, with four device-side barriers per step.
+ * Every rank must call forward and backward the same number of times.
+ * Set-up: create on every rank, exchange the DOP_IPC_HANDLE_BYTES handles
+ * (e.g. an all-gather), then connect.  Destroy only after every rank's last
+ * backward has completed on the device (e.g. after a host barrier). */
+#define DOP_IPC_HANDLE_BYTES 64
+int dop_block_create_ep(const dop_mixtral_cfg* cfg, int64_t batch, int64_t seq,
+                        int precision, int rank, int world, dop_block** out);
+/* Copy this rank's workspace IPC handle (DOP_IPC_HANDLE_BYTES bytes). */
+int dop_block_ep_handle(const dop_block* blk, void* handle);
+/* Map the peers' workspaces: `handles` holds world x DOP_IPC_HANDLE_BYTES
+ * bytes in rank order (this rank's own entry is ignored). */
+int dop_block_ep_connect(dop_block* blk, const void* handles);
+
 /* Per-phase device timing (CUDA events on the caller's stream around each
  * phase of forward/backward: "expert_gate_up", "attn_fwd", ...).  Off by
  * default; dop_block_phase() synchronises the phase's events. */
