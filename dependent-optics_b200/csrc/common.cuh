@@ -63,6 +63,21 @@ __device__ __forceinline__ void st4(bf16* p, float4 v) {
   u.y = *reinterpret_cast<const uint32_t*>(&b);
   *reinterpret_cast<uint2*>(p) = u;
 }
+// The router's E weights of model row i (wr is [D, E] row-major), E == 8.
+__device__ __forceinline__ void ld_row8(const float* p, float* v) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void ld_row8(const bf16* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[q]));
+    v[2 * q] = f.x;
+    v[2 * q + 1] = f.y;
+  }
+}
 // True when p is aligned for ld4/st4 of the element type T.
 template <typename T>
 inline bool aligned4(const T* p) {

@@ -215,7 +215,7 @@ __global__ void k_ep_combine(EpView v, const float* __restrict__ mid, const int*
 
 // Source side of the backward combine: d_xn2[t] = sum_k dXp_k + dz[t] Wr^T,
 // dXp_k read from the owners (src/mixtral.rs:516, 535-540).
-template <typename T>
+template <typename T, bool E8>
 __global__ void k_ep_unpermute_router_dx(EpView v, const int* __restrict__ top_i,
                                          const int* __restrict__ slot_row,
                                          const float* __restrict__ dz, const T* __restrict__ wr,
@@ -240,8 +240,16 @@ __global__ void k_ep_unpermute_router_dx(EpView v, const int* __restrict__ top_i
     float rr[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
+      const T* wrow = wr + (int64_t)(4 * i + u) * E;
       float acc = 0.f;
-      for (int e = 0; e < E; ++e) acc += dzs[e] * ld(&wr[(int64_t)(4 * i + u) * E + e]);
+      if (E8) {
+        float wv8[8];
+        ld_row8(wrow, wv8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc += dzs[e] * wv8[e];
+      } else {
+        for (int e = 0; e < E; ++e) acc += dzs[e] * ld(&wrow[e]);
+      }
       rr[u] = acc;
     }
     reinterpret_cast<float4*>(dxn + t * D)[i] =
@@ -291,8 +299,12 @@ void ep_unpermute_router_dx(const EpView& v, const int* top_i, const int* slot_r
                             const float* dz, const T* wr, int64_t Tn, int E, int K, int D,
                             float* dxn, cudaStream_t s, int64_t& launches) {
   tc::bind_error_word();
-  k_ep_unpermute_router_dx<T><<<(unsigned)Tn, 256, 0, s>>>(v, top_i, slot_row, dz, wr, E, K, D,
-                                                           dxn);
+  if (E == 8 && (uintptr_t)wr % 16 == 0)
+    k_ep_unpermute_router_dx<T, true><<<(unsigned)Tn, 256, 0, s>>>(v, top_i, slot_row, dz, wr, E, K,
+                                                                   D, dxn);
+  else
+    k_ep_unpermute_router_dx<T, false><<<(unsigned)Tn, 256, 0, s>>>(v, top_i, slot_row, dz, wr, E,
+                                                                    K, D, dxn);
   DOP_LAUNCHED(launches);
 }
 template void ep_unpermute_router_dx<bf16>(const EpView&, const int*, const int*, const float*,
