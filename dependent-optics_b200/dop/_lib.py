@@ -53,6 +53,19 @@ class StageC(C.Structure):
         "probs_at", "from_", "len")]
 
 
+class Qc(C.Structure):
+    _fields_ = [("n", C.c_int64), ("d", C.c_int64)]
+
+
+class ExprNode(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("pad_", C.c_int32)] + [
+        (n, C.c_int64) for n in ("a", "b", "c", "d", "var")] + [("q", Qc)]
+
+
+class LinC(C.Structure):
+    _fields_ = [("dom", C.c_uint32), ("cod", C.c_uint32), ("columns", C.c_uint32 * 32)]
+
+
 # (name, restype, argtypes) of every symbol include/dop.h declares.
 _P = C.c_void_p
 _I64 = C.c_int64
@@ -106,6 +119,21 @@ SIGNATURES = [
                                                _P, _P, _P, _P, _P, _P, _P]),
     ("dop_f32_to_bf16", C.c_int, [_P, _P, _I64, _P]),
     ("dop_sgd_step", C.c_int, [_P, _P, _I64, C.c_float, _P]),
+    ("dop_ad_forward", C.c_int, [C.POINTER(ExprNode), _I64, _I64, C.POINTER(Qc), _I64,
+                                 C.POINTER(Qc), C.POINTER(_P)]),
+    ("dop_ad_backward", C.c_int, [C.POINTER(ExprNode), _I64, _I64, _P, Qc, _I64,
+                                  C.POINTER(Qc)]),
+    ("dop_ad_stored_scalars", C.c_int, [_P, C.POINTER(Qc), _I64, C.POINTER(_I64)]),
+    ("dop_ad_tape_destroy", C.c_int, [_P]),
+    ("dop_lin_apply", C.c_uint32, [C.POINTER(LinC), C.c_uint32]),
+    ("dop_lin_zero", C.c_int, [C.c_uint32, C.c_uint32, C.POINTER(LinC)]),
+    ("dop_lin_identity", C.c_int, [C.c_uint32, C.POINTER(LinC)]),
+    ("dop_lin_compose", C.c_int, [C.POINTER(LinC), C.POINTER(LinC), C.POINTER(LinC)]),
+    ("dop_lin_add", C.c_int, [C.POINTER(LinC), C.POINTER(LinC), C.POINTER(LinC)]),
+    ("dop_lin_transpose", C.c_int, [C.POINTER(LinC), C.POINTER(LinC)]),
+    ("dop_lin_kronecker", C.c_int, [C.POINTER(LinC), C.POINTER(LinC), C.POINTER(LinC)]),
+    ("dop_lin_all", C.c_int, [C.c_uint32, C.c_uint32, C.POINTER(LinC), _I64,
+                              C.POINTER(_I64)]),
 ]
 
 _lib = None

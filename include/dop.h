@@ -297,6 +297,71 @@ int dop_f32_to_bf16(const float* src, uint16_t* dst, int64_t n, void* stream);
 int dop_sgd_step(float* params, const float* grad, int64_t n, float lr,
                  void* stream);
 
+/* ------------------------------------------------ scalar lenses (host)
+ * Exact rational reverse-mode AD with an explicit residual, src/ad.rs.
+ * Host code only (no device work: environments of a few variables).  An
+ * expression is a flat array of nodes, children referenced by index:
+ *   VAR    var                  env[var]
+ *   CONST  q                    the rational q
+ *   NEG    a                    -a
+ *   ADD    a, b                 a + b
+ *   MUL    a, b                 a * b
+ *   LET    a, b                 let x = a in b (x is variable 0 inside b,
+ *                               the outer variables shift up by one)
+ *   IFEQ   a, b, c, d           if a == b then c else d
+ * Rationals are n/d, reduced, d > 0; i64 overflow is an error. */
+typedef struct { int64_t n, d; } dop_q;
+#define DOP_EXPR_VAR 0
+#define DOP_EXPR_CONST 1
+#define DOP_EXPR_NEG 2
+#define DOP_EXPR_ADD 3
+#define DOP_EXPR_MUL 4
+#define DOP_EXPR_LET 5
+#define DOP_EXPR_IFEQ 6
+typedef struct {
+  int32_t kind;
+  int32_t pad_;
+  int64_t a, b, c, d; /* child node indices */
+  int64_t var;
+  dop_q q;
+} dop_expr_node;
+typedef struct dop_ad_tape dop_ad_tape;
+/* `ad::forward` (src/ad.rs:76-129): value and residual.  The residual
+ * stores both factors of each product and the branch each conditional took,
+ * nothing else. */
+int dop_ad_forward(const dop_expr_node* nodes, int64_t n_nodes, int64_t root,
+                   const dop_q* env, int64_t env_len, dop_q* value,
+                   dop_ad_tape** tape);
+/* `ad::backward` (src/ad.rs:131-176): cot_env[i] = d value / d env[i] times
+ * cot, from the residual. */
+int dop_ad_backward(const dop_expr_node* nodes, int64_t n_nodes, int64_t root,
+                    const dop_ad_tape* tape, dop_q cot, int64_t env_len,
+                    dop_q* cot_env);
+/* `ad::stored_scalars` (src/ad.rs:179-196): the rationals the residual
+ * holds, in tape order; out == NULL only counts. */
+int dop_ad_stored_scalars(const dop_ad_tape* tape, dop_q* out, int64_t cap,
+                          int64_t* count);
+int dop_ad_tape_destroy(dop_ad_tape* tape);
+
+/* GF(2) linear maps, src/vect.rs (host code).  A map stores the image of
+ * each basis vector as a bitset: columns[j] for j < dom, bits < cod; dom,
+ * cod <= 32.  `transpose` is the adjoint of a linear map. */
+typedef struct {
+  uint32_t dom, cod;
+  uint32_t columns[32];
+} dop_lin;
+uint32_t dop_lin_apply(const dop_lin* f, uint32_t v);              /* :14-22 */
+int dop_lin_zero(uint32_t dom, uint32_t cod, dop_lin* out);        /* :25-31 */
+int dop_lin_identity(uint32_t n, dop_lin* out);                    /* :33-38 */
+int dop_lin_compose(const dop_lin* g, const dop_lin* f, dop_lin* out); /* g after f, :40-47 */
+int dop_lin_add(const dop_lin* f, const dop_lin* g, dop_lin* out); /* :49-63 */
+int dop_lin_transpose(const dop_lin* f, dop_lin* out);             /* :65-79 */
+int dop_lin_kronecker(const dop_lin* f, const dop_lin* g, dop_lin* out); /* :81-106 */
+/* Every map dom -> cod (dom*cod <= 24) in the crate's enumeration order
+ * (:108-126); out == NULL only counts. */
+int dop_lin_all(uint32_t dom, uint32_t cod, dop_lin* out, int64_t cap,
+                int64_t* count);
+
 #ifdef __cplusplus
 }
 #endif
