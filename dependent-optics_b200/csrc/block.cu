@@ -44,7 +44,7 @@ struct Carver {
 }  // namespace
 
 Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision, int rank,
-             int world)
+             int world, bool allocate)
     : cfg(c), B(batch), S(seq), T(batch * seq), prec(precision), ep_rank(rank), ep_world(world) {
   DOP_REQUIRE(batch >= 1 && seq >= 1, "batch and seq must be >= 1");
   DOP_REQUIRE(c.dim >= 1 && c.heads >= 1 && c.kv_heads >= 1 && c.head_dim >= 2,
@@ -155,6 +155,7 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
     return cv.at;
   };
   bytes = carve(nullptr);
+  if (!allocate) return;  // size query only (no device work)
   cudaError_t e = cudaMalloc(&base, bytes);
   if (e != cudaSuccess) {
     base = nullptr;

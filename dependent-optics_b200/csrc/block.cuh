@@ -76,8 +76,10 @@ struct Block {
   void ph_begin(const char* name, cudaStream_t s);
   void ph_end(cudaStream_t s);
 
+  // allocate = false only computes `bytes` (the workspace a handle would
+  // hold) without touching the device.
   Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision, int rank = 0,
-        int world = 1);
+        int world = 1, bool allocate = true);
   ~Block();
   void forward(const void* params, const float* x, float* y, cudaStream_t s);
   void backward(const void* params, const float* dy, float* dx, float* dparams, cudaStream_t s);

@@ -119,6 +119,22 @@ SIGNATURES = [
                                                _P, _P, _P, _P, _P, _P, _P]),
     ("dop_f32_to_bf16", C.c_int, [_P, _P, _I64, _P]),
     ("dop_sgd_step", C.c_int, [_P, _P, _I64, C.c_float, _P]),
+    ("dop_derive_links", C.c_int, [_P, _I64, _P, _I64, C.POINTER(_I64)]),
+    ("dop_route_message", C.c_int, [_P, _I64, _P, _I64, C.c_int32, C.c_int32, _I64, _P, _I64,
+                                    C.POINTER(_I64)]),
+    ("dop_stage_mixtral", C.c_int, [C.POINTER(MixtralCfg), _I64, _I64, _I64, C.c_int, _P, _I64,
+                                    _P, _I64, C.POINTER(_P)]),
+    ("dop_plan_destroy", C.c_int, [_P]),
+    ("dop_plan_home_count", _I64, [_P]),
+    ("dop_plan_window_count", _I64, [_P]),
+    ("dop_plan_hop_count", _I64, [_P]),
+    ("dop_plan_home", C.c_int, [_P, _I64, _P]),
+    ("dop_plan_window", C.c_int, [_P, _I64, _P]),
+    ("dop_plan_window_hop", C.c_int, [_P, _I64, C.c_int, _I64, C.POINTER(_I64)]),
+    ("dop_plan_hop", C.c_int, [_P, _I64, _P]),
+    ("dop_plan_check", C.c_int, [_P, _P, _I64, _I64]),
+    ("dop_plan_trace", C.c_int, [_P, C.c_char_p, _I64, C.POINTER(_I64)]),
+    ("dop_run_window", C.c_int, [_P, _P, _P, _P, _P, _P, _P]),
     ("dop_ad_forward", C.c_int, [C.POINTER(ExprNode), _I64, _I64, C.POINTER(Qc), _I64,
                                  C.POINTER(Qc), C.POINTER(_P)]),
     ("dop_ad_backward", C.c_int, [C.POINTER(ExprNode), _I64, _I64, _P, Qc, _I64,

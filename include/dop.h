@@ -297,6 +297,94 @@ int dop_f32_to_bf16(const float* src, uint16_t* dst, int64_t n, void* stream);
 int dop_sgd_step(float* params, const float* grad, int64_t n, float lr,
                  void* stream);
 
+/* ------------------------------------------------------- staging plan
+ * The cluster.rs vocabulary (src/cluster.rs:27-292) for a stack of Mixtral
+ * blocks on B200s: devices and links, homes (where a block's parameters and
+ * each in-flight micro-batch's residual live), windows (one block lens on
+ * one micro-batch, forward or backward, on one device) with the hops that
+ * deliver their inputs and carry their outputs, and the StageError codes
+ * DOP_E_NO_DEVICE .. DOP_E_ROUTE_UNAVAILABLE.  A home is a whole block (a
+ * B200 holds one, where the crate's planner tiles matrices for small
+ * buffers): the blocks are cut into PP pipeline stages (the largest divisor
+ * of both the layer count and the GPU count), the remaining GPUs hold
+ * data-parallel replicas, each stage runs one-forward-one-backward over its
+ * replica's micro-batches, and a final Sgd window per parameter home takes
+ * the other replicas' adjoints of that block. */
+#define DOP_DEVICE_CPU 0
+#define DOP_DEVICE_GPU 1
+typedef struct {
+  char name[32];
+  int32_t kind;               /* DOP_DEVICE_* */
+  int32_t pad_;
+  int64_t buffer_bytes;       /* device memory the plan may use */
+  int64_t code_bytes;
+} dop_device;                 /* Device, src/cluster.rs:33-39 */
+typedef struct { int32_t a, b; } dop_link;  /* undirected, Link :42-46 */
+#define DOP_HOME_PARAM 0
+#define DOP_HOME_TAPE 1
+typedef struct {
+  int32_t kind, device, layer, replica, slot, pad_;
+  int64_t row_begin, row_end, col_begin, col_end, stride;
+  int64_t bytes;
+} dop_home;                   /* Home, :134-143 */
+#define DOP_HOP_PARAM 0
+#define DOP_HOP_ADJOINT 1
+#define DOP_HOP_ACTIVATION 2
+typedef struct {
+  int32_t from, to, kind, pad_;
+  int64_t bytes, offset, elems, row_begin, row_end, col_begin, col_end, stride;
+  int32_t layer, micro, replica, pad2_;  /* what the message carries */
+} dop_hop;                    /* Hop, :178-190 */
+#define DOP_PASS_FWD 0
+#define DOP_PASS_BWD 1
+#define DOP_EXEC_SGD 13       /* Exec, :204-219 */
+#define DOP_EXEC_BLOCK 14     /* one block lens (this library's window unit) */
+typedef struct {
+  int32_t device, pass, exec, layer, micro, replica, slot, home;
+  int64_t batch_begin, batch_end;  /* sequences of the global batch */
+  int64_t resident_bytes, tape_bytes, param_bytes, param_offset, din, dout;
+  int32_t n_inbound, n_outbound;
+} dop_window;                 /* Window, :222-250 */
+typedef struct dop_stage_plan dop_stage_plan;
+int dop_derive_links(const dop_device* devices, int64_t n_devices, dop_link* out,
+                     int64_t cap, int64_t* count);            /* :307-336 */
+/* Shortest path whose intermediate devices have `bytes` free
+ * (route_message, :350-398); DOP_E_ROUTE_UNAVAILABLE when none. */
+int dop_route_message(const dop_link* links, int64_t n_links,
+                      const int64_t* free_bytes, int64_t n_devices, int32_t from,
+                      int32_t to, int64_t bytes, int32_t* path, int64_t cap,
+                      int64_t* len);
+/* stage_mixtral / compile_mixtral (:401-490) for cfg->layers blocks of
+ * global_batch sequences of length seq in micro_batches micro-batches;
+ * links NULL derives them from the devices. */
+int dop_stage_mixtral(const dop_mixtral_cfg* cfg, int64_t global_batch, int64_t seq,
+                      int64_t micro_batches, int precision, const dop_device* devices,
+                      int64_t n_devices, const dop_link* links, int64_t n_links,
+                      dop_stage_plan** out);
+int dop_plan_destroy(dop_stage_plan* plan);
+int64_t dop_plan_home_count(const dop_stage_plan* plan);
+int64_t dop_plan_window_count(const dop_stage_plan* plan);
+int64_t dop_plan_hop_count(const dop_stage_plan* plan);
+int dop_plan_home(const dop_stage_plan* plan, int64_t i, dop_home* out);
+int dop_plan_window(const dop_stage_plan* plan, int64_t i, dop_window* out);
+/* Index (into the plan's hops) of window i's j-th inbound or outbound hop. */
+int dop_plan_window_hop(const dop_stage_plan* plan, int64_t i, int outbound, int64_t j,
+                        int64_t* hop_index);
+int dop_plan_hop(const dop_stage_plan* plan, int64_t i, dop_hop* out);
+/* StagePlan::check (:1881-1928): one copy of param_elems parameters is
+ * covered, no device stores or peaks above its buffer. */
+int dop_plan_check(const dop_stage_plan* plan, const dop_device* devices,
+                   int64_t n_devices, int64_t param_elems);
+/* The run's expected control-plane trace (src/mixtral.rs:1393-1435):
+ * MEMBERS n, JOIN r per device, then per window its inbound HOP lines,
+ * COMPUTE device exec pass, its outbound HOP lines; DONE. */
+int dop_plan_trace(const dop_stage_plan* plan, char* buf, int64_t cap, int64_t* len);
+/* Run one block window (Compute::on_window, src/dist.rs:86-97): forward
+ * reads `in` (x) and writes `out` (y); backward reads `in` (dy), writes
+ * `out` (dx) and accumulates into dparams. */
+int dop_run_window(dop_block* blk, const dop_window* w, const void* params,
+                   const float* in, float* out, float* dparams, void* stream);
+
 /* ------------------------------------------------ scalar lenses (host)
  * Exact rational reverse-mode AD with an explicit residual, src/ad.rs.
  * Host code only (no device work: environments of a few variables).  An
