@@ -59,6 +59,13 @@ WORKLOADS = {
                                                experts=8, top_k=2, rms_eps=1e-5, rope_theta=1e6,
                                                sliding_window=4096),
                                       batch=1, seq=1024, precision="bf16", skew=False),
+    # staged 4-block stack of Mixtral-8x7B-shaped blocks: global batch 32 at seq
+    # 4096 in 8 micro-batches, pipeline-staged over the GPUs (dop.cluster)
+    "mixtral8x7b_stack4": dict(cfg=dict(vocab=32000, dim=4096, layers=4, heads=32, kv_heads=8,
+                                        head_dim=128, intermediate=14336, experts=8, top_k=2,
+                                        rms_eps=1e-5, rope_theta=1e6, sliding_window=4096),
+                               batch=32, seq=4096, micro_batches=8, precision="bf16",
+                               skew=False, stack=True),
     # small Mixtral block, fp32
     "small_mixtral_block_f32": dict(cfg=dict(vocab=32000, dim=512, layers=1, heads=8, kv_heads=2,
                                              head_dim=64, intermediate=1408, experts=8, top_k=2,
@@ -209,12 +216,16 @@ def run_reference(a):
     with ctx.Pool(workers) as pool:
         res = pool.map(_worker, [(wl["cfg"], CPU_SAMPLE_SEQ, w, a.warmup + steps)
                                  for w in range(workers)])
-    per_step = [max(r[a.warmup + i] for r in res) for i in range(steps)]
+    layers = wl["cfg"]["layers"]
+    # a stack of identical blocks costs `layers` block passes per token: one
+    # block is timed and the time scaled by the layer count
+    per_step = [layers * max(r[a.warmup + i] for r in res) for i in range(steps)]
     t = sum(per_step) / steps
     tokens = workers * CPU_SAMPLE_SEQ
     v = tokens / t
     sample = (f"{workers} workers x (batch 1, seq {CPU_SAMPLE_SEQ}) at full widths of "
-              f"{a.workload}; each step = every worker's fwd+bwd")
+              f"{a.workload}; each step = every worker's fwd+bwd"
+              + (f" of one block, time x {layers} blocks" if layers > 1 else ""))
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": a.gpus,
         "steps": steps, "warmup": a.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
@@ -230,6 +241,152 @@ def _trace(msg):
     if os.environ.get("DOP_BENCH_TRACE"):
         sys.stderr.write(f"[bench {time.strftime('%H:%M:%S')}] {msg}\n")
         sys.stderr.flush()
+
+
+def run_stack(a):
+    """The staged block stack: plan with dop.cluster.stage_mixtral over the
+    job's GPUs, run with dop.cluster.run_plan (one process per GPU, NCCL hops
+    between stages, replicas' adjoints all-reduced).  A step is the whole
+    global batch through every block, forward and backward."""
+    import torch
+    import torch.distributed as dist
+    from dop import DOP_BF16, cluster, parallel
+    from dop.mixtral import Block, MixtralConfig
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    world, rank = parallel.init_from_env("nccl", timeout_s=600, device=dev)
+    wl = WORKLOADS[a.workload]
+    gb, seq, M = wl["batch"], wl["seq"], wl["micro_batches"]
+    cfg = MixtralConfig(**wl["cfg"])
+    one = dict(wl["cfg"], layers=1)
+    cap = int(torch.cuda.get_device_properties(dev).total_memory * 0.92)
+    plan = cluster.stage_mixtral(cfg, gb, seq, M, DOP_BF16, cluster.b200s(world, cap))
+    groups = {}
+    for g in plan.stage_groups():  # every rank creates every group, in the same order
+        grp = dist.new_group(g) if world > 1 and len(g) > 1 else None
+        groups[tuple(g)] = grp
+    mine = sorted(h.layer for h in plan.homes if h.device == rank and h.kind == cluster.HOME_PARAM)
+    params, dparams, lenses = {}, {}, {}
+    for l in mine:
+        _, ll, params[l] = make_params(one, "bf16", seed=l, device=dev)
+        dparams[l] = torch.zeros(ll.total, dtype=torch.float32, device=dev)
+    one_cfg = MixtralConfig(**one)
+    mb = gb // M
+    for l, n_slots in plan.slots(rank).items():
+        for k in range(n_slots):
+            lenses[(l, k)] = cluster.BlockLens(Block(one_cfg, mb, seq, DOP_BF16))
+    my_micro = sorted({w.micro for w in plan.windows if w.device == rank and w.micro >= 0})
+    first, last = 0 in mine, cfg.layers - 1 in mine
+    g = torch.Generator(device=dev).manual_seed(1000)
+    xs = {m: torch.randn(mb * seq, cfg.dim, generator=g, device=dev) for m in my_micro} if first else {}
+    dys = {m: torch.randn(mb * seq, cfg.dim, generator=g, device=dev) for m in my_micro} if last else {}
+    buf = lambda r, c: torch.empty(r, c, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(inputs, cots):
+        for t in dparams.values():
+            t.zero_()
+        return cluster.run_plan(plan, rank, lambda l, k: lenses[(l, k)], params, dparams, inputs,
+                                cots, buf, groups=groups)
+
+    def launches():
+        return sum(x.block.launches() for x in lenses.values())
+
+    _trace("stack plan, parameters and inputs ready")
+    for _ in range(a.warmup):
+        step(xs, dys)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    l0 = launches()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        ev0.record(stream)
+        for _ in range(a.steps):
+            step(xs, dys)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+    n_launch = launches() - l0
+    ms = parallel.max_over_ranks(ev0.elapsed_time(ev1) / a.steps, device=dev)
+    value = gb * seq / (ms / 1e3)
+    # end to end: each step's stack inputs and output cotangents copied in
+    # from pinned host memory, the input gradients read back
+    e2e = None
+    if not a.no_e2e:
+        hx = {m: t.cpu().pin_memory() for m, t in xs.items()}
+        hdy = {m: t.cpu().pin_memory() for m, t in dys.items()}
+        hdx = {m: torch.empty(mb * seq, cfg.dim).pin_memory() for m in xs}
+        h2d = sum(t.numel() * 4 for t in hx.values()) + sum(t.numel() * 4 for t in hdy.values())
+        d2h = sum(t.numel() * 4 for t in hdx.values())
+
+        def e2e_step():
+            ins = {m: t.to(dev, non_blocking=True) for m, t in hx.items()}
+            cts = {m: t.to(dev, non_blocking=True) for m, t in hdy.items()}
+            out = step(ins, cts)
+            for m, t in out["input_grads"].items():
+                hdx[m].copy_(t, non_blocking=True)
+        e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(1, min(3, a.steps))
+        e0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ems = parallel.max_over_ranks(e0.elapsed_time(e1) / n_e2e, device=dev)
+        h2d = int(parallel.max_over_ranks(h2d, device=dev) if world > 1 else h2d)
+        e2e = {"value": gb * seq / (ems / 1e3), "unit": "tokens/s", "steps": n_e2e,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "note": "bytes of one rank (the largest)"}
+    clk_summary = clk.summary()
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        ts = cpu_oracle_sample(one, CPU_SAMPLE_SEQ, seed=0, repeats=1)
+        cpu = {"value": CPU_SAMPLE_SEQ / (cfg.layers * ts[0]), "unit": "tokens/s", "cores": 1,
+               "kind": "port",
+               "sample": f"batch 1, seq {CPU_SAMPLE_SEQ} through one block at the full widths, "
+                         f"single thread, time x {cfg.layers} blocks"}
+    if rank == 0:
+        hbm, peak, peak_sus, src = measured_peaks()
+        flops = cfg.layers * flops_per_step(one, gb, seq)
+        tflops = flops / (ms / 1e3) / 1e12
+        pp = len(plan.stage_groups())
+        out = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) x and dy)",
+            "config": {"workload": a.workload, "global_batch": gb, "seq": seq,
+                       "micro_batches": M, **wl["cfg"],
+                       "parallelism": f"pp{pp}" + (f"xdp{world // pp}" if world // pp > 1 else ""),
+                       "schedule": "one-forward-one-backward per stage (dop.cluster plan)",
+                       "l2": "inputs larger than L2 (each micro-batch is 4 B x 16384 x 4096)"},
+            "tflops": tflops, "frac_of_bf16_peak": tflops / (world * peak),
+            "frac_of_bf16_sustained": tflops / (world * peak_sus),
+            "roofline": {"bound": "tensor", "kernel": "whole stack step", "achieved": tflops / world,
+                         "peak": peak_sus, "unit": "TFLOP/s", "frac": tflops / world / peak_sus,
+                         "traffic": None,
+                         "peak_source": f"{src} bf16_tflops_sustained (per GPU)"},
+            "e2e": e2e, "gpu_launches": n_launch, "clocks": clk_summary, "cpu_baseline": cpu,
+        }
+        print(json.dumps(out), flush=True)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+        for grp in groups.values():
+            if grp is not None:
+                dist.destroy_process_group(grp)
+        dist.destroy_process_group()
 
 
 def run_ours(a):
@@ -459,6 +616,8 @@ def main():
         a.warmup = 3
     if a.impl == "reference":
         run_reference(a)
+    elif WORKLOADS[a.workload].get("stack"):
+        run_stack(a)
     else:
         run_ours(a)
 

@@ -338,3 +338,30 @@ def run_plan(plan: StagePlan, rank: int, lens_for, params, dparams, inputs, cota
                 trace.append(_hop_line(h))
     flush()
     return {"outputs": outputs, "input_grads": input_grads, "trace": trace}
+
+
+class BlockLens:
+    """A block lens for `run_plan` that runs its windows through
+    `dop_run_window` (the plugin seam of the crate's `dist::Compute`,
+    src/dist.rs:86-97) on one block handle (one residual slot)."""
+
+    def __init__(self, block, stream=None):
+        self.block = block
+        self.stream = stream
+
+    def _run(self, pass_, params, a, dparams=None):
+        import torch
+        from ._lib import ptr, stream_ptr
+        w = WindowC()
+        w.pass_ = pass_
+        w.exec = EXEC_BLOCK
+        out = torch.empty_like(a)
+        check(lib().dop_run_window(self.block.handle, C.byref(w), ptr(params), ptr(a), ptr(out),
+                                   ptr(dparams), stream_ptr(self.stream)))
+        return out
+
+    def forward(self, params, x):
+        return self._run(PASS_FWD, params, x)
+
+    def backward(self, params, dy, dparams):
+        return self._run(PASS_BWD, params, dy, dparams)
