@@ -129,6 +129,20 @@ __global__ void k_ep_layout(EpView v, int E) {
   }
 }
 
+// One warp copies a row of n16 16-byte words from a peer: each lane issues
+// eight loads before it stores any, so eight NVLink round trips overlap.
+__device__ __forceinline__ void copy_row16(uint4* dst, const uint4* src, int n16, int lane) {
+  for (int i0 = lane; i0 < n16; i0 += 8 * 32) {
+    uint4 w[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (i0 + u * 32 < n16) w[u] = __ldcv(src + i0 + u * 32);
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (i0 + u * 32 < n16) dst[i0 + u * 32] = w[u];
+  }
+}
+
 // Owner side of the forward dispatch: receive row r (a row of source s's
 // expert-sorted buffer) = xn2_s[row_token_s[row]], or zeros for padding.
 // One warp per row, 16-byte words.
@@ -147,7 +161,7 @@ __global__ void k_ep_gather_tokens(EpView v, const bf16* xn2, int D) {
     uint4* dst = reinterpret_cast<uint4*>(v.xr) + r * n16;
     if (tok >= 0) {
       const uint4* src = reinterpret_cast<const uint4*>(peer(v, s, xn2)) + (int64_t)tok * n16;
-      for (int i = lane; i < n16; i += 32) dst[i] = __ldcv(src + i);
+      copy_row16(dst, src, n16, lane);
     } else {
       for (int i = lane; i < n16; i += 32) dst[i] = make_uint4(0u, 0u, 0u, 0u);
     }
@@ -169,7 +183,7 @@ __global__ void k_ep_gather_rows(EpView v, const bf16* dO, bf16* dst_rows, int D
     const int srow = v.recv_tile_row0[tile] + (int)(r % kRowAlign);
     const uint4* src = reinterpret_cast<const uint4*>(peer(v, s, dO)) + (int64_t)srow * n16;
     uint4* dst = reinterpret_cast<uint4*>(dst_rows) + r * n16;
-    for (int i = lane; i < n16; i += 32) dst[i] = __ldcv(src + i);
+    copy_row16(dst, src, n16, lane);
   }
 }
 
@@ -201,15 +215,31 @@ __global__ void k_ep_combine(EpView v, const float* __restrict__ mid, const int*
     ws[k] = top_w[t * K + k];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < D / 4; i += blockDim.x) {
-    float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < K; ++k) {
-      const float4 o = __ldcv(src[k] + i);
-      stash[k][i] = o;
-      m.x += ws[k] * o.x; m.y += ws[k] * o.y; m.z += ws[k] * o.z; m.w += ws[k] * o.w;
+  const int D4 = D / 4;
+  // every peer load of a thread's four columns is issued before any is used
+  for (int i0 = threadIdx.x; i0 < D4; i0 += 4 * blockDim.x) {
+    float4 o[4][kMaxTopK];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k)
+        if (k < K && i0 + u * (int)blockDim.x < D4) o[u][k] = __ldcv(src[k] + i0 + u * blockDim.x);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i >= D4) break;
+      float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k) {
+        if (k >= K) break;
+        stash[k][i] = o[u][k];
+        m.x += ws[k] * o[u][k].x; m.y += ws[k] * o[u][k].y;
+        m.z += ws[k] * o[u][k].z; m.w += ws[k] * o[u][k].w;
+      }
+      const float4 a = reinterpret_cast<const float4*>(mid + t * D)[i];
+      reinterpret_cast<float4*>(y + t * D)[i] =
+          make_float4(a.x + m.x, a.y + m.y, a.z + m.z, a.w + m.w);
     }
-    const float4 a = reinterpret_cast<const float4*>(mid + t * D)[i];
-    reinterpret_cast<float4*>(y + t * D)[i] = make_float4(a.x + m.x, a.y + m.y, a.z + m.z, a.w + m.w);
   }
 }
 
@@ -231,11 +261,23 @@ __global__ void k_ep_unpermute_router_dx(EpView v, const int* __restrict__ top_i
     src[k] = reinterpret_cast<const float4*>(peer(v, e / v.local, v.dxpr) + owner_row(v, e, sr) * D);
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < D / 4; i += blockDim.x) {
+  const int D4 = D / 4;
+  for (int i0 = threadIdx.x; i0 < D4; i0 += 4 * blockDim.x) {
+    float4 o[4][kMaxTopK];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k)
+        if (k < K && i0 + u * (int)blockDim.x < D4) o[u][k] = __ldcv(src[k] + i0 + u * blockDim.x);
+#pragma unroll
+    for (int u4 = 0; u4 < 4; ++u4) {
+    const int i = i0 + u4 * blockDim.x;
+    if (i >= D4) break;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < K; ++k) {
-      const float4 o = __ldcv(src[k] + i);
-      a.x += o.x; a.y += o.y; a.z += o.z; a.w += o.w;
+#pragma unroll
+    for (int k = 0; k < kMaxTopK; ++k) {
+      if (k >= K) break;
+      a.x += o[u4][k].x; a.y += o[u4][k].y; a.z += o[u4][k].z; a.w += o[u4][k].w;
     }
     float rr[4];
 #pragma unroll
@@ -254,6 +296,7 @@ __global__ void k_ep_unpermute_router_dx(EpView v, const int* __restrict__ top_i
     }
     reinterpret_cast<float4*>(dxn + t * D)[i] =
         make_float4(a.x + rr[0], a.y + rr[1], a.z + rr[2], a.w + rr[3]);
+    }
   }
 }
 
