@@ -177,6 +177,9 @@ Block::~Block() {
   for (int r = 0; r < (int)ep_peer_base.size(); ++r)
     if (r != ep_rank && ep_peer_base[r]) cudaIpcCloseMemHandle(ep_peer_base[r]);
   if (ep_peers_dev) cudaFree(ep_peers_dev);
+  if (ep_stream) cudaStreamDestroy(ep_stream);
+  if (ep_ev_dx) cudaEventDestroy(ep_ev_dx);
+  if (ep_ev_combined) cudaEventDestroy(ep_ev_combined);
   if (expert_adjoint_done) cudaEventDestroy(expert_adjoint_done);
   for (auto& p : phases) {
     cudaEventDestroy(p.a);
@@ -225,8 +228,10 @@ void Block::ep_fwd_experts(const bf16* P, float* y, cudaStream_t s) {
   const int64_t D = cfg.dim, I = cfg.intermediate, K = cfg.top_k;
   const int64_t ex0 = (int64_t)ep_rank * ep_local * off.expert_stride;  // first local expert
   const EpView v = ep_view();
-  ph_begin("ep_dispatch", s);
+  ph_begin("ep_wait_rows", s);
   ep_barrier_next(0, s);  // every rank's xn2, row_token, seg_off are written
+  ph_end(s);
+  ph_begin("ep_dispatch", s);
   ep_layout(v, (int)cfg.experts, s, launches);
   ep_gather_tokens(v, (const bf16*)xn2, (int)D, s, launches);
   ph_end(s);
@@ -250,8 +255,10 @@ void Block::ep_fwd_experts(const bf16* P, float* y, cudaStream_t s) {
     gemm<bf16>(gd, s);
   }
   ph_end(s);
-  ph_begin("combine", s);
+  ph_begin("ep_wait_outputs", s);
   ep_barrier_next(1, s);  // every owner's expert outputs are written
+  ph_end(s);
+  ph_begin("combine", s);
   ep_combine(v, mid, top_i, slot_row, top_w, T, (int)K, (int)D, out, y, s, launches);
   ph_end(s);
 }
@@ -263,8 +270,10 @@ void Block::ep_bwd_experts(const bf16* P, float* dP, cudaStream_t s) {
   const int64_t D = cfg.dim, I = cfg.intermediate;
   const int64_t ex0 = (int64_t)ep_rank * ep_local * off.expert_stride;
   const EpView v = ep_view();
-  ph_begin("ep_dispatch_bwd", s);
+  ph_begin("ep_wait_dO", s);
   ep_barrier_next(2, s);  // every rank's dO is written
+  ph_end(s);
+  ph_begin("ep_dispatch_bwd", s);
   ep_gather_rows(v, (const bf16*)dO, (bf16*)dOr, (int)D, s, launches);
   ph_end(s);
   ph_begin("expert_dh", s);
@@ -297,6 +306,20 @@ void Block::ep_bwd_experts(const bf16* P, float* dP, cudaStream_t s) {
     gemm<bf16>(g3, s, &up, 1);
   }
   ph_end(s);
+  // The sources' backward combine (wait for every owner's dXp, then read
+  // this rank's pairs) runs on the exchange stream while this rank computes
+  // its experts' gate/up weight adjoints, which nothing there reads.
+  if (!ep_stream) {
+    DOP_CHECK_CUDA(cudaStreamCreateWithFlags(&ep_stream, cudaStreamNonBlocking));
+    DOP_CHECK_CUDA(cudaEventCreateWithFlags(&ep_ev_dx, cudaEventDisableTiming));
+    DOP_CHECK_CUDA(cudaEventCreateWithFlags(&ep_ev_combined, cudaEventDisableTiming));
+  }
+  DOP_CHECK_CUDA(cudaEventRecord(ep_ev_dx, s));
+  DOP_CHECK_CUDA(cudaStreamWaitEvent(ep_stream, ep_ev_dx, 0));
+  ep_barrier_next(3, ep_stream);  // every owner's dXp is written
+  ep_unpermute_router_dx<bf16>(v, top_i, slot_row, dz, P + off.router, T, (int)cfg.experts,
+                               (int)cfg.top_k, (int)D, dxn2, ep_stream, launches);
+  DOP_CHECK_CUDA(cudaEventRecord(ep_ev_combined, ep_stream));
   ph_begin("expert_dw_gate_up", s);
   {
     Gemm g5; g5.M = D; g5.N = I; g5.K = recv_cap; g5.A = xr; g5.lda = D; g5.a_t = true;
@@ -551,12 +574,8 @@ void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_
   }
   // d_xn2 = sum_k dXp[row(t,k)] + dz Wr^T; router weight adjoint
   ph_begin("unpermute_router", s);
-  if (ep) {
-    if constexpr (std::is_same<Act, bf16>::value) {
-      ep_barrier_next(3, s);  // every owner's dXp is written
-      ep_unpermute_router_dx<bf16>(ep_view(), top_i, slot_row, dz, P + off.router, T, (int)E,
-                                   (int)K, (int)D, dxn2, s, launches);
-    }
+  if (ep) {  // computed on the exchange stream during the expert adjoints
+    DOP_CHECK_CUDA(cudaStreamWaitEvent(s, ep_ev_combined, 0));
   } else {
     unpermute_router_dx<Act>(dxp, slot_row, dz, P + off.router, T, (int)E, (int)K, (int)D, dxn2, s,
                              launches);

@@ -58,6 +58,8 @@ struct Block {
   std::vector<char*> ep_peer_base;  // workspace bases as mapped here, [ep_world]
   char** ep_peers_dev = nullptr;    // device copy of ep_peer_base
   unsigned* ep_flags = nullptr;
+  cudaStream_t ep_stream = nullptr;  // the backward combine, beside the dW GEMMs
+  cudaEvent_t ep_ev_dx = nullptr, ep_ev_combined = nullptr;
   int *send_off = nullptr, *recv_seg_off = nullptr, *recv_tile_expert = nullptr;
   int *recv_tile_src = nullptr, *recv_tile_row0 = nullptr;
   void *xr = nullptr, *gr = nullptr, *ur = nullptr, *hr = nullptr, *dOr = nullptr;
