@@ -406,22 +406,37 @@ void Block::fwd(const Act* P, const float* x, float* y, cudaStream_t s) {
   ph_begin("attn_norm", s);
   rmsnorm_fwd<Act>(x, P + off.attn_norm, T, (int)D, cfg.rms_eps, xn_, inv1, x_in, s, launches);
   ph_end(s);
+  // bf16 with 128-wide heads: RoPE is applied in the Q/K GEMMs' epilogue
+  // on the fp32 accumulators, which round once into the bf16 q and k
+  const bool rope_in_gemm = std::is_same<Act, bf16>::value && hd == 128;
   ph_begin("qkv_gemm", s);
   {
     Gemm gq; gq.M = T; gq.N = qd; gq.K = D; gq.A = xn_; gq.lda = D; gq.B = P + off.q; gq.ldb = qd;
-    gq.C = qpre; gq.ldc = qd; gemm<Act>(gq, s);
+    gq.C = qpre; gq.ldc = qd;
     Gemm gk = gq; gk.N = kvd; gk.B = P + off.k; gk.ldb = kvd; gk.C = kpre; gk.ldc = kvd;
-    gemm<Act>(gk, s);
+    if (rope_in_gemm) {
+      TcEpilogue te; te.kind = kTcRope;
+      te.rope_cos = rope_cos; te.rope_sin = rope_sin; te.rope_seq = (int)S;
+      gq.C = q_; gq.c_f32 = false;
+      gk.C = k_; gk.c_f32 = false;
+      gemm_tc(gq, nullptr, 0, te, s, launches);
+      gemm_tc(gk, nullptr, 0, te, s, launches);
+    } else {
+      gemm<Act>(gq, s);
+      gemm<Act>(gk, s);
+    }
     Gemm gv = gk; gv.B = P + off.v; gv.C = v_; gv.c_f32 = std::is_same<Act, float>::value;
     gemm<Act>(gv, s);
   }
   ph_end(s);
-  ph_begin("rope", s);
-  rope<float, Act>(qpre, q_, T, (int)S, H, hd, rope_cos, rope_sin, 1.f, s, launches);
-  rope<float, Act>(kpre, k_, T, (int)S, KV, hd, rope_cos, rope_sin, 1.f, s, launches);
+  if (!rope_in_gemm) {
+    ph_begin("rope", s);
+    rope<float, Act>(qpre, q_, T, (int)S, H, hd, rope_cos, rope_sin, 1.f, s, launches);
+    rope<float, Act>(kpre, k_, T, (int)S, KV, hd, rope_cos, rope_sin, 1.f, s, launches);
+    ph_end(s);
+  }
   Attn at; at.B = B; at.S = S; at.H = H; at.KV = KV; at.hd = hd; at.window = cfg.sliding_window;
   at.causal = true; at.scale = 1.0f / sqrtf((float)hd);
-  ph_end(s);
   ph_begin("attn_fwd", s);
   if (std::is_same<Act, bf16>::value && hd == 128)
     attn_fwd_tc(at, (const bf16*)q_, (const bf16*)k_, (const bf16*)v_, (bf16*)mix_, lse, s,

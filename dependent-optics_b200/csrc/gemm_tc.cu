@@ -44,6 +44,7 @@ enum EpiKind : int {
   kAddResF32 = 3,
   kSwiGLU = 4,     // dual-B forward: cols [0,BN/2) = gate, [BN/2,BN) = up -> g, u, h
   kSwiGLUBwd = 5,  // acc = dH; with g, u in global -> dG, dU
+  kRopeBF16 = 6,   // bf16 store of 128-wide heads rotated by RoPE (rotate_half)
 };
 
 struct Params {
@@ -64,6 +65,8 @@ struct Params {
   const bf16 *g_in, *u_in;       // SwiGLU backward inputs
   bf16 *dg_out, *du_out;
   int64_t ldg;
+  const float *rope_cos, *rope_sin;  // [seq][64] tables of kRopeBF16
+  int rope_seq;
 };
 
 // Tile id -> (group, m tile, n tile).  Consecutive ids walk 16 row tiles
@@ -297,8 +300,10 @@ __global__ void __launch_bounds__(THREADS, 1)
               float u1 = __bfloat162float(__float2bfloat16_rn(u[2 * j + 1]));
               pg[j] = pack_bf16(g0, g1);
               pu[j] = pack_bf16(u0, u1);
-              float h0 = g0 / (1.0f + expf(-g0)) * u0;
-              float h1 = g1 / (1.0f + expf(-g1)) * u1;
+              // silu(g) u with the fast exponential and division (h is
+              // rounded to bf16 next; for g -> -inf the quotient is 0)
+              float h0 = __fdividef(g0, 1.0f + __expf(-g0)) * u0;
+              float h1 = __fdividef(g1, 1.0f + __expf(-g1)) * u1;
               ph2[j] = pack_bf16(h0, h1);
             }
             uint4* og = (uint4*)(p.g_out + m * p.ldg + n);
@@ -312,6 +317,43 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
         }
+      } else if (p.epi == kRopeBF16) {
+        // this warp's 128 columns are one head: column d pairs with d + 64
+        const int64_t nb = (int64_t)tl.n * BN + chalf * (BN / 2);
+        const int pos = (int)(m % p.rope_seq);
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float a[32], b[32];
+          tmem_ld32(tbase + chalf * (BN / 2) + c * 32, a);
+          tmem_ld32(tbase + chalf * (BN / 2) + (c + 2) * 32, b);
+          if (!row_ok || nb >= p.N) continue;
+          const float4* c4 = (const float4*)(p.rope_cos + (int64_t)pos * 64 + c * 32);
+          const float4* s4 = (const float4*)(p.rope_sin + (int64_t)pos * 64 + c * 32);
+          uint32_t o1[16], o2[16];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 cv = c4[q], sv = s4[q];
+            const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+            float r1[4], r2[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = 4 * q + e;
+              r1[e] = a[i] * cc[e] - b[i] * ss[e];
+              r2[e] = b[i] * cc[e] + a[i] * ss[e];
+            }
+            o1[2 * q] = pack_bf16(r1[0], r1[1]);
+            o1[2 * q + 1] = pack_bf16(r1[2], r1[3]);
+            o2[2 * q] = pack_bf16(r2[0], r2[1]);
+            o2[2 * q + 1] = pack_bf16(r2[2], r2[3]);
+          }
+          uint4* d1 = (uint4*)((bf16*)p.C + m * p.ldc + nb + c * 32);
+          uint4* d2 = (uint4*)((bf16*)p.C + m * p.ldc + nb + 64 + c * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            d1[q] = make_uint4(o1[4 * q], o1[4 * q + 1], o1[4 * q + 2], o1[4 * q + 3]);
+            d2[q] = make_uint4(o2[4 * q], o2[4 * q + 1], o2[4 * q + 2], o2[4 * q + 3]);
+          }
+        }
       } else {
         const int64_t nb = (int64_t)tl.n * BN;
         char* Cb = (char*)p.C;
@@ -319,6 +361,18 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
         for (int c = chalf * (BN / 64); c < (chalf + 1) * (BN / 64); ++c) {
           float v[32];
+          // the SwiGLU adjoint's g and u: loaded before the accumulator so
+          // that the two latencies overlap
+          uint4 g4p[4], u4p[4];
+          if (p.epi == kSwiGLUBwd && row_ok && nb + c * 32 < p.N) {
+            const uint4* gi = (const uint4*)(p.g_in + m * p.ldg + nb + c * 32);
+            const uint4* ui = (const uint4*)(p.u_in + m * p.ldg + nb + c * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              g4p[q] = gi[q];
+              u4p[q] = ui[q];
+            }
+          }
           if (!empty_k) tmem_ld32(tbase + c * 32, v);
           else {
 #pragma unroll
@@ -341,20 +395,19 @@ __global__ void __launch_bounds__(THREADS, 1)
           } else if (p.epi == kSwiGLUBwd) {
             // v = dH; dG = dH * u * s (1 + g (1 - s)), dU = dH * g * s
             // (N and ldg are multiples of 32 and 8: whole 16-byte vectors)
-            const uint4* gi = (const uint4*)(p.g_in + m * p.ldg + n);
-            const uint4* ui = (const uint4*)(p.u_in + m * p.ldg + n);
             uint4* dgo = (uint4*)(p.dg_out + m * p.ldg + n);
             uint4* duo = (uint4*)(p.du_out + m * p.ldg + n);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const uint4 g4 = gi[q], u4 = ui[q];
+              const uint4 g4 = g4p[q], u4 = u4p[q];
               const __nv_bfloat162* g2 = (const __nv_bfloat162*)&g4;
               const __nv_bfloat162* u2 = (const __nv_bfloat162*)&u4;
               uint32_t rg[4], ru[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const float2 z = __bfloat1622float2(g2[e]), uu = __bfloat1622float2(u2[e]);
-                const float s0 = 1.0f / (1.0f + __expf(-z.x)), s1 = 1.0f / (1.0f + __expf(-z.y));
+                const float s0 = __fdividef(1.0f, 1.0f + __expf(-z.x));
+                const float s1 = __fdividef(1.0f, 1.0f + __expf(-z.y));
                 const float d0 = v[8 * q + 2 * e], d1 = v[8 * q + 2 * e + 1];
                 rg[e] = pack_bf16(d0 * uu.x * (s0 * (1.0f + z.x * (1.0f - s0))),
                                   d1 * uu.y * (s1 * (1.0f + z.y * (1.0f - s1))));
@@ -512,6 +565,14 @@ void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue
   p.g_out = te.g_out; p.u_out = te.u_out; p.h_out = te.h_out;
   p.g_in = te.g_in; p.u_in = te.u_in; p.dg_out = te.dg_out; p.du_out = te.du_out;
   p.ldg = te.ldg;
+  p.rope_cos = te.rope_cos;
+  p.rope_sin = te.rope_sin;
+  p.rope_seq = te.rope_seq;
+  if (te.kind == kRopeBF16) {
+    DOP_REQUIRE(g.group == 0 && g.N % 128 == 0 && g.ldc % 8 == 0 && te.rope_cos && te.rope_sin &&
+                    te.rope_seq > 0,
+                "the RoPE epilogue needs a plain GEMM, 128-wide heads and the tables");
+  }
   const int out_tile = dual ? BN / 2 : BN;
   p.n_tiles = (int)ceil_div(g.N, out_tile);
   p.m_tiles = (int)ceil_div(g.M, BM);

@@ -110,14 +110,18 @@ struct GemmPart {
   const void* A; int64_t lda; const void* B; int64_t ldb; int64_t K;
 };
 struct TcEpilogue {
-  int kind = -1;  // -1 from Gemm; 4 SwiGLU forward; 5 SwiGLU backward
+  int kind = -1;  // -1 from Gemm; 4 SwiGLU forward; 5 SwiGLU backward; 6 RoPE
   const void* up_B = nullptr;
   bf16 *g_out = nullptr, *u_out = nullptr, *h_out = nullptr;
   const bf16 *g_in = nullptr, *u_in = nullptr;
   bf16 *dg_out = nullptr, *du_out = nullptr;
   int64_t ldg = 0;
+  // kind 6: C (bf16) holds heads of 128 columns rotated by RoPE at position
+  // row mod rope_seq, from the [rope_seq][64] cos/sin tables
+  const float *rope_cos = nullptr, *rope_sin = nullptr;
+  int rope_seq = 0;
 };
-constexpr int kTcSwiGLU = 4, kTcSwiGLUBwd = 5;
+constexpr int kTcSwiGLU = 4, kTcSwiGLUBwd = 5, kTcRope = 6;
 void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue& te,
              cudaStream_t s, int64_t& launches);
 // 3-D bf16 TMA descriptor, 128-byte swizzle: extents dims (dims[0]
