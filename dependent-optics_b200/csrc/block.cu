@@ -74,7 +74,7 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
   off = layer_offsets(c);
   const int64_t D = c.dim, E = c.experts, K = c.top_k, I = c.intermediate;
   const int64_t qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim;
-  rows_cap = round_up(T * K + E * (kRowAlign - 1), kRowAlign);
+  rows_cap = round_up(T * K + E * (kSegAlign - 1), kSegAlign);
   max_tiles = (int)(rows_cap / kRowAlign);
   const bool ep = world > 1;
   ep_local = (int)(E / world);

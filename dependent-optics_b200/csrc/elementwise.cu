@@ -446,8 +446,10 @@ __global__ void k_rope(const TI* __restrict__ src, TO* __restrict__ dst, int64_t
 // ------------------------------------------------- expert permutation (K7)
 // The canonical order of the (token, slot) pairs routed to an expert is the
 // token-major order (t, then slot): a stable counting sort by expert.  Each
-// expert's segment starts at a multiple of kRowAlign rows, so a GEMM row tile
-// never straddles two experts and padded rows can be zero.
+// expert's segment starts at a multiple of kSegAlign rows, so a GEMM row tile
+// (or the 2-SM GEMM's pair of tiles) never straddles two experts and padded
+// rows can be zero; the row tile -> expert map has one entry per kRowAlign
+// rows.
 //
 // Pass 1: per chunk of kPermChunk pairs, count pairs per expert.
 __global__ void k_perm_count(const int* __restrict__ top_i, int64_t pairs, int E,
@@ -483,7 +485,7 @@ __global__ void k_perm_scan(int* __restrict__ chunk_counts, int chunks, int E,
     int off = 0;
     for (int q = 0; q < E; ++q) {
       seg_off[q] = off;
-      off += (tot[q] + kRowAlign - 1) / kRowAlign * kRowAlign;
+      off += (tot[q] + kSegAlign - 1) / kSegAlign * kSegAlign;
     }
     seg_off[E] = off;
   }

@@ -24,6 +24,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "kernels.cuh"
 
@@ -34,7 +35,8 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
-constexpr int STAGES = 4;
+constexpr int STAGES = 4;       // one CTA per tile: 48 KB stages
+constexpr int PAIR_STAGES = 6;  // a pair of CTAs per tile: 32 KB stages per CTA
 constexpr int THREADS = 320;  // TMA warp, MMA warp, 8 epilogue warps
 
 enum EpiKind : int {
@@ -87,62 +89,87 @@ __device__ __forceinline__ Tile tile_of(int t, int m_tiles, int n_tiles) {
   return r;
 }
 
-template <bool A_MN, bool B_MN, int BN, bool DUAL>
+// PAIR: a cluster of two CTAs on two SMs computes one 256-row tile with
+// cta_group::2 MMAs (M = 256): each CTA loads its 128 rows of A and half of
+// B's columns (for the SwiGLU pass: CTA 0 the gate tile, CTA 1 the up tile),
+// CTA 0's MMA thread issues for both, and each CTA's epilogue drains the 128
+// accumulator rows in its own TMEM.  Per FLOP this reads a third less
+// operand data from L2 and shared memory than one CTA per 128-row tile.
+template <bool A_MN, bool B_MN, int BN, bool DUAL, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mA1,
               const __grid_constant__ CUtensorMap mA2, const __grid_constant__ CUtensorMap mB0,
               const __grid_constant__ CUtensorMap mB1, const __grid_constant__ CUtensorMap mB2,
               const Params p) {
+  constexpr int STG = PAIR ? PAIR_STAGES : STAGES;
+  constexpr int BNL = PAIR ? BN / 2 : BN;  // B columns this CTA loads
+  constexpr int TM = PAIR ? 2 * BM : BM;   // rows of a tile
   constexpr uint32_t A_BYTES = BM * BK * 2;
-  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t B_BYTES = BNL * BK * 2;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((A_MN ? 1u : 0u) << 15) |
                              ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
-                             ((uint32_t)(BM >> 4) << 24);
-  if (tc_failed()) return;  // an earlier wait failed: do nothing (sticky error)
+                             ((uint32_t)(TM >> 4) << 24);
+  // An earlier wait failed (sticky error): do no work.  A CTA of a pair
+  // still takes part in the pair's cluster barriers below.
+  const bool failed = tc_failed();
+  if (!PAIR && failed) return;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;   // tile walker
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES);
-  // bars: full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain
-  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 5);
+  uint64_t* bars = (uint64_t*)(smem + STG * STAGE_BYTES);
+  // bars: full[STG], empty[STG], acc_full[2], acc_empty[2], drain
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STG + 5);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   const uint32_t smem0 = smem_u32(smem);
   const uint32_t bar0 = smem_u32(bars);
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
-  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
-  auto accf_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
-  auto acce_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
-  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STG + s); };
+  auto accf_bar = [&](int a) { return bar0 + 8u * (2 * STG + a); };
+  auto acce_bar = [&](int a) { return bar0 + 8u * (2 * STG + 2 + a); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * STG + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < STG; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(accf_bar(a), 1);
-      mbar_init(acce_bar(a), 8);
+      // every epilogue warp of the tile (both CTAs of a pair) frees it
+      mbar_init(acce_bar(a), PAIR ? 16 : 8);
     }
     mbar_init(drain_bar, 1);
-    *abort_flag = 0;
+    *abort_flag = failed ? 1 : 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(512));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"(512));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"(512));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // both CTAs' barriers exist before either is signalled
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   // work description shared by all roles
   int rows_total = p.M;
   if (p.mode == 1) rows_total = p.seg_off[p.G];
-  const int m_tiles = p.mode == 1 ? (rows_total + BM - 1) / BM : p.m_tiles;
+  const int m_tiles = p.mode == 1 ? (rows_total + TM - 1) / TM : p.m_tiles;
   const int groups = p.mode == 2 ? p.G : 1;
   const int total = groups * m_tiles * p.n_tiles;
   auto k_blocks = [&](const Tile& t, int part, int& k0) -> int {
@@ -162,11 +189,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       int issued = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      bool ok = !*abort_flag;
+      // a pair counts both CTAs' bytes on the first CTA's full barriers
+      auto fullb = [&](int st) { return PAIR ? mapa_shared(full_bar(st), 0) : full_bar(st); };
+      auto load = [&](uint32_t dst, const CUtensorMap* map, int st, int c0, int c1, int c2) {
+        if (PAIR) tma_load_3d_pair(dst, map, fullb(st), c0, c1, c2);
+        else tma_load_3d(dst, map, full_bar(st), c0, c1, c2);
+      };
+      for (int t = unit; t < total && ok; t += units) {
         const Tile tl = tile_of(t, m_tiles, p.n_tiles);
-        const int m0 = tl.m * BM;
-        const int z = p.mode == 1 ? max(p.tile_expert[tl.m], 0) : 0;
+        const int m0 = tl.m * TM + (int)rank * BM;  // this CTA's rows
+        // expert of the tile (segments are kSegAlign-aligned: one expert per tile)
+        const int z = p.mode == 1 ? max(p.tile_expert[tl.m * (TM / BM)], 0) : 0;
         for (int part = 0; part < p.nparts && ok; ++part) {
           const CUtensorMap* ma = part == 0 ? &mA0 : (part == 1 ? &mA1 : &mA2);
           const CUtensorMap* mb = part == 0 ? &mB0 : (part == 1 ? &mB1 : &mB2);
@@ -175,22 +209,32 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int kb = 0; kb < nk; ++kb) {
             if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, 1)) { ok = false; break; }
             const uint32_t sa = smem0 + s * STAGE_BYTES, sb = sa + A_BYTES;
-            mbar_expect_tx(full_bar(s), STAGE_BYTES);
+            if (leader) mbar_expect_tx(full_bar(s), PAIR ? 2 * STAGE_BYTES : STAGE_BYTES);
             const int k0 = kbase + kb * BK;
             if (!A_MN) {
-              tma_load_3d(sa, ma, full_bar(s), k0, m0, 0);
+              load(sa, ma, s, k0, m0, 0);
             } else {
-              tma_load_3d(sa, ma, full_bar(s), m0, k0, 0);
-              tma_load_3d(sa + A_BYTES / 2, ma, full_bar(s), m0 + 64, k0, 0);
+              load(sa, ma, s, m0, k0, 0);
+              load(sa + A_BYTES / 2, ma, s, m0 + 64, k0, 0);
             }
             if (!DUAL) {
-              const int n0 = tl.n * BN;
+              const int n0 = tl.n * BN + (int)rank * BNL;  // this CTA's columns
               if (!B_MN) {
-                tma_load_3d(sb, mb, full_bar(s), k0, n0, z);
+                load(sb, mb, s, k0, n0, z);
               } else {
 #pragma unroll
-                for (int j = 0; j < BN / 64; ++j)
-                  tma_load_3d(sb + j * 8192, mb, full_bar(s), n0 + 64 * j, k0, z);
+                for (int j = 0; j < BNL / 64; ++j) load(sb + j * 8192, mb, s, n0 + 64 * j, k0, z);
+              }
+            } else if (PAIR) {
+              // B = [gate tile | up tile]: the first CTA loads the gate
+              // columns, the second the up columns
+              const int n0 = tl.n * (BN / 2);
+              const CUtensorMap* mgu = rank == 0 ? &mB0 : &mB1;
+              if (!B_MN) {
+                load(sb, mgu, s, k0, n0, z);
+              } else {
+#pragma unroll
+                for (int j = 0; j < BNL / 64; ++j) load(sb + j * 8192, mgu, s, n0 + 64 * j, k0, z);
               }
             } else {
               // B = [gate tile | up tile], each BN/2 columns of the output
@@ -198,38 +242,52 @@ __global__ void __launch_bounds__(THREADS, 1)
               const CUtensorMap* mg = &mB0;
               const CUtensorMap* mu = &mB1;
               if (!B_MN) {
-                tma_load_3d(sb, mg, full_bar(s), k0, n0, z);
-                tma_load_3d(sb + B_BYTES / 2, mu, full_bar(s), k0, n0, z);
+                load(sb, mg, s, k0, n0, z);
+                load(sb + B_BYTES / 2, mu, s, k0, n0, z);
               } else {
 #pragma unroll
                 for (int j = 0; j < BN / 128; ++j) {
-                  tma_load_3d(sb + j * 8192, mg, full_bar(s), n0 + 64 * j, k0, z);
-                  tma_load_3d(sb + B_BYTES / 2 + j * 8192, mu, full_bar(s), n0 + 64 * j, k0, z);
+                  load(sb + j * 8192, mg, s, n0 + 64 * j, k0, z);
+                  load(sb + B_BYTES / 2 + j * 8192, mu, s, n0 + 64 * j, k0, z);
                 }
               }
             }
             ++issued;
-            if (++s == STAGES) { s = 0; ph ^= 1u; }
+            if (++s == STG) { s = 0; ph ^= 1u; }
           }
         }
       }
-      if (!ok) {
+      if (!ok && leader) {
         // drain: wait (bounded) for the copies of the stages still in flight
-        for (int q = 0; q < STAGES && q < issued; ++q) {
-          if (--s < 0) { s = STAGES - 1; ph ^= 1u; }
+        // (a pair's copies all complete on the first CTA's barriers)
+        for (int q = 0; q < STG && q < issued; ++q) {
+          if (--s < 0) { s = STG - 1; ph ^= 1u; }
           mbar_wait_drain(full_bar(s), ph);
         }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // (a pair's second CTA issues nothing: its tensor core is driven by the
+    // first CTA's cta_group::2 MMAs)
+    if (lane == 0 && leader) {
       int s = 0, a = 0;
       uint32_t ph = 0, aph = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      bool ok = !*abort_flag;
+      // arrive on a barrier in both CTAs of the pair (or this CTA alone)
+      auto commit_both = [&](uint32_t bar) {
+        if (PAIR) {
+          mma_commit_pair(bar);
+          mma_commit_pair(mapa_shared(bar, 1));
+        } else {
+          mma_commit(bar);
+        }
+      };
+      for (int t = unit; t < total && ok; t += units) {
         const Tile tl = tile_of(t, m_tiles, p.n_tiles);
-        if (!mbar_wait(acce_bar(a), aph ^ 1u, abort_flag, 2)) { ok = false; break; }
+        const bool freed = PAIR ? mbar_wait_cluster(acce_bar(a), aph ^ 1u, abort_flag, 2)
+                                : mbar_wait(acce_bar(a), aph ^ 1u, abort_flag, 2);
+        if (!freed) { ok = false; break; }
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(a * BN);
         uint32_t accum = 0;
@@ -246,19 +304,21 @@ __global__ void __launch_bounds__(THREADS, 1)
                                        : sdesc(sa + ks * 32, 16, 1024);
               const uint64_t bd = B_MN ? sdesc(sb + ks * 2048, 8192, 1024)
                                        : sdesc(sb + ks * 32, 16, 1024);
-              mma_bf16(d, ad, bd, IDESC, accum);
+              if (PAIR) mma_bf16_pair(d, ad, bd, IDESC, accum);
+              else mma_bf16(d, ad, bd, IDESC, accum);
               accum = 1;
             }
-            mma_commit(empty_bar(s));
-            if (++s == STAGES) { s = 0; ph ^= 1u; }
+            commit_both(empty_bar(s));
+            if (++s == STG) { s = 0; ph ^= 1u; }
           }
         }
         if (!ok) break;
-        mma_commit(accf_bar(a));
+        commit_both(accf_bar(a));
         if (++a == 2) { a = 0; aph ^= 1u; }
       }
       // make sure every issued MMA has finished before TMEM can be freed
-      mma_commit(drain_bar);
+      if (PAIR) mma_commit_pair(drain_bar);
+      else mma_commit(drain_bar);
       mbar_wait_drain(drain_bar, 0);
     }
   } else {
@@ -270,14 +330,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int row_in_tile = quad * 32 + lane;
     int a = 0;
     uint32_t aph = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    // the first CTA's barrier that frees accumulator a (a pair frees it from both CTAs)
+    auto acce_leader = [&](int ab) { return PAIR ? mapa_shared(acce_bar(ab), 0) : acce_bar(ab); };
+    for (int t = unit; t < total && !*abort_flag; t += units) {
       const Tile tl = tile_of(t, m_tiles, p.n_tiles);
       if (!mbar_wait(accf_bar(a), aph, abort_flag, 4)) break;
       tc_fence_after();
       int kbase;
       bool empty_k = false;
       if (p.mode == 2) empty_k = k_blocks(tl, 0, kbase) == 0;
-      const int64_t m = (int64_t)tl.m * BM + row_in_tile;
+      const int64_t m = (int64_t)tl.m * TM + (int64_t)rank * BM + row_in_tile;
       const bool row_ok = m < rows_total;
       const uint32_t tbase = tmem + (uint32_t)(a * BN) + ((uint32_t)(quad * 32) << 16);
       if (p.epi == kSwiGLU) {
@@ -449,15 +511,24 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acce_bar(a));
+      if (lane == 0) {
+        if (PAIR && !leader) mbar_arrive_cluster(acce_leader(a));
+        else mbar_arrive(acce_bar(a));
+      }
       if (++a == 2) { a = 0; aph ^= 1u; }
     }
   }
   tc_fence_before();
   __syncthreads();
+  // a pair: neither CTA frees its TMEM or leaves while the other may still
+  // signal its barriers (the first CTA's MMAs have drained by now)
+  if (PAIR) cluster_sync();
   tc_fence_after();
   if (warp == 1) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
   }
 }
 
@@ -509,18 +580,67 @@ CUtensorMap make_map(const void* base, int64_t inner, int64_t outer, int64_t dep
   return make_map3(base, dims, strides, box);
 }
 
-template <bool A_MN, bool B_MN, int BN, bool DUAL>
+template <bool A_MN, bool B_MN, int BN, bool DUAL, bool PAIR>
 void launch(const CUtensorMap* ma, const CUtensorMap* mb, const Params& p, int grid,
             cudaStream_t s) {
-  constexpr size_t smem = (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
-  auto kern = k_gemm_tc<A_MN, B_MN, BN, DUAL>;
+  constexpr int STG = PAIR ? PAIR_STAGES : STAGES;
+  constexpr int BNL = PAIR ? BN / 2 : BN;
+  constexpr size_t smem = (size_t)STG * (BM * BK * 2 + BNL * BK * 2) + 1024 + 256;
+  auto kern = k_gemm_tc<A_MN, B_MN, BN, DUAL, PAIR>;
   bind_error_word();
   static bool attr = false;
   if (!attr) {
     DOP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr = true;
   }
-  kern<<<grid, THREADS, smem, s>>>(ma[0], ma[1], ma[2], mb[0], mb[1], mb[2], p);
+  if (!PAIR) {
+    kern<<<grid, THREADS, smem, s>>>(ma[0], ma[1], ma[2], mb[0], mb[1], mb[2], p);
+    return;
+  }
+  // pairs of CTAs: clusters of two
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  DOP_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, ma[0], ma[1], ma[2], mb[0], mb[1], mb[2], p));
+}
+
+// Pairs of CTAs of this kernel that can be resident at once on the current
+// device (cudaOccupancyMaxActiveClusters, clusters of two), cached.
+template <bool A_MN, bool B_MN, int BN, bool DUAL>
+int pair_slots() {
+  static int slots[16] = {0};
+  int dev = 0;
+  DOP_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 16) dev = 0;
+  if (!slots[dev]) {
+    constexpr size_t smem = (size_t)PAIR_STAGES * (BM * BK * 2 + (BN / 2) * BK * 2) + 1024 + 256;
+    auto kern = k_gemm_tc<A_MN, B_MN, BN, DUAL, true>;
+    DOP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (unsigned)sm_count(), 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    DOP_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    slots[dev] = n > 0 ? n : 1;
+  }
+  return slots[dev];
 }
 
 }  // namespace tc
@@ -575,7 +695,9 @@ void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue
   }
   const int out_tile = dual ? BN / 2 : BN;
   p.n_tiles = (int)ceil_div(g.N, out_tile);
-  p.m_tiles = (int)ceil_div(g.M, BM);
+  // pairs of CTAs (256-row tiles) whenever there are at least 256 rows
+  const bool pair = g.M >= 2 * BM;
+  p.m_tiles = (int)ceil_div(g.M, pair ? 2 * BM : BM);
   // parts
   GemmPart parts[3];
   parts[0] = GemmPart{g.A, g.lda, g.B, g.ldb, g.K};
@@ -594,7 +716,7 @@ void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue
     else ma[i] = make_map(q.A, g.M, Kext, 1, q.lda, q.lda * Kext, 64);
     // B: (K x N); N-major [K][N] (b_t = false) or K-major [N][K]
     const int64_t Nb = dual ? g.N : g.N;
-    const int box_n = dual ? BN / 2 : BN;
+    const int box_n = (dual || pair) ? BN / 2 : BN;
     if (!g.b_t) mb[i] = make_map(q.B, Nb, Kext, Gd, q.ldb, Gd > 1 ? g.b_gs : q.ldb * Kext, 64);
     else mb[i] = make_map(q.B, Kext, Nb, Gd, q.ldb, Gd > 1 ? g.b_gs : q.ldb * Nb, box_n);
   }
@@ -606,18 +728,36 @@ void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue
   }
   for (int i = p.nparts; i < 3; ++i) ma[i] = ma[0];
   for (int i = (dual ? 2 : p.nparts); i < 3; ++i) mb[i] = mb[0];
-  int64_t tiles = (int64_t)(g.group == 2 ? g.G : 1) * p.m_tiles * p.n_tiles;
-  int grid = (int)std::min<int64_t>(tiles, sm_count());
-  if (grid < 1) grid = 1;
+  const int64_t tiles = (int64_t)(g.group == 2 ? g.G : 1) * p.m_tiles * p.n_tiles;
   const bool A = g.a_t, B = !g.b_t;  // MN-major flags
-  if (dual) {
-    if (!A && B) launch<false, true, BN, true>(ma, mb, p, grid, s);
-    else if (!A && !B) launch<false, false, BN, true>(ma, mb, p, grid, s);
-    else throw Error(-4, "SwiGLU GEMM needs a K-major A");
-  } else if (!A && B) launch<false, true, BN, false>(ma, mb, p, grid, s);
-  else if (!A && !B) launch<false, false, BN, false>(ma, mb, p, grid, s);
-  else if (A && B) launch<true, true, BN, false>(ma, mb, p, grid, s);
-  else launch<true, false, BN, false>(ma, mb, p, grid, s);
+  if (dual && A) throw Error(-4, "SwiGLU GEMM needs a K-major A");
+  auto go = [&](auto a_mn, auto b_mn, auto du, auto pr) {
+    constexpr bool AM = decltype(a_mn)::value, BMN = decltype(b_mn)::value;
+    constexpr bool DU = decltype(du)::value, PR = decltype(pr)::value;
+    // persistent grid: one CTA (pair) per SM (pair of SMs) that can be resident
+    int units = PR ? pair_slots<AM, BMN, BN, DU>() : sm_count();
+    int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, units));
+    launch<AM, BMN, BN, DU, PR>(ma, mb, p, PR ? 2 * grid : grid, s);
+  };
+  using T_ = std::true_type;
+  using F_ = std::false_type;
+  if (pair) {
+    if (dual) {
+      if (B) go(F_{}, T_{}, T_{}, T_{});
+      else go(F_{}, F_{}, T_{}, T_{});
+    } else if (!A && B) go(F_{}, T_{}, F_{}, T_{});
+    else if (!A && !B) go(F_{}, F_{}, F_{}, T_{});
+    else if (A && B) go(T_{}, T_{}, F_{}, T_{});
+    else go(T_{}, F_{}, F_{}, T_{});
+  } else {
+    if (dual) {
+      if (B) go(F_{}, T_{}, T_{}, F_{});
+      else go(F_{}, F_{}, T_{}, F_{});
+    } else if (!A && B) go(F_{}, T_{}, F_{}, F_{});
+    else if (!A && !B) go(F_{}, F_{}, F_{}, F_{});
+    else if (A && B) go(T_{}, T_{}, F_{}, F_{});
+    else go(T_{}, F_{}, F_{}, F_{});
+  }
   DOP_LAUNCHED(launches);
 }
 

@@ -11,7 +11,9 @@ namespace dop {
 
 constexpr int kMaxExperts = 16;  // router kernels keep E logits in registers
 constexpr int kMaxTopK = 4;
-constexpr int kRowAlign = 128;   // expert segments start at multiples of this
+constexpr int kRowAlign = 128;   // row tiles of the expert-sorted buffers
+constexpr int kSegAlign = 256;   // expert segments start at multiples of this (a
+                                 // pair of row tiles: the 2-SM GEMM's 256-row tile)
 constexpr int kPermChunk = 1024; // (token, slot) pairs per permutation CTA
 
 // ----------------------------------------------------- elementwise.cu

@@ -325,6 +325,89 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool 
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// ------------------------------------------- pairs of CTAs (cta_group::2)
+// Rank of this CTA in its cluster.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every CTA of the cluster meets here.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+// The shared::cluster address of this CTA's shared variable `addr` in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// TMA tile load into this CTA's shared memory whose completion is counted on
+// `bar`, a barrier of either CTA of the pair (shared::cluster address).
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                                 int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+// D[tmem] (+)= A B over the pair: M = 256 rows, 128 in each CTA's TMEM; A's
+// rows and B's columns come half from each CTA's shared memory at the same
+// descriptor addresses.  Issued by one thread of the pair's first CTA.
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                              uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// Arrive once on `bar` (shared::cluster address, either CTA of the pair)
+// when the pair MMAs issued so far have completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+// Arrive on a barrier of another CTA of the cluster (release at cluster scope).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait at cluster scope (arrivals from the other CTA of the pair).
+static __device__ __noinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
+                                                      volatile int* abort_flag, int code) {
+  const uint64_t t0 = gtime_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_cluster(bar, parity)) return true;
+    if ((i & 127u) == 127u) {
+      if (*abort_flag) return false;
+      if (*(volatile int*)g_err) {
+        *abort_flag = 1;
+        return false;
+      }
+      if (gtime_ns() - t0 > kWaitNs) break;
+    }
+  }
+  atomicCAS(g_err, 0, code);
+  *abort_flag = 1;
+  return false;
+}
+
 // Point this translation unit's g_err at the device's error word (once per
 // device; call before the first launch of a kernel of this unit).
 static inline void bind_error_word() {

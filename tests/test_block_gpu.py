@@ -198,11 +198,11 @@ def test_permutation_is_the_stable_expert_sort(cuda):
     top_i = gpu["top_i"].reshape(-1)
     T, k, E = batch * seq, cfg.top_k, cfg.experts
     # reference: stable counting sort of (token, slot) pairs by expert,
-    # segments padded to 128 rows
+    # segments padded to 256 rows
     counts = np.bincount(top_i, minlength=E)
     off = np.zeros(E + 1, np.int64)
     for e in range(E):
-        off[e + 1] = off[e] + (counts[e] + 127) // 128 * 128
+        off[e + 1] = off[e] + (counts[e] + 255) // 256 * 256
     assert np.array_equal(seg_off, off)
     fill = off[:-1].copy()
     exp_row = np.zeros(T * k, np.int64)

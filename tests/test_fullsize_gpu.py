@@ -72,7 +72,7 @@ def test_mixtral8x7b_block_full_size_properties(cuda):
     top_i = blk.routing()[0].cpu().numpy().reshape(-1)
     slot_row, seg_off, _ = (t.cpu().numpy() for t in blk.permutation())
     counts = np.bincount(top_i, minlength=cfg.experts)
-    off = np.concatenate([[0], np.cumsum((counts + 127) // 128 * 128)])
+    off = np.concatenate([[0], np.cumsum((counts + 255) // 256 * 256)])
     assert np.array_equal(seg_off, off)
     order = np.argsort(top_i, kind="stable")
     sorted_e = top_i[order]
