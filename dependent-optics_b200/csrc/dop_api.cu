@@ -147,7 +147,6 @@ void program_forward(dop_program* p, const float* x, const float* params, float*
                      cudaStream_t s) {
   float* cur = p->buf[0];
   DOP_CHECK_CUDA(cudaMemcpyAsync(cur, x, sizeof(float) * p->input_len, cudaMemcpyDeviceToDevice, s));
-  int64_t cur_len = p->input_len;
   int which = 0, ai = 0;
   for (const dop_stage& st : p->stages) {
     float* nxt = p->buf[(which + 1) % 2];
@@ -164,7 +163,6 @@ void program_forward(dop_program* p, const float* x, const float* params, float*
       g.relu = st.relu != 0;
       g.mask = st.relu ? p->mask + st.mask_at : nullptr;
       dop::gemm_simt<float>(g, s, p->launches);
-      cur_len = st.batch * st.dout;
       which = (which + 1) % 2;
       cur = nxt;
     } else if (st.kind == DOP_STAGE_ATTENTION) {
@@ -179,14 +177,12 @@ void program_forward(dop_program* p, const float* x, const float* params, float*
       DOP_CHECK_CUDA(cudaMemcpyAsync(nxt, p->attn_out[ai], sizeof(float) * n,
                                      cudaMemcpyDeviceToDevice, s));
       ++ai;
-      cur_len = n;
       which = (which + 1) % 2;
       cur = nxt;
     } else {
       dop::add_inplace(cur, p->tape + st.from, st.len, s, p->launches);
     }
   }
-  (void)cur_len;
   DOP_CHECK_CUDA(cudaMemcpyAsync(y, cur, sizeof(float) * p->output_len, cudaMemcpyDeviceToDevice, s));
   p->have_tape = true;
 }

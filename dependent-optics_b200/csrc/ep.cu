@@ -64,19 +64,17 @@ __global__ void k_ep_barrier(EpView v, int k, unsigned epoch) {
     st_release_sys(peer(v, s, v.flags) + k * kEpMaxWorld + v.rank, epoch);
     const unsigned* mine = v.flags + k * kEpMaxWorld + s;
     const uint64_t t0 = gtime_ns();
-    bool ok = true;
+    // bounded: gives up when another wait already failed or after kBarrierNs
     for (uint32_t i = 0;; ++i) {
       if ((int)(ld_acquire_sys(mine) - epoch) >= 0) break;
       if ((i & 255u) == 255u) {
-        if (*(volatile int*)g_err) { ok = false; break; }
+        if (*(volatile int*)g_err) break;
         if (gtime_ns() - t0 > kBarrierNs) {
           atomicCAS(g_err, 0, 60 + k);
-          ok = false;
           break;
         }
       }
     }
-    (void)ok;
     __threadfence_system();
   }
 }
