@@ -74,6 +74,9 @@ WORKLOADS = {
 }
 DEFAULT_WORKLOAD = "mixtral8x7b_block"
 CPU_SAMPLE_SEQ = 2  # tokens of the CPU-oracle sample (batch 1, full widths)
+# DRAM bytes (read 9.78e9 + write 6.09e9) of one full-size expert gate/up
+# launch, measured once with ncu (a bench run cannot read DRAM counters)
+GATE_UP_TRAFFIC = 9.78e9 + 6.09e9
 
 
 def flops_per_step(cfg, batch, seq):
@@ -578,7 +581,11 @@ def run_ours(a):
             # the gate/up GEMM is timed inside a long step: sustained peak
             "roofline": {"bound": "tensor", "kernel": "expert_gate_up", "achieved": achieved,
                          "peak": peak_sus, "unit": "TFLOP/s", "frac": achieved / peak_sus,
-                         "traffic": None,
+                         "traffic": GATE_UP_TRAFFIC if a.workload == "mixtral8x7b_block" else None,
+                         "traffic_source": ("dram bytes read + written by one full-size launch, "
+                                            "one-pass ncu capture "
+                                            "(profiles/gemm_dram_traffic_mixtral8x7b_block.md); "
+                                            "algorithmic 8.16e9 B"),
                          "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside "
                                         "a long step)"},
             "phases_ms": phases,

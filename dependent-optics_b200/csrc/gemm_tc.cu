@@ -17,7 +17,10 @@
 // epilogue of tile i overlaps the main loop of tile i+1.  Either operand may be
 // K-major or M/N-major (the instruction descriptor's transpose bits), which
 // covers Y = X W, dX = dY W^T and dW = X^T dY on the crate's [din, dout]
-// weights without a transpose.  Every mbarrier wait is bounded; a wait that
+// weights without a transpose.  Outputs that a tile writes once (everything
+// but the accumulated weight gradients) are stored with the streaming
+// (evict-first) hint, so the output stream does not push the operand tiles
+// that later tiles re-read out of L2.  Every mbarrier wait is bounded; a wait that
 // runs out records an error code, stops the tile loop and drains what is in
 // flight before TMEM is freed.
 #include <cuda.h>
@@ -373,9 +376,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint4* oh = (uint4*)(p.h_out + m * p.ldg + n);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              og[q] = make_uint4(pg[4 * q], pg[4 * q + 1], pg[4 * q + 2], pg[4 * q + 3]);
-              ou[q] = make_uint4(pu[4 * q], pu[4 * q + 1], pu[4 * q + 2], pu[4 * q + 3]);
-              oh[q] = make_uint4(ph2[4 * q], ph2[4 * q + 1], ph2[4 * q + 2], ph2[4 * q + 3]);
+              __stcs(og + q, make_uint4(pg[4 * q], pg[4 * q + 1], pg[4 * q + 2], pg[4 * q + 3]));
+              __stcs(ou + q, make_uint4(pu[4 * q], pu[4 * q + 1], pu[4 * q + 2], pu[4 * q + 3]));
+              __stcs(oh + q, make_uint4(ph2[4 * q], ph2[4 * q + 1], ph2[4 * q + 2], ph2[4 * q + 3]));
             }
           }
         }
@@ -412,8 +415,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint4* d2 = (uint4*)((bf16*)p.C + m * p.ldc + nb + 64 + c * 32);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            d1[q] = make_uint4(o1[4 * q], o1[4 * q + 1], o1[4 * q + 2], o1[4 * q + 3]);
-            d2[q] = make_uint4(o2[4 * q], o2[4 * q + 1], o2[4 * q + 2], o2[4 * q + 3]);
+            __stcs(d1 + q, make_uint4(o1[4 * q], o1[4 * q + 1], o1[4 * q + 2], o1[4 * q + 3]));
+            __stcs(d2 + q, make_uint4(o2[4 * q], o2[4 * q + 1], o2[4 * q + 2], o2[4 * q + 3]));
           }
         }
       } else {
@@ -449,8 +452,8 @@ __global__ void __launch_bounds__(THREADS, 1)
               uint4* o4 = (uint4*)out;
 #pragma unroll
               for (int q = 0; q < 4; ++q)
-                o4[q] = make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]), pack_bf16(v[8 * q + 2], v[8 * q + 3]),
-                                   pack_bf16(v[8 * q + 4], v[8 * q + 5]), pack_bf16(v[8 * q + 6], v[8 * q + 7]));
+                __stcs(o4 + q, make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]), pack_bf16(v[8 * q + 2], v[8 * q + 3]),
+                                          pack_bf16(v[8 * q + 4], v[8 * q + 5]), pack_bf16(v[8 * q + 6], v[8 * q + 7])));
             } else {
               for (int j = 0; j < 32 && n + j < p.N; ++j) out[j] = __float2bfloat16_rn(v[j]);
             }
@@ -475,8 +478,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                                   d1 * uu.y * (s1 * (1.0f + z.y * (1.0f - s1))));
                 ru[e] = pack_bf16(d0 * (z.x * s0), d1 * (z.y * s1));
               }
-              dgo[q] = make_uint4(rg[0], rg[1], rg[2], rg[3]);
-              duo[q] = make_uint4(ru[0], ru[1], ru[2], ru[3]);
+              __stcs(dgo + q, make_uint4(rg[0], rg[1], rg[2], rg[3]));
+              __stcs(duo + q, make_uint4(ru[0], ru[1], ru[2], ru[3]));
             }
           } else {
             float* out = (float*)Cb + m * p.ldc + n;
@@ -501,7 +504,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               if (full) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q)
-                  ((float4*)out)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                  __stcs((float4*)out + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
               } else {
                 for (int j = 0; j < 32 && n + j < p.N; ++j) out[j] = v[j];
               }
