@@ -23,7 +23,6 @@ import ctypes as C
 from dataclasses import dataclass, field
 
 from ._lib import check, lib
-from . import _lib
 
 DEVICE_CPU, DEVICE_GPU = 0, 1
 HOME_PARAM, HOME_TAPE = 0, 1
