@@ -71,6 +71,9 @@ WORKLOADS = {
                                              head_dim=64, intermediate=1408, experts=8, top_k=2,
                                              rms_eps=1e-5, rope_theta=1e6, sliding_window=128),
                                     batch=4, seq=512, precision="f32", skew=False),
+    # the crate's CPU-run case: kernel.rs MLP program, batch 64, 128 -> 256 -> 128,
+    # ReLU hidden, MSE against targets
+    "mlp_f32": dict(program="mlp", batch=64, dims=[128, 256, 128], precision="f32", skew=False),
 }
 DEFAULT_WORKLOAD = "mixtral8x7b_block"
 CPU_SAMPLE_SEQ = 2  # tokens of the CPU-oracle sample (batch 1, full widths)
@@ -207,6 +210,9 @@ def run_reference(a):
         return
     wl = WORKLOADS[a.workload]
     cores = os.cpu_count() or 1
+    if wl.get("program"):
+        run_reference_program(a, wl, cores)
+        return
     try:
         avail = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
     except (ValueError, OSError):
@@ -236,6 +242,194 @@ def run_reference(a):
         "config": {"workload": a.workload, "batch": 1, "seq": CPU_SAMPLE_SEQ, **wl["cfg"]},
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": workers, "kind": "port",
                          "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def mlp_inputs(wl, seed=0):
+    """x, targets ~ N(0,1); W ~ N(0, 1/fan_in); b = 0 (host fp32 tensors)."""
+    import torch
+    from dop import kernel as K
+    prog = K.Program.mlp(wl["batch"], wl["dims"])
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(prog.input_len, generator=g)
+    t = torch.randn(prog.output_len, generator=g)
+    params = torch.zeros(prog.param_len)
+    for st in prog.stages:
+        n = st.din * st.dout
+        params[st.param_at: st.param_at + n] = torch.randn(n, generator=g) / st.din ** 0.5
+    return prog, x, t, params
+
+
+def mlp_flops(wl):
+    """fwd+bwd = 3 x the forward's 2 * batch * din * dout per layer."""
+    d = wl["dims"]
+    return 3 * sum(2 * wl["batch"] * a * b for a, b in zip(d[:-1], d[1:]))
+
+
+def cpu_program_sample(wl, seconds=1.0):
+    """(steps, seconds) of the oracle's program forward+backward (the crate's
+    single-threaded CPU path) with the MSE cotangent of the targets."""
+    import numpy as np
+    import oracle_ffi as orc
+    prog, x, t, params = mlp_inputs(wl)
+    x, t, params = x.numpy(), t.numpy(), params.numpy()
+    y = orc.program_forward_backward(prog, x, params)[0]
+    dy = (2.0 * (y - t) / y.size).astype(np.float32)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        orc.program_forward_backward(prog, x, params, dy=dy)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            return n, el
+
+
+def _program_worker(args):
+    wl, seconds = args
+    return cpu_program_sample(wl, seconds)
+
+
+def run_program(a):
+    """A kernel.rs program workload: one step = forward, MSE head, backward of
+    the compiled program, replayed from a CUDA graph; every rank runs its own
+    replica (the program has no data-parallel exchange)."""
+    import torch
+    import torch.distributed as dist
+    from dop import kernel as K
+    from dop import parallel
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    world, rank = parallel.init_from_env("nccl", timeout_s=600, device=dev)
+    wl = WORKLOADS[a.workload]
+    prog, hx, ht, hp = mlp_inputs(wl)
+    cp = K.CompiledProgram(prog)
+    X, Tt, P = hx.to(dev), ht.to(dev), hp.to(dev)
+    stream = torch.cuda.Stream(dev)
+    rows = wl["batch"]
+
+    def step(x, t, s):
+        y = cp.forward(x, P, stream=s)
+        loss, dy = K.mse_loss_grad(y, t, stream=s)
+        dx, dp = cp.backward(P, dy, stream=s)
+        return loss, dx, dp
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, a.warmup)):
+            step(X, Tt, stream)
+    stream.synchronize()
+    l_per = cp.launches()
+    step(X, Tt, stream)
+    stream.synchronize()
+    l_per = cp.launches() - l_per + 1  # + the MSE head
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step(X, Tt, torch.cuda.current_stream(dev))
+    for _ in range(a.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    cur = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(cur)
+    for _ in range(a.steps):
+        graph.replay()
+    ev1.record(cur)
+    torch.cuda.synchronize(dev)
+    ms = parallel.max_over_ranks(ev0.elapsed_time(ev1) / a.steps, device=dev)
+    value = world * rows / (ms / 1e3)
+    # a step takes microseconds: a longer run of replays gives the clock
+    # sampler something to see and a steady-state time beside the K steps
+    reps = 20000
+    with ClockSampler(local) as clk:
+        ev0.record(cur)
+        for _ in range(reps):
+            graph.replay()
+        ev1.record(cur)
+        torch.cuda.synchronize(dev)
+    steady_ms = parallel.max_over_ranks(ev0.elapsed_time(ev1) / reps, device=dev)
+
+    # end to end through the public calls: x and targets from pinned host
+    # memory, the loss read back, every step
+    e2e = None
+    if not a.no_e2e:
+        px, pt = hx.pin_memory(), ht.pin_memory()
+        hl = torch.empty(500, dtype=torch.float32).pin_memory()
+        Xd, Td = torch.empty_like(X), torch.empty_like(Tt)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = 500
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for i in range(n_e2e):
+                Xd.copy_(px, non_blocking=True)
+                Td.copy_(pt, non_blocking=True)
+                loss, _, _ = step(Xd, Td, stream)
+                hl[i:i + 1].copy_(loss.view(1), non_blocking=True)
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ems = parallel.max_over_ranks(e0.elapsed_time(e1) / n_e2e, device=dev)
+        e2e = {"value": world * rows / (ems / 1e3), "unit": "tokens/s", "steps": n_e2e,
+               "h2d_bytes_per_step": (hx.numel() + ht.numel()) * 4, "d2h_bytes_per_step": 4,
+               "note": "eager public calls (CompiledProgram.forward, mse_loss_grad, backward)"}
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        n, sec = cpu_program_sample(wl, seconds=10.0)
+        cpu = {"value": n * rows / sec, "unit": "tokens/s", "cores": 1, "kind": "port",
+               "sample": f"{n} forward+backward passes of the program (batch {rows}) with the "
+                         "MSE cotangent, single thread"}
+    if rank == 0:
+        tflops = mlp_flops(wl) / (ms / 1e3) / 1e12
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "steady_state": {"steps": reps, "ms_per_step": steady_ms,
+                             "value": world * rows / (steady_ms / 1e3)},
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (x, targets ~ N(0,1); W ~ N(0, 1/fan_in); b = 0; seed 0)",
+            "config": {"workload": a.workload, "batch_per_gpu": rows, "dims": wl["dims"],
+                       "loss": "mse", "parallelism": "single" if world == 1 else
+                       f"{world} independent replicas",
+                       "graph": "one CUDA graph per step (forward, MSE head, backward)",
+                       "l2": "inputs smaller than L2 (the workload is 2 x 32 KiB)"},
+            "tflops": tflops,
+            "roofline": {"bound": "latency", "kernel": "whole step", "achieved": tflops,
+                         "peak": None, "unit": "TFLOP/s", "frac": None, "traffic": None,
+                         "note": f"{l_per} dependent launches of kernels that each take "
+                                 "a few microseconds or less; no throughput roof applies"},
+            "e2e": e2e, "gpu_launches": l_per * a.steps, "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }), flush=True)
+    cp.close()
+    if world > 1:
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference_program(a, wl, cores):
+    """The oracle's program forward+backward on every host core: one
+    independent replica per worker process, each step a 1 s sample."""
+    import multiprocessing as mp
+    steps = max(1, a.steps)
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores) as pool:
+        pool.map(_program_worker, [(wl, 0.2)] * cores)  # warm-up
+        per_step = []
+        for _ in range(steps):
+            res = pool.map(_program_worker, [(wl, 1.0)] * cores)
+            per_step.append(sum(n for n, _ in res) * wl["batch"] / max(t for _, t in res))
+    v = sum(per_step) / steps
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": a.gpus,
+        "steps": steps, "warmup": a.warmup, "ms_per_step": wl["batch"] / v * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": a.workload, "batch": wl["batch"],
+                                        "dims": wl["dims"], "loss": "mse"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{cores} workers, each 1 s of forward+backward passes"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -628,6 +822,8 @@ def main():
         a.warmup = 3
     if a.impl == "reference":
         run_reference(a)
+    elif WORKLOADS[a.workload].get("program"):
+        run_program(a)
     elif WORKLOADS[a.workload].get("stack"):
         run_stack(a)
     else:

@@ -85,6 +85,7 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
   const int64_t chunks = ceil_div(T * K, kPermChunk);
   part_cap = std::max<int64_t>((int64_t)sm_count() * 4 * D, 64 * D * E);
   part_cap = std::max<int64_t>(part_cap, 64 * std::max(qd, D));
+  split_cap = prec == DOP_F32 ? std::min<int64_t>(1 << 22, 16 * D * std::max(qd, D)) : 0;
 
   auto carve = [&](char* base_) {
     Carver cv;
@@ -129,6 +130,7 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
     cv.take(dv, 4 * T * kvd, base_);
     cv.take(delta, 4 * T * c.heads, base_);
     cv.take(part, 4 * part_cap, base_);
+    cv.take(split_ws, 4 * split_cap, base_);
     cv.take(dO, a * rows_cap * D, base_);
     cv.take(dg, xe * a * rows_cap * I, base_);
     cv.take(du, xe * a * rows_cap * I, base_);
@@ -367,9 +369,12 @@ void Block::gemm(const Gemm& g, cudaStream_t s, const GemmPart* extra, int n_ext
     gemm_tc(g, extra, n_extra, TcEpilogue{}, s, launches);
     return;
   }
-  gemm_simt<Act>(g, s, launches);
+  Gemm gs = g;
+  gs.ws = split_ws;
+  gs.ws_cap = split_cap;
+  gemm_simt<Act>(gs, s, launches);
   for (int i = 0; i < n_extra; ++i) {
-    Gemm gi = g;
+    Gemm gi = gs;
     gi.A = extra[i].A; gi.lda = extra[i].lda; gi.B = extra[i].B; gi.ldb = extra[i].ldb;
     gi.K = extra[i].K; gi.epi = Epi::Accum;
     gemm_simt<Act>(gi, s, launches);

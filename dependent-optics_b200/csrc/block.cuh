@@ -44,6 +44,8 @@ struct Block {
   // backward scratch
   float *dz, *dh, *dxp, *dxn2, *dmid, *dxn, *dq, *dk, *dv, *delta, *part;
   int64_t part_cap;
+  float* split_ws = nullptr;  // fp32 lens: split-contraction partials (gemm_simt)
+  int64_t split_cap = 0;
   void *dO, *dg, *du, *dmid_a, *dmix, *dq_a, *dk_a, *dv_a;
 
   // expert parallelism (ep_world > 1, bf16 only; ep.cu): this rank owns

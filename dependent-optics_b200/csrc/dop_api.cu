@@ -125,7 +125,13 @@ struct dop_program {
   int64_t part_cap = 0;
   int64_t launches = 0;
   bool have_tape = false;
-  float* y_dev = nullptr;  // output of the last forward
+  // per stage: the skip cotangent an Add stage carries back to its source
+  // (nullptr for other stages), and dy = 1 for the sum loss; allocated at
+  // creation so that forward and backward only enqueue work on the stream
+  std::vector<float*> side_buf;
+  float* ones = nullptr;
+  float* split_ws = nullptr;  // split-contraction partials of the CUDA-core GEMM
+  int64_t split_cap = 0;
   std::vector<float*> owned;
 
   float* alloc(int64_t n) {
@@ -162,6 +168,7 @@ void program_forward(dop_program* p, const float* x, const float* params, float*
       g.bias = params + st.param_at + st.din * st.dout;
       g.relu = st.relu != 0;
       g.mask = st.relu ? p->mask + st.mask_at : nullptr;
+      g.ws = p->split_ws; g.ws_cap = p->split_cap;
       dop::gemm_simt<float>(g, s, p->launches);
       which = (which + 1) % 2;
       cur = nxt;
@@ -191,18 +198,11 @@ void program_backward(dop_program* p, const float* params, const float* dy, floa
                       float* dparams, cudaStream_t s) {
   if (!p->have_tape) throw dop::Error(DOP_E_STATE, "backward called before forward");
   float* cur = p->dbuf[0];
-  if (dy) {
-    DOP_CHECK_CUDA(cudaMemcpyAsync(cur, dy, sizeof(float) * p->output_len, cudaMemcpyDeviceToDevice, s));
-  } else {
-    // sum loss: dy = 1 (src/kernel.rs:237)
-    std::vector<float> ones(p->output_len, 1.0f);
-    DOP_CHECK_CUDA(cudaMemcpyAsync(cur, ones.data(), sizeof(float) * p->output_len,
-                                   cudaMemcpyHostToDevice, s));
-    DOP_CHECK_CUDA(cudaStreamSynchronize(s));
-  }
+  // sum loss when dy is null: dy = 1 (src/kernel.rs:237)
+  DOP_CHECK_CUDA(cudaMemcpyAsync(cur, dy ? dy : p->ones, sizeof(float) * p->output_len,
+                                 cudaMemcpyDeviceToDevice, s));
   struct Side { int64_t at; float* buf; int64_t len; };
   std::vector<Side> side;
-  std::vector<float*> side_bufs;
   auto add_side = [&](int64_t at, float* d, int64_t len) {  // src/kernel.rs:376-388
     for (size_t i = 0; i < side.size();) {
       if (side[i].at == at) {
@@ -215,12 +215,11 @@ void program_backward(dop_program* p, const float* params, const float* dy, floa
   };
   int which = 0;
   int ai = (int)p->attn_out.size();
-  for (auto it = p->stages.rbegin(); it != p->stages.rend(); ++it) {
-    const dop_stage& st = *it;
+  for (size_t si = p->stages.size(); si-- > 0;) {
+    const dop_stage& st = p->stages[si];
     float* nxt = p->dbuf[(which + 1) % 2];
     if (st.kind == DOP_STAGE_ADD) {
-      float* b = p->alloc(st.len);
-      side_bufs.push_back(b);
+      float* b = p->side_buf[si];
       DOP_CHECK_CUDA(cudaMemcpyAsync(b, cur, sizeof(float) * st.len, cudaMemcpyDeviceToDevice, s));
       side.push_back({st.from, b, st.len});
     } else if (st.kind == DOP_STAGE_GEMM) {
@@ -231,12 +230,14 @@ void program_backward(dop_program* p, const float* params, const float* dy, floa
       gx.A = cur; gx.lda = st.dout;
       gx.B = params + st.param_at; gx.ldb = st.dout; gx.b_t = true;
       gx.C = nxt; gx.ldc = st.din;
+      gx.ws = p->split_ws; gx.ws_cap = p->split_cap;
       dop::gemm_simt<float>(gx, s, p->launches);
       dop::Gemm gw;  // dW = x^T dy (assigned, src/kernel.rs:342)
       gw.M = st.din; gw.N = st.dout; gw.K = st.batch;
       gw.A = xs; gw.lda = st.din; gw.a_t = true;
       gw.B = cur; gw.ldb = st.dout;
       gw.C = dparams + st.param_at; gw.ldc = st.dout;
+      gw.ws = p->split_ws; gw.ws_cap = p->split_cap;
       dop::gemm_simt<float>(gw, s, p->launches);
       // db = sum_m dy (assigned, src/kernel.rs:345-351)
       dop::col_sum(cur, st.batch, st.dout, dparams + st.param_at + st.din * st.dout, p->part,
@@ -264,12 +265,6 @@ void program_backward(dop_program* p, const float* params, const float* dy, floa
   }
   if (!side.empty()) throw dop::Error(DOP_E_STATE, "skip cotangent had no saved activation");
   DOP_CHECK_CUDA(cudaMemcpyAsync(dx, cur, sizeof(float) * p->input_len, cudaMemcpyDeviceToDevice, s));
-  DOP_CHECK_CUDA(cudaStreamSynchronize(s));
-  for (float* b : side_bufs) {
-    auto itb = std::find(p->owned.begin(), p->owned.end(), b);
-    if (itb != p->owned.end()) p->owned.erase(itb);
-    cudaFree(b);
-  }
 }
 }  // namespace
 
@@ -518,6 +513,20 @@ int dop_program_create(const dop_stage* stages, int64_t n_stages, int64_t input_
     p->dv = p->alloc(cap);
     p->part_cap = 64 * max_cols;
     p->part = p->alloc(p->part_cap);
+    for (const dop_stage& st : p->stages)
+      p->side_buf.push_back(st.kind == DOP_STAGE_ADD ? p->alloc(st.len) : nullptr);
+    p->ones = p->alloc(output_len);
+    int64_t widest = 1;
+    for (const dop_stage& st : p->stages)
+      if (st.kind == DOP_STAGE_GEMM)
+        widest = std::max({widest, st.din * st.dout, st.batch * st.din, st.batch * st.dout});
+    p->split_cap = std::min<int64_t>(1 << 22, 16 * widest);
+    p->split_ws = p->alloc(p->split_cap);
+    {
+      std::vector<float> h(std::max<int64_t>(output_len, 1), 1.0f);
+      DOP_CHECK_CUDA(cudaMemcpy(p->ones, h.data(), sizeof(float) * h.size(),
+                                cudaMemcpyHostToDevice));
+    }
     (void)max_rows;
     *out = p.release();
   });
@@ -526,6 +535,8 @@ int dop_program_create(const dop_stage* stages, int64_t n_stages, int64_t input_
 int dop_program_destroy(dop_program* p) {
   return guarded([&] { delete p; });
 }
+
+int64_t dop_program_launches(const dop_program* p) { return p ? p->launches : -1; }
 
 int dop_program_forward(dop_program* p, const float* x, const float* params, float* y, void* s) {
   return guarded([&] {

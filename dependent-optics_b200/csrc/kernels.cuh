@@ -99,6 +99,9 @@ struct Gemm {
   const float* bias = nullptr; uint8_t* mask = nullptr; bool relu = false;
   int group = 0; const int* seg_off = nullptr; const int* tile_expert = nullptr; int G = 0;
   int64_t b_gs = 0, c_gs = 0;
+  // CUDA-core path: fp32 scratch (ws_cap floats) for split-contraction
+  // partials; without it a narrow problem runs unsplit
+  float* ws = nullptr; int64_t ws_cap = 0;
 };
 template <typename T>
 void gemm_simt(const Gemm& g, cudaStream_t s, int64_t& launches);

@@ -104,6 +104,7 @@ SIGNATURES = [
     ("dop_program_create", C.c_int, [C.POINTER(StageC), _I64, _I64, _I64, _I64, _I64, _I64,
                                      C.POINTER(_P)]),
     ("dop_program_destroy", C.c_int, [_P]),
+    ("dop_program_launches", _I64, [_P]),
     ("dop_program_forward", C.c_int, [_P, _P, _P, _P, _P]),
     ("dop_program_backward", C.c_int, [_P, _P, _P, _P, _P, _P]),
     ("dop_program_forward_backward", C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P]),

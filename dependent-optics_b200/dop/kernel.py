@@ -151,6 +151,10 @@ class CompiledProgram:
     def __del__(self):
         self.close()
 
+    def launches(self) -> int:
+        """Kernels launched on this handle since creation."""
+        return int(lib().dop_program_launches(self._h))
+
     def forward(self, x, params, stream=None):
         import torch
         y = torch.empty(self.prog.output_len, dtype=torch.float32, device=x.device)
@@ -178,10 +182,11 @@ def forward_backward(prog: Program, x, params, dy=None):
         cp.close()
 
 
-def mse_loss_grad(y, target):
+def mse_loss_grad(y, target, stream=None):
     """MSE head: (loss, dy) with loss = mean((y-t)^2), dy = 2 (y-t) / n."""
     import torch
     loss = torch.empty((), dtype=torch.float32, device=y.device)
     dy = torch.empty_like(y)
-    check(lib().dop_mse_loss_grad(ptr(y), ptr(target), y.numel(), ptr(loss), ptr(dy), None))
+    check(lib().dop_mse_loss_grad(ptr(y), ptr(target), y.numel(), ptr(loss), ptr(dy),
+                                  stream_ptr(stream)))
     return loss, dy

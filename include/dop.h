@@ -223,7 +223,11 @@ int dop_program_create(const dop_stage* stages, int64_t n_stages,
                        int64_t param_len, int64_t tape_f32, int64_t tape_u8,
                        dop_program** out);
 int dop_program_destroy(dop_program* prog);
-/* get: y = program(x); the residual stays in the handle. */
+/* Number of kernels the library launched on this handle since creation. */
+int64_t dop_program_launches(const dop_program* prog);
+/* get: y = program(x); the residual stays in the handle.  Forward and
+ * backward only enqueue work on `stream` (no allocation, no host
+ * synchronisation), so a training step can be captured in a CUDA graph. */
 int dop_program_forward(dop_program* prog, const float* x, const float* params,
                         float* y, void* stream);
 /* put: dy (NULL = the crate's sum loss, dy = 1, src/kernel.rs:237) ->

@@ -165,6 +165,23 @@ def test_f32_block_c2_widths(cuda):
     compare(cfg, gpu, ref, F32_TOL)
 
 
+def test_f32_block_long_contraction(cuda):
+    """batch 4, seq 200: the weight gradients contract over 800 tokens into
+    64-wide outputs, which the CUDA-core GEMM splits over the contraction
+    (partials summed in split order)."""
+    cfg = small_cfg()
+    lp, x, dy = make_inputs(cfg, 4, 200, seed=4)
+    gpu = run_gpu(cfg, 4, 200, lp, x, dy, DOP_F32)
+    ref = run_oracle(cfg, 4, 200, lp, x, dy)
+    forced = check_routing(cfg, gpu, ref, 1e-6, 0.01)
+    if forced is not None:
+        ref = run_oracle(cfg, 4, 200, lp, x, dy, forced=forced)
+    compare(cfg, gpu, ref, F32_TOL)
+    again = run_gpu(cfg, 4, 200, lp, x, dy, DOP_F32)
+    for k in ("y", "dx", "dP"):
+        assert np.array_equal(gpu[k], again[k]), k
+
+
 @pytest.mark.parametrize("kind", ["moe", "dense", "moe-hd128"])
 def test_bf16_block_matches_oracle_on_rounded_inputs(cuda, kind):
     if kind == "moe":
