@@ -17,9 +17,10 @@
 //   combine (bwd)    each source sums the expert-input cotangents of its
 //                    pairs from the owners (k_ep_unpermute_router_dx).
 // Receive buffers are expert-major: local expert j's rows from source 0, 1,
-// ...; each (expert, source) piece keeps the source's 128-row padding, so a
-// GEMM row tile belongs to one expert and the weight-gradient contraction of
-// expert j runs over one contiguous range.
+// ...; each (expert, source) piece keeps the source's segment padding (a
+// multiple of 256 rows, the pair GEMM's tile), so a GEMM row tile belongs to
+// one expert and the weight-gradient contraction of expert j runs over one
+// contiguous range.
 //
 // Ordering between ranks uses four flag barriers per step (k_ep_barrier):
 // after the permutation (sources' rows readable), after the down projection
