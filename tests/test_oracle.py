@@ -158,3 +158,12 @@ def test_oracle_block_matches_float64_autograd(kw):
     assert rel(r.y, y64.detach().numpy().reshape(-1)) < 1e-5
     assert rel(dx, x64.grad.numpy().reshape(-1)) < 1e-4
     assert rel(dlp, lp64.grad.numpy()) < 1e-4
+    # the vectorised model (the referee of the full-size GPU check) agrees too
+    lpb = torch.tensor(lp, dtype=torch.float64, requires_grad=True)
+    xb = torch.tensor(x, dtype=torch.float64).view(batch * seq, c.dim).requires_grad_(True)
+    yb, _, top_b = torch_block.block_forward_batched(c, lpb, xb, seq)
+    (yb * torch.tensor(dy, dtype=torch.float64).view_as(yb)).sum().backward()
+    assert np.array_equal(top_b.numpy(), r.routing()[0])
+    assert rel(r.y, yb.detach().numpy().reshape(-1)) < 1e-5
+    assert rel(dx, xb.grad.numpy().reshape(-1)) < 1e-4
+    assert rel(dlp, lpb.grad.numpy()) < 1e-4

@@ -97,3 +97,57 @@ def block_forward(cfg, lp, x, batch, seq, bias=None):
         rows.append(acc)
     mixed = torch.stack(rows)
     return mid + mixed, top_i
+
+
+def block_forward_batched(cfg, lp, x, seq, forced_top_i=None):
+    """The same block on any device, vectorised over tokens: x is [T, D] for
+    T = n * seq tokens of n sequences; lp the layer's parameters (leaf
+    tensor; autograd flows into it).  Expert selection is by (prob desc,
+    index asc); `forced_top_i` [T, k] replaces it (the indices carry no
+    gradient).  Returns (y, probs, top_i)."""
+    p = split_layer(cfg, lp)
+    H, KV, hd = cfg.heads, cfg.kv_heads, cfg.head_dim
+    T, D = x.shape
+    n = T // seq
+    dev = x.device
+    xn = rmsnorm(x, p["attn_norm"], cfg.rms_eps)
+    half = hd // 2
+    i = torch.arange(half, dtype=torch.float32, device=dev)
+    freq = torch.tensor(cfg.rope_theta, dtype=torch.float32, device=dev) ** (-(2.0 * i) / hd)
+    ang = (torch.arange(T, device=dev) % seq).to(torch.float32)[:, None] * freq[None, :]
+    cos, sin = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
+
+    def rot(t, heads):
+        th = t.view(T, heads, hd)
+        a, b = th[..., :half], th[..., half:]
+        return torch.cat([a * cos - b * sin, b * cos + a * sin], -1)
+
+    q = rot(xn @ p["q"], H).view(n, seq, H, hd).transpose(1, 2)
+    k = rot(xn @ p["k"], KV).view(n, seq, KV, hd).transpose(1, 2)
+    v = (xn @ p["v"]).view(n, seq, KV, hd).transpose(1, 2)
+    k = k.repeat_interleave(H // KV, dim=1)
+    v = v.repeat_interleave(H // KV, dim=1)
+    iq = torch.arange(seq, device=dev)[:, None]
+    jk = torch.arange(seq, device=dev)[None, :]
+    vis = (jk <= iq) & (iq - jk < cfg.sliding_window)
+    s = (q @ k.transpose(-1, -2)) / (hd ** 0.5)
+    pr = torch.softmax(s.masked_fill(~vis, float("-inf")), -1)
+    mix = (pr @ v).transpose(1, 2).reshape(T, H * hd)
+    mid = x + mix @ p["o"]
+    xn2 = rmsnorm(mid, p["ffn_norm"], cfg.rms_eps)
+    probs = torch.softmax(xn2 @ p["router"], -1)
+    with torch.no_grad():
+        order = torch.sort(probs, dim=-1, descending=True, stable=True).indices
+        top_i = order[:, : cfg.top_k]
+    sel = top_i if forced_top_i is None else forced_top_i
+    ps = probs.gather(1, sel)
+    w = ps / ps.sum(-1, keepdim=True)
+    mixed = torch.zeros_like(x)
+    for e in range(cfg.experts):
+        tok, slot = (sel == e).nonzero(as_tuple=True)
+        if tok.numel() == 0:
+            continue
+        xe = xn2[tok]
+        h = torch.nn.functional.silu(xe @ p["gate"][e]) * (xe @ p["up"][e])
+        mixed = mixed.index_add(0, tok, w[tok, slot, None] * (h @ p["down"][e]))
+    return mid + mixed, probs, top_i
