@@ -4,8 +4,11 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
 
 One step is one pass of the block lens over one batch: zero the parameter
-adjoint, forward (get), backward (put) and, with N > 1 GPUs, the
-data-parallel reduction of the parameter adjoint over NCCL.  Inputs are
+adjoint, forward (get), backward (put) and, with N > 1 GPUs, the exchange of
+the expert-parallel block (or the data-parallel reduction of the parameter
+adjoint over NCCL).  The stack workload runs the staged plan of four blocks
+(one step = the global batch through every block); the MLP workload runs the
+kernel.rs program (forward, MSE head, backward) from a CUDA graph.  Inputs are
 seeded synthetic tensors of the workload's shapes (no dataset exists for this
 path): matrices ~ N(0, 0.02^2), RMSNorm weights 1, x and dy ~ N(0, 1).
 
