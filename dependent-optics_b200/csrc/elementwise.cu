@@ -88,6 +88,70 @@ __device__ void router_select(const float* lg, int nw, const float* bias, int E,
   }
 }
 
+// router_select run by one warp (all 32 lanes call it): lane e < E holds
+// expert e's logit, the selection is K rounds of a warp argmax (probability
+// desc, index asc).  The per-expert partial sums, the softmax denominator
+// (expert order) and the top-k weight sum (selection order) are summed in
+// router_select's order, so the results are bit-identical, without its
+// per-thread arrays in local memory.
+__device__ void router_select_warp(const float* lg, int nw, const float* bias, int E, int K,
+                                   int64_t row, float* probs, int* top_i, float* top_p,
+                                   float* top_w) {
+  const int lane = threadIdx.x & 31;
+  const bool on = lane < E;
+  float z = -INFINITY;
+  if (on) {
+    float v = 0.f;
+    for (int q = 0; q < nw; ++q) v += lg[q * kMaxExperts + lane];
+    if (bias) v += bias[lane];
+    z = v;
+  }
+  const float m = warp_max(z);
+  const float pe = on ? expf(z - m) : 0.f;
+  float s = 0.f;
+  for (int e = 0; e < E; ++e) s += __shfl_sync(0xffffffffu, pe, e);
+  const float p = pe / s;
+  if (on) probs[row * E + lane] = p;
+  float cand = on ? p : -1.f;
+  float pk[kMaxTopK];
+  int ik[kMaxTopK];
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) {
+    pk[k] = 0.f;
+    ik[k] = 0;
+    if (k < K) {
+      float bv = cand;
+      int bi = lane;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      pk[k] = bv;
+      ik[k] = bi;
+      if (lane == bi) cand = -1.f;
+    }
+  }
+  if (lane == 0) {
+    float sk = 0.f;
+#pragma unroll
+    for (int k = 0; k < kMaxTopK; ++k)
+      if (k < K) sk += pk[k];
+#pragma unroll
+    for (int k = 0; k < kMaxTopK; ++k) {
+      if (k < K) {
+        top_i[row * K + k] = ik[k];
+        top_p[row * K + k] = pk[k];
+        top_w[row * K + k] = pk[k] / sk;
+      }
+    }
+  }
+}
+
 // RMSNorm of the feed-forward input fused with the router (src/mixtral.rs:
 // 311-327, softmax :924-929, topk_renorm :931-939).  Router logits are
 // computed in fp32 from the fp32 normalised row (not from its rounded copy),
@@ -265,7 +329,7 @@ __global__ void __launch_bounds__(256) k_rmsnorm_router_v(
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) router_select(lg, 8, bias, E, K, row, probs, top_i, top_p, top_w);
+  if (threadIdx.x < 32) router_select_warp(lg, 8, bias, E, K, row, probs, top_i, top_p, top_w);
 }
 
 // Xp[r] = xn[row_token[r]] in 16-byte words (zero rows for padding).
@@ -376,6 +440,57 @@ __global__ void k_rmsnorm_bwd_rows(const float* __restrict__ dy, const float* __
       if (res) v += res[row * D + i];
       dx[row * D + i] = v;
       if (dx_act) st(&dx_act[row * D + i], v);
+    }
+  }
+}
+
+// The same adjoint with one CTA per row and the row's dy, x and residual
+// cotangent loaded before the reduction and held in registers until the
+// output pass (NV quads per thread), so each is read from DRAM once and no
+// load waits behind the reduction.
+template <typename T, int NV>
+__global__ void __launch_bounds__(256) k_rmsnorm_bwd_v(const float* __restrict__ dy,
+                                                       const float* __restrict__ x,
+                                                       const float* __restrict__ inv,
+                                                       const T* __restrict__ w,
+                                                       const float* __restrict__ res, int D,
+                                                       float* __restrict__ dx,
+                                                       T* __restrict__ dx_act) {
+  const int64_t row = blockIdx.x;
+  const int D4 = D >> 2;
+  const float r = inv[row];
+  __shared__ float red[33];
+  float4 xv[NV], gv[NV], rv[NV];
+  float dot = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * 256;
+    if (i < D4) {
+      xv[j] = ld4(x + row * D + 4 * i);
+      gv[j] = ld4(dy + row * D + 4 * i);
+      if (res) rv[j] = ld4(res + row * D + 4 * i);
+      const float4 wv = ld4(w + 4 * i);
+      dot += (gv[j].x * wv.x) * (xv[j].x * r) + (gv[j].y * wv.y) * (xv[j].y * r) +
+             (gv[j].z * wv.z) * (xv[j].z * r) + (gv[j].w * wv.w) * (xv[j].w * r);
+    }
+  }
+  const float mean = block_sum(dot, red) / (float)D;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * 256;
+    if (i < D4) {
+      const float4 wv = ld4(w + 4 * i);
+      const float4 xq = xv[j], gq = gv[j];
+      float4 o;
+      o.x = r * (gq.x * wv.x - (xq.x * r) * mean);
+      o.y = r * (gq.y * wv.y - (xq.y * r) * mean);
+      o.z = r * (gq.z * wv.z - (xq.z * r) * mean);
+      o.w = r * (gq.w * wv.w - (xq.w * r) * mean);
+      if (res) {
+        o.x += rv[j].x; o.y += rv[j].y; o.z += rv[j].z; o.w += rv[j].w;
+      }
+      st4(dx + row * D + 4 * i, o);
+      if (dx_act) st4(dx_act + row * D + 4 * i, o);
     }
   }
 }
@@ -779,6 +894,61 @@ __global__ void k_router_dw(const float* __restrict__ mid, const float* __restri
     if (e < E) part[((int64_t)c * D + i) * E + e] = acc[e];
 }
 
+// k_router_dw for 8 experts with four columns a thread and eight rows' loads
+// in flight (the scalar kernel has one 4-byte load in flight per thread and
+// is latency-bound).  Same products summed in the same row order per
+// element, so the partials are bit-identical to k_router_dw's.
+template <typename T>
+__global__ void __launch_bounds__(128) k_router_dw_v(const float* __restrict__ mid,
+                                                     const float* __restrict__ inv,
+                                                     const T* __restrict__ w,
+                                                     const float* __restrict__ dz, int64_t rows,
+                                                     int D, int rows_per_chunk,
+                                                     float* __restrict__ part) {
+  constexpr int E = 8, U = 8;
+  const int i4 = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  const int c = blockIdx.y;
+  if (i4 >= D) return;
+  const int64_t t0 = (int64_t)c * rows_per_chunk;
+  const int64_t t1 = ::min((int64_t)rows, t0 + rows_per_chunk);
+  float acc[4][E];
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[q][e] = 0.f;
+  const float4 wv = ld4(w + i4);
+  const float wq[4] = {wv.x, wv.y, wv.z, wv.w};
+  for (int64_t t = t0; t < t1; t += U) {
+    float4 mv[U];
+    float iv[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (t + u < t1) {
+        mv[u] = ld4(mid + (t + u) * D + i4);
+        iv[u] = inv[t + u];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (t + u < t1) {
+        const float4 d0 = ld4(dz + (t + u) * E), d1 = ld4(dz + (t + u) * E + 4);
+        const float dv[E] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+        const float mq[4] = {mv[u].x, mv[u].y, mv[u].z, mv[u].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float xn = mq[q] * iv[u] * wq[q];
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[q][e] += xn * dv[e];
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int e = 0; e < E; ++e) part[((int64_t)c * D + i4 + q) * E + e] = acc[q][e];
+}
+
 // --------------------------------------------------------------- misc
 template <typename T>
 __global__ void k_convert(const float* __restrict__ s, T* __restrict__ d, int64_t n) {
@@ -909,8 +1079,15 @@ void rmsnorm_bwd(const float* dy, const float* x, const float* inv, const T* w,
                  float* part_buf, int64_t part_cap, cudaStream_t s, int64_t& launches) {
   const bool vec = D % 128 == 0 && aligned4(dy) && aligned4(x) && aligned4(w) &&
                    (!res || aligned4(res)) && aligned4(dx) && (!dx_act || aligned4(dx_act));
-  k_rmsnorm_bwd_rows<T><<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(dy, x, inv, w, res, rows, D,
-                                                                     dx, dx_act, vec);
+  const int nv = row_quads(D);
+  if (vec && nv) {
+    auto k = nv == 1 ? k_rmsnorm_bwd_v<T, 1> : nv == 2 ? k_rmsnorm_bwd_v<T, 2>
+           : nv == 4 ? k_rmsnorm_bwd_v<T, 4> : k_rmsnorm_bwd_v<T, 8>;
+    k<<<(unsigned)rows, 256, 0, s>>>(dy, x, inv, w, res, D, dx, dx_act);
+  } else {
+    k_rmsnorm_bwd_rows<T><<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(dy, x, inv, w, res, rows,
+                                                                       D, dx, dx_act, vec);
+  }
   DOP_LAUNCHED(launches);
   int64_t chunks = std::max<int64_t>(1, std::min<int64_t>(rows, 64));
   int rows_per_chunk = (int)ceil_div(rows, chunks);
@@ -1041,8 +1218,13 @@ void router_dw(const float* mid, const float* inv, const T* w, const float* dz, 
   int rows_per_chunk = (int)ceil_div(rows, chunks);
   chunks = ceil_div(rows, rows_per_chunk);
   DOP_REQUIRE(chunks * D * E <= part_cap, "partial buffer too small");
-  dim3 grid((unsigned)ceil_div(D, 128), (unsigned)chunks);
-  k_router_dw<T><<<grid, 128, 0, s>>>(mid, inv, w, dz, rows, D, E, rows_per_chunk, part_buf);
+  if (E == 8 && D % 4 == 0 && aligned4(mid) && aligned4(w) && aligned4(dz)) {
+    dim3 grid((unsigned)ceil_div(D / 4, 128), (unsigned)chunks);
+    k_router_dw_v<T><<<grid, 128, 0, s>>>(mid, inv, w, dz, rows, D, rows_per_chunk, part_buf);
+  } else {
+    dim3 grid((unsigned)ceil_div(D, 128), (unsigned)chunks);
+    k_router_dw<T><<<grid, 128, 0, s>>>(mid, inv, w, dz, rows, D, E, rows_per_chunk, part_buf);
+  }
   DOP_LAUNCHED(launches);
   k_reduce_chunks<<<(unsigned)ceil_div((int64_t)D * E, 256), 256, 0, s>>>(part_buf, (int)chunks,
                                                                            (int64_t)D * E, dwr_accum);
