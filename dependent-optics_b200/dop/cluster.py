@@ -11,6 +11,12 @@ a rank posts a window's inbound messages just before its compute and its
 outbound messages right after it, grouping the sends of one window with the
 receives of the next into one batch, so that two stages exchanging an
 activation and an adjoint in opposite directions never wait on each other.
+A message whose route passes through other devices (sparse links) is
+forwarded by each of them at the consuming window: the relay receives its
+hop and sends the next one at once.  Receives from a rank are posted in the
+order that rank sends (`StagePlan.p2p_order`), so point-to-point matching
+pairs each send with its own receive when relayed and direct messages share
+a pair of ranks.
 Sgd windows sum each block's adjoint over the data-parallel replicas that
 hold it (an all-reduce in the replicas' group) and apply `p -= lr * dp` when
 lr is not zero.  Every rank records the events it performed in the crate's
@@ -193,15 +199,43 @@ class StagePlan:
         return buf.value.decode().splitlines()
 
     def rank_trace(self, r: int) -> list:
-        """The events rank r performs: its inbound hops and computes, and the
-        outbound hops it sends, in plan order."""
+        """The events rank r performs, in plan order: at each window its
+        inbound hops (a relay on the message's route receives its hop and
+        forwards the next one there), its compute, and the first hop of the
+        window's outbound message when r produced it."""
         out = []
         for w in self.windows:
-            out += [_hop_line(h) for h in w.inbound if h.dst == r]
+            for i, h in enumerate(w.inbound):
+                if h.dst == r or (w.exec == EXEC_BLOCK and i > 0 and h.src == r):
+                    out.append(_hop_line(h))
             if w.device == r:
                 out.append(f"COMPUTE {w.device} {w.exec} {w.pass_}")
-            out += [_hop_line(h) for h in w.outbound if h.src == r]
+            if w.outbound and w.outbound[0].src == r:
+                out.append(_hop_line(w.outbound[0]))
         return out
+
+    def p2p_order(self) -> dict:
+        """{(src, dst): hops in the order src posts them}.  A message's first
+        hop is posted by its producer right after the producing window, each
+        later hop by its relay at the consuming window (in route order).  A
+        receiver posts its receives from src in this order, so point-to-point
+        matching (which follows posting order per pair of ranks) pairs every
+        send with its own receive even when relayed and direct messages share
+        a pair of ranks.  Sgd inbound hops are all-reduces, not messages."""
+        produced_at = {}
+        for w in self.windows:
+            if w.exec == EXEC_BLOCK and w.outbound:
+                produced_at[w.outbound[0].index] = w.index
+        posts = []
+        for w in self.windows:
+            if w.exec != EXEC_BLOCK or not w.inbound:
+                continue
+            posts.append((produced_at[w.inbound[0].index], 0, w.inbound[0]))
+            posts += [(w.index, i, h) for i, h in enumerate(w.inbound) if i > 0]
+        order = {}
+        for _, _, h in sorted(posts, key=lambda t: (t[0], t[1])):
+            order.setdefault((h.src, h.dst), []).append(h)
+        return order
 
     def slots(self, device: int) -> dict:
         """{layer: residual slots} of the blocks homed on `device`."""
@@ -266,6 +300,9 @@ def run_plan(plan: StagePlan, rank: int, lens_for, params, dparams, inputs, cota
     import torch.distributed as dist
 
     n_layers = 1 + max(w.layer for w in plan.windows)
+    order = plan.p2p_order()
+    cursor, posted = {}, set()   # per source: next hop of order[(src, rank)] to post
+    arrived = {}                 # hop index -> received tensor
     acts, cots = {}, {}
     outputs, input_grads, trace = {}, {}, []
     pending = []   # (op, hop, tensor) posted at the next flush
@@ -284,18 +321,42 @@ def run_plan(plan: StagePlan, rank: int, lens_for, params, dparams, inputs, cota
             w.wait()
         for op, h, t in pending:
             if op == "recv":
-                if h.kind == HOP_ACTIVATION:
-                    acts[(h.layer + 1, h.micro)] = t
-                else:
-                    cots[(h.layer - 1, h.micro)] = t
+                arrived[h.index] = t
         pending.clear()
         keep.clear()
 
+    def want(h):
+        """Post the receives from h.src up to h, in the order h.src sends."""
+        if h.index in posted:
+            return
+        seq = order[(h.src, rank)]
+        k = cursor.get(h.src, 0)
+        while True:
+            g = seq[k]
+            k += 1
+            posted.add(g.index)
+            pending.append(("recv", g, make_buffer(g.rows, g.cols)))
+            if g.index == h.index:
+                break
+        cursor[h.src] = k
+
     for w in plan.windows:
-        for h in w.inbound:
-            if h.dst == rank and w.exec == EXEC_BLOCK:
-                pending.append(("recv", h, make_buffer(h.rows, h.cols)))
+        if w.exec == EXEC_BLOCK:
+            for i, h in enumerate(w.inbound):
+                if h.dst != rank:
+                    continue
+                want(h)
                 trace.append(_hop_line(h))
+                if w.device != rank:
+                    # a relay on the message's route: receive, then forward
+                    # the next hop at once (its receiver posts it here too)
+                    flush()
+                    t = arrived.pop(h.index)
+                    nxt = w.inbound[i + 1]
+                    pending.append(("send", nxt, t))
+                    keep.append(t)
+                    trace.append(_hop_line(nxt))
+                    flush()
         if w.device != rank:
             continue
         if w.exec == EXEC_SGD:
@@ -310,6 +371,9 @@ def run_plan(plan: StagePlan, rank: int, lens_for, params, dparams, inputs, cota
             trace.append(f"COMPUTE {w.device} {w.exec} {w.pass_}")
             continue
         flush()
+        if w.inbound:
+            got = arrived.pop(w.inbound[-1].index)
+            (acts if w.pass_ == PASS_FWD else cots)[(w.layer, w.micro)] = got
         lens = lens_for(w.layer, w.slot)
         if w.pass_ == PASS_FWD:
             x = acts.pop((w.layer, w.micro)) if w.layer > 0 else inputs[w.micro]
@@ -328,13 +392,11 @@ def run_plan(plan: StagePlan, rank: int, lens_for, params, dparams, inputs, cota
                 cots[(w.layer - 1, w.micro)] = dx
             result = dx
         trace.append(f"COMPUTE {w.device} {w.exec} {w.pass_}")
-        if len(w.outbound) > 1:
-            raise NotImplementedError("routes through an intermediate device are planned, not run")
-        for h in w.outbound:
-            if h.src == rank:
-                pending.append(("send", h, result))
-                keep.append(result)
-                trace.append(_hop_line(h))
+        if w.outbound:  # the message's first hop; relays carry the rest
+            h = w.outbound[0]
+            pending.append(("send", h, result))
+            keep.append(result)
+            trace.append(_hop_line(h))
     flush()
     return {"outputs": outputs, "input_grads": input_grads, "trace": trace}
 

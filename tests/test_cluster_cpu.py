@@ -157,7 +157,7 @@ def _reference(LAYERS):
     return ys, dxs, dWs
 
 
-def _worker(rank, world, LAYERS, port, q):
+def _worker(rank, world, LAYERS, port, q, links=None):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                           WORLD_SIZE=str(world))
@@ -171,7 +171,7 @@ def _worker(rank, world, LAYERS, port, q):
         parallel.init_from_env("gloo", timeout_s=60.0)
         cfg = small_cfg(LAYERS)
         # ROWS rows per micro-batch: micro-batches of one sequence of ROWS tokens
-        plan = cl.stage_mixtral(cfg, MICRO, ROWS, MICRO, DOP_F32, cl.b200s(world))
+        plan = cl.stage_mixtral(cfg, MICRO, ROWS, MICRO, DOP_F32, cl.b200s(world), links=links)
         groups = {tuple(g): dist.new_group(g) for g in plan.stage_groups()}
         Ws, xs, dys = _data(LAYERS)
         mine = {h.layer for h in plan.homes if h.device == rank and h.kind == cl.HOME_PARAM}
@@ -197,14 +197,30 @@ def _worker(rank, world, LAYERS, port, q):
         q.put((rank, False, 0, traceback.format_exc()))
 
 
-@pytest.mark.parametrize("world,layers", [(2, 4), (4, 2)])
-def test_executor_matches_single_process(world, layers):
+# sparse links: messages between stages that share no link are relayed
+RING3 = [(0, 2), (1, 2)]
+RING4 = [(0, 2), (2, 1), (1, 3), (3, 0)]
+
+
+@pytest.mark.parametrize("world,layers,links", [(2, 4, None), (4, 2, None), (3, 3, RING3),
+                                                (4, 4, RING4)],
+                         ids=["pp2", "pp2xdp2", "pp3-relay", "pp4-relays"])
+def test_executor_matches_single_process(world, layers, links):
     """2 ranks x 4 layers: PP 2, two blocks chained on each GPU; 4 ranks x 2
-    layers: PP 2 x DP 2, replicas' adjoints summed by the Sgd windows."""
+    layers: PP 2 x DP 2, replicas' adjoints summed by the Sgd windows.  With
+    sparse links the planner routes messages through intermediate devices
+    (in the 3-rank case stage 2 relays between stages 0 and 1 while running
+    its own blocks; in the 4-rank ring relayed and direct messages share
+    pairs of ranks), and the executor's relays forward them."""
+    if links:
+        plan = cluster.stage_mixtral(small_cfg(layers), MICRO, ROWS, MICRO, DOP_F32,
+                                     cluster.b200s(world), links=links)
+        assert any(len(w.inbound) > 1 for w in plan.windows if w.exec == cluster.EXEC_BLOCK)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, layers, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, layers, port, q, links))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in range(world)]
