@@ -230,3 +230,61 @@ def test_executor_matches_single_process(world, layers, links):
         assert ok, f"rank {rank}: {err}"
     # every micro-batch's output and input gradient came out somewhere
     assert sum(n for _, _, n, _ in res) == 2 * MICRO
+
+
+def _dying_worker(rank, world, port, q):
+    """Rank 1's first block window raises and its process exits without
+    leaving the group; rank 0 runs the plan until its next exchange with
+    rank 1."""
+    import time
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                          WORLD_SIZE=str(world))
+        import sys
+        root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+        sys.path.insert(0, os.path.join(root, "dependent-optics_b200"))
+        import torch
+        from dop import cluster as cl
+        from dop import parallel
+        parallel.init_from_env("gloo", timeout_s=10.0)
+        cfg = small_cfg(2)
+        plan = cl.stage_mixtral(cfg, MICRO, ROWS, MICRO, DOP_F32, cl.b200s(world))
+        Ws, xs, dys = _data(2)
+        mine = {h.layer for h in plan.homes if h.device == rank and h.kind == cl.HOME_PARAM}
+        dWs = {l: torch.zeros_like(Ws[l]) for l in mine}
+
+        class Dying(LinearLens):
+            def forward(self, W, x):
+                raise RuntimeError("stage died")
+
+        lens = Dying() if rank == 1 else LinearLens()
+        t0 = time.monotonic()
+        try:
+            cl.run_plan(plan, rank, lambda l, s: lens, Ws, dWs, xs, dys,
+                        lambda r, c: torch.empty(r, c))
+            q.put((rank, "finished", time.monotonic() - t0))
+        except Exception as e:  # the failure as this rank sees it
+            q.put((rank, f"error: {type(e).__name__}", time.monotonic() - t0))
+    except Exception:
+        q.put((rank, "setup: " + traceback.format_exc(), 0.0))
+    q.close()
+    q.join_thread()  # the report reaches the parent before the abrupt exit
+    os._exit(0)  # leave without tearing the group down, like a crashed rank
+
+
+def test_executor_reports_a_dead_stage():
+    """A stage that dies between windows: the surviving stage's next
+    point-to-point exchange with it ends with an error (within the process
+    group's 10 s timeout) instead of waiting for good."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict((r, (s, t)) for r, s, t in (q.get(timeout=120) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1][0].startswith("error: RuntimeError"), res
+    assert res[0][0].startswith("error"), res
+    assert res[0][1] < 60.0, res
