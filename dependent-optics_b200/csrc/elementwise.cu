@@ -390,8 +390,9 @@ __global__ void k_combine_v(const float* __restrict__ mid, const float* __restri
 
 // rmsnorm_bwd (src/mixtral.rs:696-723), input cotangent: one warp per row,
 // dx = r (dy*w - xhat * mean(dy*w*xhat)) (+ res), xhat = x r.  Rows are read
-// twice (the second pass hits L2), float4 when D % 128 == 0 and every
-// pointer is 16-byte (fp32) or 8-byte (bf16) aligned.
+// twice (at large T the second pass misses L2), float4 when D % 128 == 0 and
+// every pointer is 16-byte (fp32) or 8-byte (bf16) aligned.  The launcher
+// prefers k_rmsnorm_bwd_v (one read) when D fits one CTA's registers.
 template <typename T>
 __global__ void k_rmsnorm_bwd_rows(const float* __restrict__ dy, const float* __restrict__ x,
                                    const float* __restrict__ inv, const T* __restrict__ w,
