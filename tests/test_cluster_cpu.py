@@ -107,6 +107,34 @@ def test_links_and_routes():
     assert cluster.route_message(sorted(links), free, 2, 4, 50) == [2, 4]
 
 
+def test_p2p_order_covers_every_message_hop_once():
+    """Every hop of every block message appears once, under its own (src,
+    dst) pair; a message's first hop follows its producer's position and its
+    relayed hops follow the consumer's, in route order."""
+    plan = cluster.stage_mixtral(small_cfg(4), 8, 6, 8, DOP_F32, cluster.b200s(4),
+                                 links=[(0, 2), (2, 1), (1, 3), (3, 0)])
+    order = plan.p2p_order()
+    listed = [h.index for hops in order.values() for h in hops]
+    msg_hops = [h.index for w in plan.windows if w.exec == cluster.EXEC_BLOCK for h in w.inbound]
+    assert sorted(listed) == sorted(msg_hops) and len(set(listed)) == len(listed)
+    for (a, b), hops in order.items():
+        assert all((h.src, h.dst) == (a, b) for h in hops)
+    pos = {}
+    produced = {w.outbound[0].index: w.index for w in plan.windows
+                if w.exec == cluster.EXEC_BLOCK and w.outbound}
+    for w in plan.windows:
+        if w.exec == cluster.EXEC_BLOCK and w.inbound:
+            pos[w.inbound[0].index] = (produced[w.inbound[0].index], 0)
+            for i, h in enumerate(w.inbound[1:], 1):
+                pos[h.index] = (w.index, i)
+    for hops in order.values():
+        keys = [pos[h.index] for h in hops]
+        assert keys == sorted(keys)
+    # fully connected B200s: every message is one hop
+    dense = cluster.stage_mixtral(small_cfg(4), 8, 6, 8, DOP_F32, cluster.b200s(4))
+    assert all(len(w.inbound) <= 1 for w in dense.windows if w.exec == cluster.EXEC_BLOCK)
+
+
 # ------------------------------------------------------------ executor
 def _free_port():
     s = socket.socket()
