@@ -239,11 +239,17 @@ def test_executor_matches_single_process(world, layers, links):
     sparse links the planner routes messages through intermediate devices
     (in the 3-rank case stage 2 relays between stages 0 and 1 while running
     its own blocks; in the 4-rank ring relayed and direct messages share
-    pairs of ranks), and the executor's relays forward them."""
+    pairs of ranks), and the executor's relays forward them: the crate's
+    bridge test (src/dist.rs:1008-1053) in this executor's terms, where each
+    hop of a route is one message, sent once and received once."""
     if links:
         plan = cluster.stage_mixtral(small_cfg(layers), MICRO, ROWS, MICRO, DOP_F32,
                                      cluster.b200s(world), links=links)
         assert any(len(w.inbound) > 1 for w in plan.windows if w.exec == cluster.EXEC_BLOCK)
+        n_hops = sum(len(w.inbound) for w in plan.windows if w.exec == cluster.EXEC_BLOCK)
+        hop_events = sum(line.startswith("HOP") for r in range(world)
+                         for line in plan.rank_trace(r))
+        assert hop_events == 2 * n_hops
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
