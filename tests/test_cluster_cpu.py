@@ -119,6 +119,9 @@ def test_p2p_order_covers_every_message_hop_once():
     assert sorted(listed) == sorted(msg_hops) and len(set(listed)) == len(listed)
     for (a, b), hops in order.items():
         assert all((h.src, h.dst) == (a, b) for h in hops)
+    # every message hop follows a link (src/cluster.rs:2174-2230, hops_follow_links)
+    ring = {frozenset(l) for l in [(0, 2), (2, 1), (1, 3), (3, 0)]}
+    assert all(frozenset((h.src, h.dst)) in ring for hops in order.values() for h in hops)
     pos = {}
     produced = {w.outbound[0].index: w.index for w in plan.windows
                 if w.exec == cluster.EXEC_BLOCK and w.outbound}
