@@ -299,6 +299,10 @@ def run_plan(plan: StagePlan, rank: int, lens_for, params, dparams, inputs, cota
     """
     import torch.distributed as dist
 
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    if len(plan.devices) != world or not 0 <= rank < world:
+        raise ValueError(f"the plan has {len(plan.devices)} devices; run_plan needs one process "
+                         f"per device (world size {world}, rank {rank})")
     n_layers = 1 + max(w.layer for w in plan.windows)
     order = plan.p2p_order()
     cursor, posted = {}, set()   # per source: next hop of order[(src, rank)] to post

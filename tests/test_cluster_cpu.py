@@ -138,6 +138,12 @@ def test_p2p_order_covers_every_message_hop_once():
     assert all(len(w.inbound) <= 1 for w in dense.windows if w.exec == cluster.EXEC_BLOCK)
 
 
+def test_executor_needs_one_process_per_device():
+    plan = cluster.stage_mixtral(small_cfg(4), 8, 6, 8, DOP_F32, cluster.b200s(2))
+    with pytest.raises(ValueError, match="one process per device"):
+        cluster.run_plan(plan, 0, None, {}, {}, {}, {}, None)
+
+
 # ------------------------------------------------------------ executor
 def _free_port():
     s = socket.socket()
