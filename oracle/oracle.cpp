@@ -20,14 +20,20 @@
 // experts, SGD descent, tape sizes, parameter counts) and by an independent
 // torch-autograd model of the same block in float64.
 //
-// Build: compiled by oracle/Makefile with -O2 -ffp-contract=off so that, like
-// rustc, no multiply-add is fused.  Rust's f32 exp/ln/powf/sin_cos/sqrt call
-// the platform libm; this file calls the same libm entry points.
+// Build: compiled by oracle/Makefile with -O3 -ffp-contract=off and no
+// fast-math, so that, like rustc, no multiply-add is fused and no sum is
+// reassociated.  Rust's f32 exp/ln/powf/sin_cos/sqrt call the platform libm;
+// this file calls the same libm entry points.  Loop nests are interchanged
+// and threaded only where every output keeps the crate's accumulation
+// sequence (see `g_literal` below); orc_set_literal(1) runs the crate's
+// literal loop order instead, and the two give the same bytes.
 
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <atomic>
+#include <thread>
 #include <vector>
 
 #include "../include/dop.h"
@@ -76,8 +82,55 @@ LL layer_layout(const Cfg& c) {
   return l;
 }
 
-// linear (src/mixtral.rs:616-628)
-vecf linear(const float* x, const float* w, int64_t n, int64_t din, int64_t dout) {
+// Loop order.  The crate's `linear`/`linear_bwd` walk the weight matrix
+// column by column (stride dout); restated literally that takes minutes per
+// token at the Mixtral-8x7B widths.  By default the loop nests below are
+// interchanged and split over OpenMP threads ONLY where every output keeps
+// the crate's accumulation sequence: each y[m][o] still starts at 0.0f and
+// adds x[m][k] * w[k][o] for k = 0, 1, ... in order, each dw[k][o] adds its
+// terms for m = 0, 1, ... in order, and reductions over a contiguous index
+// (dx) are still one sequential sum per output.  Without -ffast-math and with
+// -ffp-contract=off the results are therefore bit-identical to the literal
+// loops, which orc_set_literal(1) selects (tests/test_oracle.py compares the
+// two modes byte for byte).
+int g_literal = 0;
+int g_threads = 0;  // 0: every hardware thread
+
+int oracle_threads() {
+  if (g_threads > 0) return g_threads;
+  unsigned h = std::thread::hardware_concurrency();
+  return h ? (int)h : 1;
+}
+
+// f(i) for i in [0, n): in order on this thread when `par` is false (or in
+// literal mode), else on up to oracle_threads() threads taking grains of
+// consecutive indices.  Callers only split work whose outputs are disjoint.
+template <class F>
+void par_for(int64_t n, bool par, F&& f) {
+  int nt = oracle_threads();
+  if (!par || g_literal || nt <= 1 || n <= 1) {
+    for (int64_t i = 0; i < n; ++i) f(i);
+    return;
+  }
+  const int64_t grain = std::max<int64_t>(1, n / (8 * (int64_t)nt));
+  std::atomic<int64_t> next(0);
+  auto work = [&]() {
+    for (;;) {
+      const int64_t i0 = next.fetch_add(grain);
+      if (i0 >= n) return;
+      const int64_t i1 = std::min(n, i0 + grain);
+      for (int64_t i = i0; i < i1; ++i) f(i);
+    }
+  };
+  const int64_t extra = std::min<int64_t>(nt, (n + grain - 1) / grain) - 1;
+  std::vector<std::thread> pool;
+  for (int64_t t = 0; t < extra; ++t) pool.emplace_back(work);
+  work();
+  for (auto& t : pool) t.join();
+}
+
+// linear (src/mixtral.rs:616-628), literal loop order
+vecf linear_lit(const float* x, const float* w, int64_t n, int64_t din, int64_t dout) {
   vecf y(n * dout, 0.0f);
   for (int64_t m = 0; m < n; ++m)
     for (int64_t o = 0; o < dout; ++o) {
@@ -88,9 +141,31 @@ vecf linear(const float* x, const float* w, int64_t n, int64_t din, int64_t dout
   return y;
 }
 
-// linear_bwd (src/mixtral.rs:630-659)
-void linear_bwd(const float* x, const float* dy, const float* w, int64_t n, int64_t din,
-                int64_t dout, vecf& dx, vecf& dw) {
+// linear (src/mixtral.rs:616-628): jobs of (8 rows, 128 columns), k ascending
+vecf linear(const float* x, const float* w, int64_t n, int64_t din, int64_t dout) {
+  if (g_literal) return linear_lit(x, w, n, din, dout);
+  vecf y(n * dout, 0.0f);
+  const int64_t MB = 8, OB = 128;
+  const int64_t nmb = (n + MB - 1) / MB, nob = (dout + OB - 1) / OB;
+  float* yp = y.data();
+  par_for(nmb * nob, n * din * dout > (1 << 18), [&](int64_t job) {
+    const int64_t m0 = (job / nob) * MB, m1 = std::min(n, m0 + MB);
+    const int64_t o0 = (job % nob) * OB, o1 = std::min(dout, o0 + OB);
+    for (int64_t k = 0; k < din; ++k) {
+      const float* wr = w + k * dout;
+      for (int64_t m = m0; m < m1; ++m) {
+        const float xk = x[m * din + k];
+        float* yr = yp + m * dout;
+        for (int64_t o = o0; o < o1; ++o) yr[o] += xk * wr[o];
+      }
+    }
+  });
+  return y;
+}
+
+// linear_bwd (src/mixtral.rs:630-659), literal loop order
+void linear_bwd_lit(const float* x, const float* dy, const float* w, int64_t n, int64_t din,
+                    int64_t dout, vecf& dx, vecf& dw) {
   dx.assign(n * din, 0.0f);
   dw.assign(din * dout, 0.0f);
   for (int64_t m = 0; m < n; ++m)
@@ -105,6 +180,62 @@ void linear_bwd(const float* x, const float* dy, const float* w, int64_t n, int6
       for (int64_t m = 0; m < n; ++m) acc += x[m * din + k] * dy[m * dout + o];
       dw[k * dout + o] = acc;
     }
+}
+
+// linear_bwd (src/mixtral.rs:630-659): dx one sequential sum per output;
+// dw row k accumulates the rows m = 0, 1, ... in order
+void linear_bwd(const float* x, const float* dy, const float* w, int64_t n, int64_t din,
+                int64_t dout, vecf& dx, vecf& dw) {
+  if (g_literal) return linear_bwd_lit(x, dy, w, n, din, dout, dx, dw);
+  dx.assign(n * din, 0.0f);
+  dw.assign(din * dout, 0.0f);
+  float* dxp = dx.data();
+  float* dwp = dw.data();
+  const bool par = n * din * dout > (1 << 18);
+  par_for(din * n, par, [&](int64_t job) {
+    const int64_t k = job / n, m = job % n;
+    const float* wr = w + k * dout;
+    const float* dyr = dy + m * dout;
+    float acc = 0.0f;
+    for (int64_t o = 0; o < dout; ++o) acc += dyr[o] * wr[o];
+    dxp[m * din + k] = acc;
+  });
+  par_for(din, par, [&](int64_t k) {
+    float* dr = dwp + k * dout;
+    for (int64_t m = 0; m < n; ++m) {
+      const float xk = x[m * din + k];
+      const float* dyr = dy + m * dout;
+      for (int64_t o = 0; o < dout; ++o) dr[o] += xk * dyr[o];
+    }
+  });
+}
+
+// The crate's per-token expert adjoint: linear_bwd on one row (n = 1)
+// followed by add_assign of its dw into `grad` (src/mixtral.rs:463-475).
+// The dw of one row is the single product 0.0f + x[k] * dy[o]; the default
+// mode adds that same value into grad in the same pass.
+void linear_bwd_row_acc(const float* x, const float* dy, const float* w, int64_t din,
+                        int64_t dout, vecf& dx, float* grad) {
+  if (g_literal) {
+    vecf dw;
+    linear_bwd_lit(x, dy, w, 1, din, dout, dx, dw);
+    for (int64_t i = 0; i < din * dout; ++i) grad[i] += dw[i];
+    return;
+  }
+  dx.assign(din, 0.0f);
+  float* dxp = dx.data();
+  par_for(din, din * dout > (1 << 18), [&](int64_t k) {
+    const float* wr = w + k * dout;
+    float acc = 0.0f;
+    for (int64_t o = 0; o < dout; ++o) acc += dy[o] * wr[o];
+    dxp[k] = acc;
+    const float xk = x[k];
+    float* g = grad + k * dout;
+    for (int64_t o = 0; o < dout; ++o) {
+      const float p = xk * dy[o];
+      g[o] += 0.0f + p;
+    }
+  });
 }
 
 // add_assign (src/mixtral.rs:661-665)
@@ -208,9 +339,12 @@ void gqa_forward(const Cfg& c, const float* q, const float* k, const float* v, i
   int64_t group = c.group();
   probs.assign(batch * c.heads * seq * seq, 0.0f);
   mix.assign(batch * seq * c.q_dim(), 0.0f);
-  vecf row(seq);
-  for (int64_t b = 0; b < batch; ++b)
-    for (int64_t h = 0; h < c.heads; ++h) {
+  // (b, h) rows are independent: split over threads, each row computed as
+  // the crate computes it
+  par_for(batch * c.heads, true, [&](int64_t bh) {
+    const int64_t b = bh / c.heads, h = bh % c.heads;
+    vecf row(seq);
+    {
       int64_t kv = h / group;
       for (int64_t i = 0; i < seq; ++i) {
         std::fill(row.begin(), row.end(), -INFINITY);
@@ -245,6 +379,7 @@ void gqa_forward(const Cfg& c, const float* q, const float* k, const float* v, i
         }
       }
     }
+  });
 }
 
 // gqa_backward (src/mixtral.rs:861-922)
@@ -257,9 +392,12 @@ void gqa_backward(const Cfg& c, const float* q, const float* k, const float* v,
   dq.assign(q_len, 0.0f);
   dk.assign(kv_len, 0.0f);
   dv.assign(kv_len, 0.0f);
-  vecf da(seq);
-  for (int64_t b = 0; b < batch; ++b)
-    for (int64_t h = 0; h < c.heads; ++h) {
+  // dk/dv of KV head kvh receive only the heads of its group: (b, kvh) pairs
+  // are split over threads and each walks its heads in the crate's order
+  par_for(batch * c.kv_heads, true, [&](int64_t bg) {
+    const int64_t b = bg / c.kv_heads;
+    vecf da(seq);
+    for (int64_t h = (bg % c.kv_heads) * group; h < (bg % c.kv_heads + 1) * group; ++h) {
       int64_t kvh = h / group;
       for (int64_t i = 0; i < seq; ++i) {
         std::fill(da.begin(), da.end(), 0.0f);
@@ -291,6 +429,7 @@ void gqa_backward(const Cfg& c, const float* q, const float* k, const float* v,
         }
       }
     }
+  });
 }
 
 // softmax (src/mixtral.rs:924-929)
@@ -441,7 +580,7 @@ vecf backward_layer(const Cfg& c, const float* lp, const orc_tape& lt, const flo
   vecf xn2 = rmsnorm_out(lt.ffn_in.data(), lt.ffn_inv.data(), lp + L.ffn_norm, n, c.dim);
   vecf d_xn2(n * c.dim, 0.0f);
   vecf hid(c.inter), d_out(c.dim), d_gate(c.inter), d_up(c.inter);
-  vecf d_hid, d_down, dx_g, dw_g, dx_u, dw_u, dx_r, dw_r;
+  vecf d_hid, dx_g, dx_u, dx_r;
   for (int64_t t = 0; t < n; ++t) {
     vecf dvalues(c.top_k, 0.0f);
     float weight_dot = 0.0f;
@@ -460,8 +599,8 @@ vecf backward_layer(const Cfg& c, const float* lp, const orc_tape& lt, const flo
       dvalues[k2] = dw;
       float w = lt.top_w[t * c.top_k + k2];
       for (int64_t d = 0; d < c.dim; ++d) d_out[d] = w * d_mixed[t * c.dim + d];
-      linear_bwd(hid.data(), d_out.data(), lp + L.down[e], 1, c.inter, c.dim, d_hid, d_down);
-      add_assign(grad + L.down[e], d_down.data(), c.inter * c.dim);
+      linear_bwd_row_acc(hid.data(), d_out.data(), lp + L.down[e], c.inter, c.dim, d_hid,
+                         grad + L.down[e]);
       for (int64_t i = 0; i < c.inter; ++i) {
         float z = g[i];
         float sg = sigmoid(z);
@@ -470,10 +609,10 @@ vecf backward_layer(const Cfg& c, const float* lp, const orc_tape& lt, const flo
         d_up[i] = d_hid[i] * silu(z);
       }
       const float* xrow = xn2.data() + t * c.dim;
-      linear_bwd(xrow, d_gate.data(), lp + L.gate[e], 1, c.dim, c.inter, dx_g, dw_g);
-      linear_bwd(xrow, d_up.data(), lp + L.up[e], 1, c.dim, c.inter, dx_u, dw_u);
-      add_assign(grad + L.gate[e], dw_g.data(), c.dim * c.inter);
-      add_assign(grad + L.up[e], dw_u.data(), c.dim * c.inter);
+      linear_bwd_row_acc(xrow, d_gate.data(), lp + L.gate[e], c.dim, c.inter, dx_g,
+                         grad + L.gate[e]);
+      linear_bwd_row_acc(xrow, d_up.data(), lp + L.up[e], c.dim, c.inter, dx_u,
+                         grad + L.up[e]);
       for (int64_t d = 0; d < c.dim; ++d) d_xn2[t * c.dim + d] += dx_g[d] + dx_u[d];
     }
     for (int64_t k2 = 0; k2 < c.top_k; ++k2) dvalues[k2] = dvalues[k2] / s - weight_dot / s;
@@ -485,8 +624,8 @@ vecf backward_layer(const Cfg& c, const float* lp, const orc_tape& lt, const flo
     vecf dz(c.experts, 0.0f);
     for (int64_t e = 0; e < c.experts; ++e) dz[e] = p[e] * (dp[e] - dot);
     const float* xrow = xn2.data() + t * c.dim;
-    linear_bwd(xrow, dz.data(), lp + L.router, 1, c.dim, c.experts, dx_r, dw_r);
-    add_assign(grad + L.router, dw_r.data(), c.dim * c.experts);
+    linear_bwd_row_acc(xrow, dz.data(), lp + L.router, c.dim, c.experts, dx_r,
+                       grad + L.router);
     for (int64_t d = 0; d < c.dim; ++d) d_xn2[t * c.dim + d] += dx_r[d];
   }
   vecf d_mid, d_ffn_w;
@@ -551,6 +690,17 @@ extern "C" {
 
 int64_t orc_layer_params(const dop_mixtral_cfg* c) { return layer_layout(Cfg(c)).total; }
 
+// 1: the crate's literal loop order, single-threaded; 0 (default): the
+// interchanged, threaded loop nests (same bytes).
+void orc_set_literal(int on) { g_literal = on ? 1 : 0; }
+
+// Host threads the oracle may use (0 = every hardware thread); returns the
+// number in effect.
+int orc_set_threads(int n) {
+  if (n >= 0) g_threads = n;
+  return oracle_threads();
+}
+
 // offsets out[0..7) = attn_norm,q,k,v,o,ffn_norm,router; then gate[E],up[E],down[E]
 void orc_layer_offsets(const dop_mixtral_cfg* c, int64_t* out) {
   Cfg cfg(c);
@@ -599,6 +749,35 @@ void orc_tape_routing(const orc_tape* lt, int64_t* top_i, float* top_p, float* t
 }
 
 void orc_tape_free(orc_tape* lt) { delete lt; }
+
+// The router stage of forward_layer on a given feed-forward input `mid`
+// [n, D] (src/mixtral.rs:311-327): xn2 = rmsnorm(mid), logits = xn2 Wr
+// (+ bias, the skewed-routing workload), softmax, topk_renorm.  Outputs
+// top_i/top_p/top_w [n, k] and router_probs [n, E] (any may be null).
+void orc_router_stage(const dop_mixtral_cfg* c, const float* lp, const float* mid, int64_t n,
+                      const float* bias, int64_t* top_i, float* top_p, float* top_w,
+                      float* router_probs) {
+  Cfg cfg(c);
+  LL L = layer_layout(cfg);
+  vecf xn2, inv;
+  rmsnorm(mid, lp + L.ffn_norm, n, cfg.dim, cfg.eps, xn2, inv);
+  vecf logits = linear(xn2.data(), lp + L.router, n, cfg.dim, cfg.experts);
+  if (bias)
+    for (int64_t t = 0; t < n; ++t)
+      for (int64_t e = 0; e < cfg.experts; ++e) logits[t * cfg.experts + e] += bias[e];
+  std::vector<int64_t> idx;
+  vecf pk, wk;
+  for (int64_t t = 0; t < n; ++t) {
+    vecf row = softmax(logits.data() + t * cfg.experts, cfg.experts);
+    if (router_probs) std::copy(row.begin(), row.end(), router_probs + t * cfg.experts);
+    topk_renorm(row, cfg.top_k, idx, pk, wk);
+    for (int64_t k2 = 0; k2 < cfg.top_k; ++k2) {
+      if (top_i) top_i[t * cfg.top_k + k2] = idx[k2];
+      if (top_p) top_p[t * cfg.top_k + k2] = pk[k2];
+      if (top_w) top_w[t * cfg.top_k + k2] = wk[k2];
+    }
+  }
+}
 
 // forward_backward (src/mixtral.rs:245-261) with forward (:263-289) and backward (:382-432).
 float orc_mixtral_forward_backward(const dop_mixtral_cfg* c, const float* P,

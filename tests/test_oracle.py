@@ -167,3 +167,35 @@ def test_oracle_block_matches_float64_autograd(kw):
     assert rel(r.y, yb.detach().numpy().reshape(-1)) < 1e-5
     assert rel(dx, xb.grad.numpy().reshape(-1)) < 1e-4
     assert rel(dlp, lpb.grad.numpy()) < 1e-4
+
+
+@pytest.mark.parametrize("threads", [1, 3, 8])
+def test_threaded_loops_give_the_literal_loops_bytes(threads):
+    """The oracle's interchanged, threaded loop nests keep every output's
+    accumulation sequence, so they give the bytes of the crate's literal
+    loop order (src/mixtral.rs:616-659): checked at the small-Mixtral widths,
+    where every contraction takes the threaded path, for y, dx, the whole
+    adjoint, the routing and the router stage."""
+    c = MixtralConfig(vocab=32, dim=512, layers=1, heads=8, kv_heads=2, head_dim=64,
+                      intermediate=1408, experts=8, top_k=2, rms_eps=1e-5, rope_theta=1e6,
+                      sliding_window=24)
+    batch, seq = 2, 20
+    g = torch.Generator().manual_seed(5)
+    n = orc.layer_params(c)
+    lp = (torch.randn(n, generator=g) * 0.02).float().numpy()
+    x = torch.randn(batch * seq * c.dim, generator=g).float().numpy()
+    dy = torch.randn(batch * seq * c.dim, generator=g).float().numpy()
+    outs = []
+    try:
+        for literal in (True, False):
+            orc.set_literal(literal)
+            orc.set_threads(threads)
+            r = orc.block_forward(c, lp, x, batch, seq)
+            dx, dlp = orc.block_backward(c, lp, r, dy)
+            stage = orc.router_stage(c, lp, r.y)
+            outs.append([r.y.copy(), dx, dlp, r.routing()[0], *stage])
+    finally:
+        orc.set_literal(False)
+        orc.set_threads(0)
+    for a, b in zip(*outs):
+        assert a.dtype == b.dtype and np.array_equal(a.view(np.uint8), b.view(np.uint8))
