@@ -415,6 +415,16 @@ int dop_block_routing(const dop_block* blk_, int32_t* top_i, float* top_w, float
   });
 }
 
+int dop_block_ffn_input(const dop_block* blk_, float* mid, void* s) {
+  return guarded([&] {
+    DOP_REQUIRE(blk_ && mid, "null block or buffer");
+    auto* b = reinterpret_cast<const dop::Block*>(blk_);
+    if (!b->have_tape) throw dop::Error(DOP_E_STATE, "no forward has run");
+    DOP_CHECK_CUDA(cudaMemcpyAsync(mid, b->mid, 4 * b->T * b->cfg.dim, cudaMemcpyDeviceToDevice,
+                                   as_stream(s)));
+  });
+}
+
 int dop_block_permutation(const dop_block* blk_, int32_t* slot_row, int32_t* seg_off,
                           int32_t* row_token, void* s) {
   return guarded([&] {

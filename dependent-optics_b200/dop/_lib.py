@@ -18,6 +18,7 @@ DOP_STAGE_GEMM = 0
 DOP_STAGE_ATTENTION = 1
 DOP_STAGE_ADD = 2
 DOP_IPC_HANDLE_BYTES = 64
+DOP_SELFTEST_MBARRIER_CODE = 90
 
 ERRORS = {
     -1: "DOP_E_INVALID", -2: "DOP_E_CUDA", -3: "DOP_E_NOMEM", -4: "DOP_E_UNSUPPORTED",
@@ -82,6 +83,7 @@ SIGNATURES = [
     ("dop_block_workspace_bytes", _I64, [_P]),
     ("dop_block_routing", C.c_int, [_P, _P, _P, _P, _P, _P]),
     ("dop_block_permutation", C.c_int, [_P, _P, _P, _P, _P]),
+    ("dop_block_ffn_input", C.c_int, [_P, _P, _P]),
     ("dop_block_permuted_rows", _I64, [_P]),
     ("dop_block_launches", _I64, [_P]),
     ("dop_block_create_ep", C.c_int, [C.POINTER(MixtralCfg), _I64, _I64, C.c_int, C.c_int,
@@ -112,6 +114,9 @@ SIGNATURES = [
     ("dop_gemm_bf16", C.c_int, [_I64, _I64, _I64, _P, _I64, C.c_int, _P, _I64, C.c_int, _P,
                                 _I64, C.c_int, C.c_int, _P]),
     ("dop_device_status", C.c_int, []),
+    ("dop_clear_device_status", C.c_int, []),
+    ("dop_set_wait_limits", C.c_int, [_I64, _I64]),
+    ("dop_selftest_wait_expiry", C.c_int, [C.c_int, _P]),
     ("dop_gqa_forward", C.c_int, [_I64, _I64, _I64, _I64, _I64, _I64, C.c_int, _P, _P, _P, _P,
                                   _P, _P]),
     ("dop_gqa_backward", C.c_int, [_I64, _I64, _I64, _I64, _I64, _I64, C.c_int, _P, _P, _P, _P,

@@ -255,6 +255,14 @@ class Block:
         torch.cuda.synchronize()
         return sr, so, rt
 
+    def ffn_input(self):
+        """mid = x + attention [T, D] (fp32) of the last forward: the router's input."""
+        import torch
+        mid = torch.empty(self.batch * self.seq, self.cfg.dim, dtype=torch.float32, device="cuda")
+        check(lib().dop_block_ffn_input(self._h, ptr(mid), None))
+        torch.cuda.synchronize()
+        return mid
+
     def set_adjoint_stream(self, stream) -> None:
         """Make `stream` (a torch.cuda.Stream or None) wait, in every backward,
         until the experts' parameter adjoints are final."""

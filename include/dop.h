@@ -128,6 +128,10 @@ int dop_block_routing(const dop_block* blk, int32_t* top_i, float* top_w,
 int dop_block_permutation(const dop_block* blk, int32_t* slot_row,
                           int32_t* seg_off, int32_t* row_token, void* stream);
 int64_t dop_block_permuted_rows(const dop_block* blk);
+/* The feed-forward input of the last forward, mid = x + attention [T, D]
+ * fp32, copied to a device buffer: the router's input (src/mixtral.rs:308-312),
+ * for checking the router stage on the lens's own input. */
+int dop_block_ffn_input(const dop_block* blk, float* mid, void* stream);
 /* Number of kernels the library launched on this handle since creation. */
 int64_t dop_block_launches(const dop_block* blk);
 /* Overlap of the adjoint reduction with the rest of the backward: after
@@ -280,19 +284,45 @@ int dop_gqa_backward(int64_t batch, int64_t seq, int64_t heads, int64_t kv_heads
  * reference crate.  Its scratch is a 4 MiB array inside libdop's own device
  * memory, held on every GPU that loads the library until exit, so it accepts
  * batch * heads * seq <= 1,048,576 and rejects larger shapes with
- * DOP_E_INVALID.  The first call on a device (with that device current)
- * looks the array up with cudaGetSymbolAddress; make that first call before
- * any stream capture.  All calls share the array: calls that overlap on the
- * GPU race. */
+ * DOP_E_INVALID.  A call made while its stream is not capturing looks the
+ * array up with cudaGetSymbolAddress (with the call's device current) and
+ * keeps the address per device; a call made during a capture reuses it.
+ * Make the first call on a device before any stream capture, and again after
+ * a cudaDeviceReset (the kept address belongs to the old context).  All
+ * calls share the array: calls that overlap on the GPU race. */
 int dop_gqa_backward_f32_noalloc(int64_t batch, int64_t seq, int64_t heads,
                                  int64_t kv_heads, int64_t head_dim, int64_t window,
                                  const float* q, const float* k, const float* v,
                                  const float* o, const float* dout, const float* lse,
                                  float* dq, float* dk, float* dv, void* stream);
 
-/* First bounded-wait failure a tensor-core kernel recorded since load
- * (0 = none); a non-zero code means a kernel gave up waiting and returned. */
+/* ------------------------------------------------- failure detection
+ * Every wait a libdop kernel makes on another agent is bounded: mbarrier
+ * waits of the tensor-core kernels (TMA copies, MMAs, the other CTA of a
+ * pair) and the expert exchange's flag barriers (other ranks).  A wait that
+ * runs out records a code in the current device's error word, drains what
+ * its CTA has in flight (bounded), frees its TMEM and returns; every later
+ * libdop kernel on that device skips its work until the word is cleared.
+ * The crate's counterpart is its control plane's timeout (DistError,
+ * src/dist.rs:36-56).
+ *
+ * dop_device_status: the first code recorded on the current device (0 =
+ * none): 1..59 a tensor-core kernel's mbarrier wait, 60 + k the exchange's
+ * barrier k, DOP_SELFTEST_MBARRIER_CODE the self-test below. */
 int dop_device_status(void);
+/* Clear the current device's error word (after synchronising the device). */
+int dop_clear_device_status(void);
+/* Wait limits of the current device in ns of device time, 0 = the built-in
+ * default (4 s per tensor-core wait, 20 s per exchange barrier). */
+int dop_set_wait_limits(int64_t tensor_core_ns, int64_t exchange_ns);
+/* Make one bounded wait run out on purpose, on the current device:
+ * which = 0 launches one CTA that holds TMEM while it waits on an mbarrier
+ * nothing arrives at (records DOP_SELFTEST_MBARRIER_CODE); which = 1 runs the
+ * exchange's barrier 0 over a two-rank view of this device's own memory in
+ * which rank 1's flag is never written (records 60) and waits for it.  Each
+ * returns after its wait limit; nothing faults or hangs. */
+#define DOP_SELFTEST_MBARRIER_CODE 90
+int dop_selftest_wait_expiry(int which, void* stream);
 
 /* ----------------------------------------------------------- utilities */
 /* fp32 -> bf16 (round to nearest even), device arrays. */

@@ -20,6 +20,8 @@ pytestmark = pytest.mark.gpu
 
 F32_TOL = 1e-4
 BF16_TOL = 2e-2
+ROUTER_GAP = 1e-6  # top-k decision gap below which a routing difference is excused
+PROB_TOL = 1e-6    # router probabilities and renormalised gates, absolute
 
 
 def rel(a, b):
@@ -117,6 +119,22 @@ def check_routing(cfg, gpu, ref, max_gap, max_frac):
     return None if len(diff) == 0 else gpu["top_i"].astype(np.int64)
 
 
+def check_router_stage(cfg, blk, lp, bias=None):
+    """The device's routing equals the oracle's router stage run on the
+    device's own feed-forward input, except at decision gaps below 1e-6."""
+    mid = blk.ffn_input().cpu().numpy()
+    ti_ref, tw_ref, _, pr_ref = orc.router_stage(cfg, lp, mid, bias)
+    ti, tw, _, pr = (t.cpu().numpy() for t in blk.routing())
+    assert np.abs(pr - pr_ref).max() < PROB_TOL, "router probabilities"
+    diff = np.nonzero((ti != ti_ref).any(axis=1))[0]
+    for t in diff:
+        gap = decision_gap(pr_ref[t], cfg.top_k)
+        assert gap < ROUTER_GAP, f"token {t}: router stage differs at decision gap {gap}"
+    same = np.setdiff1d(np.arange(ti.shape[0]), diff)
+    assert np.abs(tw[same] - tw_ref[same]).max() < PROB_TOL, "renormalised gates"
+    return len(diff)
+
+
 def compare(cfg, gpu, ref, tol):
     ry, rdx = rel(gpu["y"], ref["y"]), rel(gpu["dx"], ref["dx"])
     rp, worst = max_param_rel(cfg, gpu["dP"], ref["dP"])
@@ -196,6 +214,7 @@ def test_bf16_block_matches_oracle_on_rounded_inputs(cuda, kind):
     lp, x, dy = make_inputs(cfg, batch, seq, seed=3)
     lp, x, dy = bf16_round(lp), bf16_round(x), bf16_round(dy)
     gpu = run_gpu(cfg, batch, seq, lp, x, dy, DOP_BF16)
+    check_router_stage(cfg, gpu["blk"], lp)  # the 1e-6 bar on the lens's own input
     ref = run_oracle(cfg, batch, seq, lp, x, dy)
     forced = check_routing(cfg, gpu, ref, 1e-2, 0.03)
     if forced is not None:
