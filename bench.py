@@ -26,6 +26,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -44,45 +45,50 @@ WORKLOADS = {
     "mixtral8x7b_block": dict(cfg=dict(vocab=32000, dim=4096, layers=1, heads=32, kv_heads=8,
                                        head_dim=128, intermediate=14336, experts=8, top_k=2,
                                        rms_eps=1e-5, rope_theta=1e6, sliding_window=4096),
-                              batch=8, seq=4096, precision="bf16", skew=False),
+                              batch=8, seq=4096, precision="bf16", skew=False, cpu_seq=16),
     # same, with a Zipf(s=1.2) per-expert logit bias scaled to 2.0
     "mixtral8x7b_block_skewed": dict(cfg=dict(vocab=32000, dim=4096, layers=1, heads=32,
                                               kv_heads=8, head_dim=128, intermediate=14336,
                                               experts=8, top_k=2, rms_eps=1e-5, rope_theta=1e6,
                                               sliding_window=4096),
-                                     batch=8, seq=4096, precision="bf16", skew=True),
+                                     batch=8, seq=4096, precision="bf16", skew=True,
+                                     cpu_seq=16),
     # dense block (one expert, top-1, full causal attention)
     "dense_block": dict(cfg=dict(vocab=32000, dim=2048, layers=1, heads=16, kv_heads=16,
                                  head_dim=128, intermediate=5632, experts=1, top_k=1,
                                  rms_eps=1e-5, rope_theta=1e4, sliding_window=2048),
-                        batch=8, seq=2048, precision="bf16", skew=False),
+                        batch=8, seq=2048, precision="bf16", skew=False, cpu_seq=128),
     # Mixtral-8x7B widths at batch 1, seq 1024: the small case for profiler captures
     "mixtral8x7b_block_profile": dict(cfg=dict(vocab=32000, dim=4096, layers=1, heads=32,
                                                kv_heads=8, head_dim=128, intermediate=14336,
                                                experts=8, top_k=2, rms_eps=1e-5, rope_theta=1e6,
                                                sliding_window=4096),
-                                      batch=1, seq=1024, precision="bf16", skew=False),
+                                      batch=1, seq=1024, precision="bf16", skew=False,
+                                      cpu_seq=16),
     # staged 4-block stack of Mixtral-8x7B-shaped blocks: global batch 32 at seq
     # 4096 in 8 micro-batches, pipeline-staged over the GPUs (dop.cluster)
     "mixtral8x7b_stack4": dict(cfg=dict(vocab=32000, dim=4096, layers=4, heads=32, kv_heads=8,
                                         head_dim=128, intermediate=14336, experts=8, top_k=2,
                                         rms_eps=1e-5, rope_theta=1e6, sliding_window=4096),
                                batch=32, seq=4096, micro_batches=8, precision="bf16",
-                               skew=False, stack=True),
+                               skew=False, stack=True, cpu_seq=16),
     # small Mixtral block, fp32
     "small_mixtral_block_f32": dict(cfg=dict(vocab=32000, dim=512, layers=1, heads=8, kv_heads=2,
                                              head_dim=64, intermediate=1408, experts=8, top_k=2,
                                              rms_eps=1e-5, rope_theta=1e6, sliding_window=128),
-                                    batch=4, seq=512, precision="f32", skew=False),
+                                    batch=4, seq=512, precision="f32", skew=False, cpu_seq=512),
     # the crate's CPU-run case: kernel.rs MLP program, batch 64, 128 -> 256 -> 128,
     # ReLU hidden, MSE against targets
     "mlp_f32": dict(program="mlp", batch=64, dims=[128, 256, 128], precision="f32", skew=False),
 }
 DEFAULT_WORKLOAD = "mixtral8x7b_block"
-CPU_SAMPLE_SEQ = 2  # tokens of the CPU-oracle sample (batch 1, full widths)
-# DRAM bytes (read 9.78e9 + write 6.09e9) of one full-size expert gate/up
-# launch, measured once with ncu (a bench run cannot read DRAM counters)
-GATE_UP_TRAFFIC = 9.78e9 + 6.09e9
+# The CPU sample of a block workload is one sequence of `cpu_seq` tokens at
+# the workload's full widths (batch 1), sized so one oracle fwd+bwd takes
+# seconds on a many-core host; it includes the attention over its positions.
+# DRAM bytes (read + write) of one expert gate/up launch per routed row,
+# from a one-pass ncu capture of the small case (batch 1, seq 1024, 2048
+# routed rows) scaled by rows; a bench run cannot read DRAM counters.
+GATE_UP_TRAFFIC_PER_ROW = (9.78e9 + 6.09e9) / 65536
 
 
 def flops_per_step(cfg, batch, seq):
@@ -171,21 +177,28 @@ def make_params(cfg_d, precision, seed, device):
     return cfg, ll, P
 
 
-def cpu_oracle_sample(cfg_d, seq, seed, repeats=1):
-    """Seconds for one fwd+bwd of the CPU oracle on (batch 1, seq) at full widths."""
+class _Cfg:
+    """A MixtralConfig-shaped record for the oracle (no library load)."""
+    def __init__(self, d):
+        self.__dict__.update(d)
+
+
+def cpu_oracle_sample(cfg_d, seq, seed, repeats=1, threads=0):
+    """(seconds of each fwd+bwd, threads used) of the CPU oracle on
+    (batch 1, seq) at full widths, on `threads` host threads (0 = all)."""
     import numpy as np
     import torch
     import oracle_ffi as orc
-    from dop.mixtral import MixtralConfig, layer_layout
-    cfg = MixtralConfig(**cfg_d)
-    ll = layer_layout(cfg)
+    cfg = _Cfg(cfg_d)
+    ll = orc.layer_offsets(cfg)
+    used = orc.set_threads(threads)
     g = torch.Generator().manual_seed(seed)
     # 16 Mi seeded N(0, 0.02^2) values tiled over the layer: drawing 1.45e9
     # normals on the host would take longer than the sample itself
     base = (torch.randn(1 << 24, generator=g) * 0.02).numpy()
-    lp = np.resize(base, ll.total)
-    lp[ll.attn_norm: ll.attn_norm + cfg.dim] = 1.0
-    lp[ll.ffn_norm: ll.ffn_norm + cfg.dim] = 1.0
+    lp = np.resize(base, ll["total"])
+    lp[ll["attn_norm"]: ll["attn_norm"] + cfg.dim] = 1.0
+    lp[ll["ffn_norm"]: ll["ffn_norm"] + cfg.dim] = 1.0
     x = torch.randn(seq * cfg.dim, generator=g).numpy()
     dy = torch.randn(seq * cfg.dim, generator=g).numpy()
     times = []
@@ -195,55 +208,79 @@ def cpu_oracle_sample(cfg_d, seq, seed, repeats=1):
         orc.block_backward(cfg, lp, r, dy)
         times.append(time.perf_counter() - t0)
         del r
-    return times
+    return times, used
 
 
-def _worker(args):
-    cfg_d, seq, seed, repeats = args
-    return cpu_oracle_sample(cfg_d, seq, seed, repeats)
+def use_expert_parallel(a, wl, world) -> bool:
+    """Expert parallel when the experts split over the ranks (the contract's
+    partitioning of the Mixtral block), else data parallel.  With skewed
+    routing an expert-parallel step waits for the owner of the hottest
+    expert (measured at 8 GPUs: 43% scaling efficiency against 85% for data
+    parallelism), so `auto` runs skewed workloads data-parallel."""
+    from dop import parallel
+    return (world > 1 and a.parallel != "dp"
+            and parallel.ep_mode(world, wl["cfg"]["experts"], wl["precision"] == "bf16")
+            and (a.parallel == "ep" or not wl["skew"]))
+
+
+def arm_config(a, wl, world) -> dict:
+    """The `config` both arms print for a workload at `world` GPUs."""
+    if wl.get("program"):
+        return {"workload": a.workload, "batch_per_gpu": wl["batch"], "dims": wl["dims"],
+                "loss": "mse", "parallelism": "single" if world == 1 else
+                f"{world} independent replicas",
+                "graph": "one CUDA graph per step (forward, MSE head, backward)",
+                "l2": "inputs smaller than L2 (the workload is 2 x 32 KiB)"}
+    if wl.get("stack"):
+        pp = math.gcd(wl["cfg"]["layers"], world)
+        return {"workload": a.workload, "global_batch": wl["batch"], "seq": wl["seq"],
+                "micro_batches": wl["micro_batches"], **wl["cfg"],
+                "parallelism": f"pp{pp}" + (f"xdp{world // pp}" if world // pp > 1 else ""),
+                "schedule": "one-forward-one-backward per stage (dop.cluster plan)",
+                "l2": "inputs larger than L2 (each micro-batch is 4 B x 16384 x 4096)"}
+    E = wl["cfg"]["experts"]
+    return {"workload": a.workload, "batch_per_gpu": wl["batch"], "seq": wl["seq"],
+            "global_batch": wl["batch"] * world, **wl["cfg"],
+            "parallelism": ("single" if world == 1 else
+                            f"ep{world} ({E // world} experts per rank, exchange over NVLink "
+                            "peer reads, shared adjoint all-reduced)"
+                            if use_expert_parallel(a, wl, world) else
+                            f"dp{world}, expert adjoints reduced during the attention backward"),
+            "l2": "inputs larger than L2 (x, dy are 4 B x T x D each)"}
 
 
 def run_reference(a):
-    """CPU lens (oracle port of the crate's single-threaded CPU lens) on all
-    host cores: one independent (batch 1, seq CPU_SAMPLE_SEQ) sample per
-    worker process; tokens/s = workers * tokens / slowest worker's time."""
-    import multiprocessing as mp
+    """The CPU lens (the oracle, a port of the crate's CPU lens) on every
+    host thread: each step is one fwd+bwd of a (batch 1, cpu_seq) sample at
+    the workload's full widths; tokens/s = sample tokens / its time.  Only
+    rank 0 works (the other ranks of a torchrun launch exit at once)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     wl = WORKLOADS[a.workload]
+    world = int(os.environ.get("WORLD_SIZE", str(a.gpus)))
     cores = os.cpu_count() or 1
     if wl.get("program"):
-        run_reference_program(a, wl, cores)
+        run_reference_program(a, wl, cores, world)
         return
-    try:
-        avail = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
-    except (ValueError, OSError):
-        avail = 64 << 30
-    from dop.mixtral import MixtralConfig, layer_layout
-    per_worker = layer_layout(MixtralConfig(**wl["cfg"])).total * 4 * 2.6 + (1 << 30)
-    workers = max(1, min(cores, int(avail * 0.7 // per_worker)))
-    ctx = mp.get_context("spawn")
     steps = max(1, a.steps)
-    with ctx.Pool(workers) as pool:
-        res = pool.map(_worker, [(wl["cfg"], CPU_SAMPLE_SEQ, w, a.warmup + steps)
-                                 for w in range(workers)])
+    seq = wl["cpu_seq"]
+    times, used = cpu_oracle_sample(wl["cfg"], seq, seed=0, repeats=a.warmup + steps)
     layers = wl["cfg"]["layers"]
     # a stack of identical blocks costs `layers` block passes per token: one
     # block is timed and the time scaled by the layer count
-    per_step = [layers * max(r[a.warmup + i] for r in res) for i in range(steps)]
+    per_step = [layers * t for t in times[a.warmup:]]
     t = sum(per_step) / steps
-    tokens = workers * CPU_SAMPLE_SEQ
-    v = tokens / t
-    sample = (f"{workers} workers x (batch 1, seq {CPU_SAMPLE_SEQ}) at full widths of "
-              f"{a.workload}; each step = every worker's fwd+bwd"
-              + (f" of one block, time x {layers} blocks" if layers > 1 else ""))
+    v = seq / t
+    sample = (f"batch 1, seq {seq} at the full widths of {a.workload}, one fwd+bwd per step "
+              f"on {used} host threads"
+              + (f", one block timed x {layers} blocks" if layers > 1 else ""))
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": a.gpus,
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
         "steps": steps, "warmup": a.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": a.workload, "batch": 1, "seq": CPU_SAMPLE_SEQ, **wl["cfg"]},
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": workers, "kind": "port",
+        "config": arm_config(a, wl, world),
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": used, "kind": "port",
                          "sample": sample},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -392,11 +429,7 @@ def run_program(a):
                              "value": world * rows / (steady_ms / 1e3)},
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (x, targets ~ N(0,1); W ~ N(0, 1/fan_in); b = 0; seed 0)",
-            "config": {"workload": a.workload, "batch_per_gpu": rows, "dims": wl["dims"],
-                       "loss": "mse", "parallelism": "single" if world == 1 else
-                       f"{world} independent replicas",
-                       "graph": "one CUDA graph per step (forward, MSE head, backward)",
-                       "l2": "inputs smaller than L2 (the workload is 2 x 32 KiB)"},
+            "config": arm_config(a, wl, world),
             "tflops": tflops,
             "roofline": {"bound": "latency", "kernel": "whole step", "achieved": tflops,
                          "peak": None, "unit": "TFLOP/s", "frac": None, "traffic": None,
@@ -412,7 +445,7 @@ def run_program(a):
         dist.destroy_process_group()
 
 
-def run_reference_program(a, wl, cores):
+def run_reference_program(a, wl, cores, world):
     """The oracle's program forward+backward on every host core: one
     independent replica per worker process, each step a 1 s sample."""
     import multiprocessing as mp
@@ -426,11 +459,10 @@ def run_reference_program(a, wl, cores):
             per_step.append(sum(n for n, _ in res) * wl["batch"] / max(t for _, t in res))
     v = sum(per_step) / steps
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": a.gpus,
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
         "steps": steps, "warmup": a.warmup, "ms_per_step": wl["batch"] / v * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": a.workload, "batch": wl["batch"],
-                                        "dims": wl["dims"], "loss": "mse"},
+        "data": "synthetic", "config": arm_config(a, wl, world),
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"{cores} workers, each 1 s of forward+backward passes"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -463,6 +495,7 @@ def run_stack(a):
     one = dict(wl["cfg"], layers=1)
     cap = int(torch.cuda.get_device_properties(dev).total_memory * 0.92)
     plan = cluster.stage_mixtral(cfg, gb, seq, M, DOP_BF16, cluster.b200s(world, cap))
+    assert len(plan.stage_groups()) == math.gcd(cfg.layers, world)
     groups = {}
     for g in plan.stage_groups():  # every rank creates every group, in the same order
         grp = dist.new_group(g) if world > 1 and len(g) > 1 else None
@@ -551,26 +584,22 @@ def run_stack(a):
     clk_summary = clk.summary()
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        ts = cpu_oracle_sample(one, CPU_SAMPLE_SEQ, seed=0, repeats=1)
-        cpu = {"value": CPU_SAMPLE_SEQ / (cfg.layers * ts[0]), "unit": "tokens/s", "cores": 1,
+        cs = wl["cpu_seq"]
+        ts, used = cpu_oracle_sample(one, cs, seed=0, repeats=1)
+        cpu = {"value": cs / (cfg.layers * ts[0]), "unit": "tokens/s", "cores": used,
                "kind": "port",
-               "sample": f"batch 1, seq {CPU_SAMPLE_SEQ} through one block at the full widths, "
-                         f"single thread, time x {cfg.layers} blocks"}
+               "sample": f"batch 1, seq {cs} through one block at the full widths, "
+                         f"{used} host threads, time x {cfg.layers} blocks"}
     if rank == 0:
         hbm, peak, peak_sus, src = measured_peaks()
         flops = cfg.layers * flops_per_step(one, gb, seq)
         tflops = flops / (ms / 1e3) / 1e12
-        pp = len(plan.stage_groups())
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) x and dy)",
-            "config": {"workload": a.workload, "global_batch": gb, "seq": seq,
-                       "micro_batches": M, **wl["cfg"],
-                       "parallelism": f"pp{pp}" + (f"xdp{world // pp}" if world // pp > 1 else ""),
-                       "schedule": "one-forward-one-backward per stage (dop.cluster plan)",
-                       "l2": "inputs larger than L2 (each micro-batch is 4 B x 16384 x 4096)"},
+            "config": arm_config(a, wl, world),
             "tflops": tflops, "frac_of_bf16_peak": tflops / (world * peak),
             "frac_of_bf16_sustained": tflops / (world * peak_sus),
             "roofline": {"bound": "tensor", "kernel": "whole stack step", "achieved": tflops / world,
@@ -605,14 +634,7 @@ def run_ours(a):
     T = batch * seq
     cfg, ll, P = make_params(wl["cfg"], wl["precision"], seed=0, device=dev)  # same weights on every rank
     prec = DOP_BF16 if wl["precision"] == "bf16" else DOP_F32
-    # expert parallel when the experts split over the ranks (the contract's
-    # partitioning of the Mixtral block), else data parallel.  With skewed
-    # routing an expert-parallel step waits for the owner of the hottest
-    # expert (measured at 8 GPUs: 43% scaling efficiency against 85% for data
-    # parallelism), so `auto` runs skewed workloads data-parallel.
-    ep = (world > 1 and a.parallel != "dp"
-          and parallel.ep_mode(world, cfg.experts, prec == DOP_BF16)
-          and (a.parallel == "ep" or not wl["skew"]))
+    ep = use_expert_parallel(a, wl, world)
     if a.parallel == "ep" and world > 1 and not ep:
         raise SystemExit(f"--parallel ep needs bf16 and experts % {world} == 0")
     blk = Block(cfg, batch, seq, prec, ep=(rank, world) if ep else None)
@@ -757,10 +779,11 @@ def run_ours(a):
     _trace("e2e done")
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        ts = cpu_oracle_sample(wl["cfg"], CPU_SAMPLE_SEQ, seed=0, repeats=1)
-        cpu = {"value": CPU_SAMPLE_SEQ / ts[0], "unit": "tokens/s", "cores": 1, "kind": "port",
-               "sample": f"batch 1, seq {CPU_SAMPLE_SEQ} at the full widths of {a.workload}, "
-                         f"one fwd+bwd, single thread"}
+        cs = wl["cpu_seq"]
+        ts, used = cpu_oracle_sample(wl["cfg"], cs, seed=0, repeats=1)
+        cpu = {"value": cs / ts[0], "unit": "tokens/s", "cores": used, "kind": "port",
+               "sample": f"batch 1, seq {cs} at the full widths of {a.workload}, "
+                         f"one fwd+bwd on {used} host threads"}
 
     if rank == 0:
         out = {
@@ -768,26 +791,20 @@ def run_ours(a):
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": wl["precision"],
             "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) x and dy)",
-            "config": {"workload": a.workload, "batch_per_gpu": batch, "seq": seq,
-                       "global_batch": batch * world, **wl["cfg"],
-                       "parallelism": ("single" if world == 1 else
-                                       f"ep{world} ({cfg.experts // world} experts per rank, "
-                                       "exchange over NVLink peer reads, shared adjoint "
-                                       "all-reduced)" if ep else
-                                       f"dp{world}, expert adjoints reduced during the "
-                                       "attention backward"),
-                       "l2": "inputs larger than L2 (x, dy are 4 B x T x D each)"},
+            "config": arm_config(a, wl, world),
             "tflops": flops / (ms / 1e3) / 1e12,
             "frac_of_bf16_peak": flops / (ms / 1e3) / 1e12 / peak,
             "frac_of_bf16_sustained": flops / (ms / 1e3) / 1e12 / peak_sus,
             # the gate/up GEMM is timed inside a long step: sustained peak
             "roofline": {"bound": "tensor", "kernel": "expert_gate_up", "achieved": achieved,
                          "peak": peak_sus, "unit": "TFLOP/s", "frac": achieved / peak_sus,
-                         "traffic": GATE_UP_TRAFFIC if a.workload == "mixtral8x7b_block" else None,
-                         "traffic_source": ("dram bytes read + written by one full-size launch, "
-                                            "one-pass ncu capture "
-                                            "(profiles/gemm_dram_traffic_mixtral8x7b_block.md); "
-                                            "algorithmic 8.16e9 B"),
+                         "traffic": (GATE_UP_TRAFFIC_PER_ROW * T * cfg.top_k
+                                     if wl["cfg"]["dim"] == 4096 and wl["cfg"]["experts"] == 8
+                                     else None),
+                         "traffic_source": ("dram bytes read + written per launch: one-pass ncu "
+                                            "capture of the batch 1, seq 1024 case scaled by "
+                                            "routed rows; algorithmic 8.16e9 B at batch 8, "
+                                            "seq 4096"),
                          "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside "
                                         "a long step)"},
             "phases_ms": phases,
