@@ -39,7 +39,12 @@ namespace ep {
 using tc::g_err;
 using tc::gtime_ns;
 
-constexpr uint64_t kBarrierNs = 20000000000ull;  // 20 s per barrier
+constexpr uint64_t kBarrierNs = 20000000000ull;  // default: 20 s per barrier
+
+__device__ __forceinline__ uint64_t barrier_limit_ns() {
+  const uint64_t v = *(volatile const uint64_t*)(g_err + 4);
+  return v ? v : kBarrierNs;
+}
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -65,12 +70,12 @@ __global__ void k_ep_barrier(EpView v, int k, unsigned epoch) {
     st_release_sys(peer(v, s, v.flags) + k * kEpMaxWorld + v.rank, epoch);
     const unsigned* mine = v.flags + k * kEpMaxWorld + s;
     const uint64_t t0 = gtime_ns();
-    // bounded: gives up when another wait already failed or after kBarrierNs
+    // bounded: gives up when another wait already failed or after the limit
     for (uint32_t i = 0;; ++i) {
       if ((int)(ld_acquire_sys(mine) - epoch) >= 0) break;
       if ((i & 255u) == 255u) {
         if (*(volatile int*)g_err) break;
-        if (gtime_ns() - t0 > kBarrierNs) {
+        if (gtime_ns() - t0 > barrier_limit_ns()) {
           atomicCAS(g_err, 0, 60 + k);
           break;
         }

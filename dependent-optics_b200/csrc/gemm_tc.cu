@@ -772,8 +772,8 @@ int* tc_error_word() {
   DOP_REQUIRE(dev >= 0 && dev < 16, "device index out of range");
   std::lock_guard<std::mutex> lock(mu);
   if (!words[dev]) {
-    DOP_CHECK_CUDA(cudaMalloc(&words[dev], sizeof(int)));
-    DOP_CHECK_CUDA(cudaMemset(words[dev], 0, sizeof(int)));
+    DOP_CHECK_CUDA(cudaMalloc(&words[dev], kErrWords * sizeof(int)));
+    DOP_CHECK_CUDA(cudaMemset(words[dev], 0, kErrWords * sizeof(int)));
   }
   return words[dev];
 }

@@ -5,7 +5,8 @@
 // Every tensor-core kernel shares one process-wide error word per device
 // (tc_error_word(), bound to each translation unit's g_err before its first
 // launch): the first bounded wait that runs out records its code there, and
-// every CTA that sees it set skips its work.
+// every CTA that sees it set skips its work.  The words after it hold the
+// wait limits (dop_set_wait_limits; 0 selects the built-in default).
 #pragma once
 
 #include <cuda.h>
@@ -13,7 +14,10 @@
 #include "common.cuh"
 
 namespace dop {
-// Process-wide error word of the current device (allocated and zeroed once).
+// Process-wide error word of the current device (allocated and zeroed once):
+// kErrWords ints, [0] the error code, [2..3] the tensor-core wait limit and
+// [4..5] the expert-exchange barrier limit, in ns (u64; 0 = default).
+constexpr int kErrWords = 8;
 int* tc_error_word();
 namespace tc {
 
@@ -21,8 +25,14 @@ namespace {
 __device__ int* g_err;  // -> the process-wide error word of this device
 }
 
-constexpr uint64_t kWaitNs = 4000000000ull;   // 4 s of device time per wait
+constexpr uint64_t kWaitNs = 4000000000ull;   // default: 4 s of device time per wait
 constexpr uint64_t kDrainNs = 200000000ull;   // 0.2 s per wait while draining
+
+// Limit of one bounded mbarrier wait (ns of %globaltimer).
+__device__ __forceinline__ uint64_t wait_limit_ns() {
+  const uint64_t v = *(volatile const uint64_t*)(g_err + 2);
+  return v ? v : kWaitNs;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -68,7 +78,7 @@ static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity
         *abort_flag = 1;
         return false;
       }
-      if (gtime_ns() - t0 > kWaitNs) break;
+      if (gtime_ns() - t0 > wait_limit_ns()) break;
     }
   }
   atomicCAS(g_err, 0, code);
@@ -400,7 +410,7 @@ static __device__ __noinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t par
         *abort_flag = 1;
         return false;
       }
-      if (gtime_ns() - t0 > kWaitNs) break;
+      if (gtime_ns() - t0 > wait_limit_ns()) break;
     }
   }
   atomicCAS(g_err, 0, code);
