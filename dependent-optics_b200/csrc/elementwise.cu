@@ -45,168 +45,6 @@ __global__ void k_rmsnorm_fwd(const float* __restrict__ x, const T* __restrict__
   }
 }
 
-// Router tail for one token, run by one thread: logits z = sum of the
-// per-warp partials (+ bias), softmax (src/mixtral.rs:924-929), top-k by
-// (probability desc, index asc) and renormalisation (:931-939).
-__device__ void router_select(const float* lg, int nw, const float* bias, int E, int K,
-                              int64_t row, float* probs, int* top_i, float* top_p, float* top_w) {
-  float z[kMaxExperts], p[kMaxExperts];
-  float m = -INFINITY;
-  for (int e = 0; e < E; ++e) {
-    float v = 0.f;
-    for (int q = 0; q < nw; ++q) v += lg[q * kMaxExperts + e];
-    if (bias) v += bias[e];
-    z[e] = v;
-    m = fmaxf(m, v);
-  }
-  float s = 0.f;
-  for (int e = 0; e < E; ++e) p[e] = expf(z[e] - m);
-  for (int e = 0; e < E; ++e) s += p[e];
-  for (int e = 0; e < E; ++e) {
-    p[e] = p[e] / s;
-    probs[row * E + e] = p[e];
-  }
-  uint64_t taken = 0;
-  int idx[kMaxTopK];
-  float pk[kMaxTopK];
-  for (int k = 0; k < K; ++k) {
-    int best = -1;
-    for (int e = 0; e < E; ++e) {
-      if (taken >> e & 1) continue;
-      if (best < 0 || p[e] > p[best]) best = e;
-    }
-    taken |= 1ull << best;
-    idx[k] = best;
-    pk[k] = p[best];
-  }
-  float sk = 0.f;
-  for (int k = 0; k < K; ++k) sk += pk[k];
-  for (int k = 0; k < K; ++k) {
-    top_i[row * K + k] = idx[k];
-    top_p[row * K + k] = pk[k];
-    top_w[row * K + k] = pk[k] / sk;
-  }
-}
-
-// router_select run by one warp (all 32 lanes call it): lane e < E holds
-// expert e's logit, the selection is K rounds of a warp argmax (probability
-// desc, index asc).  The per-expert partial sums, the softmax denominator
-// (expert order) and the top-k weight sum (selection order) are summed in
-// router_select's order, so the results are bit-identical, without its
-// per-thread arrays in local memory.
-__device__ void router_select_warp(const float* lg, int nw, const float* bias, int E, int K,
-                                   int64_t row, float* probs, int* top_i, float* top_p,
-                                   float* top_w) {
-  const int lane = threadIdx.x & 31;
-  const bool on = lane < E;
-  float z = -INFINITY;
-  if (on) {
-    float v = 0.f;
-    for (int q = 0; q < nw; ++q) v += lg[q * kMaxExperts + lane];
-    if (bias) v += bias[lane];
-    z = v;
-  }
-  const float m = warp_max(z);
-  const float pe = on ? expf(z - m) : 0.f;
-  float s = 0.f;
-  for (int e = 0; e < E; ++e) s += __shfl_sync(0xffffffffu, pe, e);
-  const float p = pe / s;
-  if (on) probs[row * E + lane] = p;
-  float cand = on ? p : -1.f;
-  float pk[kMaxTopK];
-  int ik[kMaxTopK];
-#pragma unroll
-  for (int k = 0; k < kMaxTopK; ++k) {
-    pk[k] = 0.f;
-    ik[k] = 0;
-    if (k < K) {
-      float bv = cand;
-      int bi = lane;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      pk[k] = bv;
-      ik[k] = bi;
-      if (lane == bi) cand = -1.f;
-    }
-  }
-  if (lane == 0) {
-    float sk = 0.f;
-#pragma unroll
-    for (int k = 0; k < kMaxTopK; ++k)
-      if (k < K) sk += pk[k];
-#pragma unroll
-    for (int k = 0; k < kMaxTopK; ++k) {
-      if (k < K) {
-        top_i[row * K + k] = ik[k];
-        top_p[row * K + k] = pk[k];
-        top_w[row * K + k] = pk[k] / sk;
-      }
-    }
-  }
-}
-
-// RMSNorm of the feed-forward input fused with the router (src/mixtral.rs:
-// 311-327, softmax :924-929, topk_renorm :931-939).  Router logits are
-// computed in fp32 from the fp32 normalised row (not from its rounded copy),
-// so routing decisions only differ from the fp32 lens at near-ties.
-// Tie-break: higher probability first, then lower expert index.
-template <typename T>
-__global__ void k_rmsnorm_router(const float* __restrict__ x, const T* __restrict__ w,
-                                 const T* __restrict__ wr, const float* __restrict__ bias, int D,
-                                 int E, int K, float eps, T* __restrict__ y,
-                                 float* __restrict__ inv, float* __restrict__ probs,
-                                 int* __restrict__ top_i, float* __restrict__ top_p,
-                                 float* __restrict__ top_w) {
-  const int64_t row = blockIdx.x;
-  const float* xr = x + row * D;
-  __shared__ float red[32];
-  __shared__ float lg[kMaxExperts * 8];  // per-warp partial logits (<= 8 warps)
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) {
-    float v = xr[i];
-    ss += v * v;
-  }
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-    v = warp_sum(v);
-    if (threadIdx.x == 0) red[0] = v;
-  }
-  __syncthreads();
-  const float r = 1.0f / sqrtf(red[0] / (float)D + eps);
-  if (threadIdx.x == 0) inv[row] = r;
-  float part[kMaxExperts];
-#pragma unroll
-  for (int e = 0; e < kMaxExperts; ++e) part[e] = 0.f;
-  for (int i = threadIdx.x; i < D; i += blockDim.x) {
-    float xn = xr[i] * r * ld(&w[i]);
-    st(&y[row * D + i], xn);
-#pragma unroll
-    for (int e = 0; e < kMaxExperts; ++e)
-      if (e < E) part[e] += xn * ld(&wr[(int64_t)i * E + e]);
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int e = 0; e < kMaxExperts; ++e) {
-    if (e < E) {
-      float v = warp_sum(part[e]);
-      if (lane == 0) lg[warp * kMaxExperts + e] = v;
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0)
-    router_select(lg, blockDim.x >> 5, bias, E, K, row, probs, top_i, top_p, top_w);
-}
-
 // ------------------------------------------- vectorised row kernels
 // The kernels below are the row kernels above with 4-wide accesses (float4
 // for fp32, 8-byte bf16 quads) and the row held in registers between the
@@ -266,70 +104,325 @@ __global__ void __launch_bounds__(256) k_rmsnorm_fwd_v(const float* __restrict__
   }
 }
 
-// RMSNorm of the feed-forward input fused with the router, NV quads per
-// thread; E8: the router has 8 experts and its rows are read 16 or 32
-// bytes at a time.
-template <typename T, int NV, bool E8>
-__global__ void __launch_bounds__(256) k_rmsnorm_router_v(
-    const float* __restrict__ x, const T* __restrict__ w, const T* __restrict__ wr,
-    const float* __restrict__ bias, int D, int E, int K, float eps, T* __restrict__ y,
-    float* __restrict__ inv, float* __restrict__ probs, int* __restrict__ top_i,
-    float* __restrict__ top_p, float* __restrict__ top_w) {
-  const int64_t row = blockIdx.x;
-  const int D4 = D >> 2;
-  const float* xr = x + row * D;
-  __shared__ float red[33];
-  __shared__ float lg[kMaxExperts * 8];  // per-warp partial logits (8 warps)
-  float4 xv[NV];
-  float ss = 0.f;
+// ------------------------------------------------------------- router stage
+// RMSNorm of the feed-forward input and the router, in the crate's
+// arithmetic (rmsnorm src/mixtral.rs:667-684, router logits `linear`
+// :616-628 at :312, softmax :924-929, topk_renorm :931-939): every sum runs
+// over the model dimension in index order from 0.0f, no multiply-add is
+// fused (__fmul_rn / __fadd_rn; paired .f32x2 multiply-add sequences are
+// not used because they do not keep the two roundings apart), division and
+// square root are IEEE, and exp is evaluated in double precision and
+// rounded once to float.  On the same input row the routing is therefore
+// the crate's to the bit (an exp result can differ in its last bit only
+// where the libm's own result is not the correctly rounded one).
+//
+// Sequential sums leave one dependent chain per row and expert, so four
+// lanes share a row: each sums the squares of the whole row (the same chain,
+// so the same value) and then owns E / 4 of the router's logit chains.  A
+// warp takes 8 rows, which stream through a per-warp shared tile of 8 rows x
+// 64 columns (row pitch 68 floats: the coalesced 16-byte stores and the
+// rows' 16-byte reads are bank-conflict free), two tiles ahead in registers.
+// Pass 1 sums the squares; pass 2 writes xn = (x * r) * w from the tile in
+// its coalesced layout and accumulates the logits.
+constexpr int kRtLanes = 4;               // lanes per row
+constexpr int kRtRows = 32 / kRtLanes;    // rows per warp
+constexpr int kRtCols = 64;               // columns per tile
+constexpr int kRtPitch = kRtCols + 4;     // floats per tile row in shared memory
+constexpr int kRtWarps = 4;               // warps per CTA
+
+template <bool VEC>
+struct RowTile {
+  float v[16];
+  // columns [c0, c0 + 64) of rows r0 .. r0 + 7 (zeros outside the matrix)
+  __device__ __forceinline__ void load(const float* __restrict__ x, int64_t rows, int D,
+                                       int64_t r0, int c0, int lane) {
+    if (VEC) {
 #pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int i = threadIdx.x + j * 256;
-    if (i < D4) {
-      xv[j] = ld4(xr + 4 * i);
-      ss += xv[j].x * xv[j].x + xv[j].y * xv[j].y + xv[j].z * xv[j].z + xv[j].w * xv[j].w;
+      for (int j = 0; j < 4; ++j) {
+        const int64_t row = r0 + (lane >> 4) + 2 * j;
+        const int col = c0 + 4 * (lane & 15);
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row < rows && col < D) t = *reinterpret_cast<const float4*>(x + row * D + col);
+        v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int64_t row = r0 + (j >> 1);
+        const int col = c0 + 32 * (j & 1) + lane;
+        v[j] = (row < rows && col < D) ? x[row * D + col] : 0.f;
+      }
     }
   }
-  ss = block_sum(ss, red);
-  const float r = 1.0f / sqrtf(ss / (float)D + eps);
-  if (threadIdx.x == 0) inv[row] = r;
-  float part[kMaxExperts];
+  __device__ __forceinline__ void store(float* tile, int lane) const {
+    if (VEC) {
 #pragma unroll
-  for (int e = 0; e < kMaxExperts; ++e) part[e] = 0.f;
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<float4*>(tile + ((lane >> 4) + 2 * j) * kRtPitch + 4 * (lane & 15)) =
+            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
 #pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int i = threadIdx.x + j * 256;
-    if (i < D4) {
-      const float4 wv = ld4(w + 4 * i);
-      const float xn[4] = {xv[j].x * r * wv.x, xv[j].y * r * wv.y, xv[j].z * r * wv.z,
-                           xv[j].w * r * wv.w};
-      st4(y + row * D + 4 * i, make_float4(xn[0], xn[1], xn[2], xn[3]));
+      for (int j = 0; j < 16; ++j) tile[(j >> 1) * kRtPitch + 32 * (j & 1) + lane] = v[j];
+    }
+  }
+};
+
+// Stream columns [0, D) of the warp's rows through its two shared tiles;
+// f(tile, c0, ncols) runs once per tile on every lane.
+template <bool VEC, class F>
+__device__ __forceinline__ void stream_rows(const float* __restrict__ x, int64_t rows, int D,
+                                            int64_t r0, float* tiles, int lane, F&& f) {
+  const int nt = (D + kRtCols - 1) / kRtCols;
+  RowTile<VEC> a, b;
+  a.load(x, rows, D, r0, 0, lane);
+  if (nt > 1) b.load(x, rows, D, r0, kRtCols, lane);
+  for (int t = 0; t < nt; ++t) {
+    __syncwarp();
+    float* slot = tiles + (t & 1) * kRtRows * kRtPitch;
+    if (t & 1) {
+      b.store(slot, lane);
+      if (t + 2 < nt) b.load(x, rows, D, r0, kRtCols * (t + 2), lane);
+    } else {
+      a.store(slot, lane);
+      if (t + 2 < nt) a.load(x, rows, D, r0, kRtCols * (t + 2), lane);
+    }
+    __syncwarp();
+    f(slot, kRtCols * t, min(kRtCols, D - kRtCols * t));
+  }
+}
+
+// The norm weights and router rows of one tile (64 model rows), loaded one
+// tile ahead into registers (lane l: model rows l and l + 32) and stored in
+// fp32 for the lane groups: the norm weights at ws[c], the router weights of
+// group q (experts q * EPL .. + EPL - 1) at wrs[q * QS + c * EPL + k].
+template <typename T, int NE>
+struct TileWeights {
+  static constexpr int EPL = NE / kRtLanes;
+  static constexpr int QS = kRtCols * EPL + 4;
+  static constexpr bool WIDE = NE == 8;  // a router row is 16 (bf16) or 32 (fp32) bytes
+  float wn[2];
+  float wv[2][NE];
+  __device__ __forceinline__ void load(const T* __restrict__ w, const T* __restrict__ wr, int E,
+                                       int D, int c0, int lane) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const T* wrow = wr + (int64_t)(4 * i + u) * E;
-        if (E8) {
-          float wv8[8];
-          ld_row8(wrow, wv8);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) part[e] += xn[u] * wv8[e];
+    for (int h = 0; h < 2; ++h) {
+      const int c = c0 + lane + 32 * h;
+      const bool in = c < D;
+      wn[h] = in ? ld(&w[c]) : 0.f;
+      if (EPL == 0) continue;
+      if (WIDE && in) {
+        if (sizeof(T) == 2) {
+          ld_row8(wr + (int64_t)c * 8, wv[h]);
         } else {
+          const float4 a = *reinterpret_cast<const float4*>(wr + (int64_t)c * 8);
+          const float4 b = *reinterpret_cast<const float4*>(wr + (int64_t)c * 8 + 4);
+          wv[h][0] = a.x; wv[h][1] = a.y; wv[h][2] = a.z; wv[h][3] = a.w;
+          wv[h][4] = b.x; wv[h][5] = b.y; wv[h][6] = b.z; wv[h][7] = b.w;
+        }
+      } else {
 #pragma unroll
-          for (int e = 0; e < kMaxExperts; ++e)
-            if (e < E) part[e] += xn[u] * ld(&wrow[e]);
+        for (int e = 0; e < NE; ++e) wv[h][e] = (in && e < E) ? ld(&wr[(int64_t)c * E + e]) : 0.f;
+      }
+    }
+  }
+  __device__ __forceinline__ void store(float* ws, float* wrs, int lane) const {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = lane + 32 * h;
+      ws[c] = wn[h];
+#pragma unroll
+      for (int e = 0; e < NE; e += EPL > 0 ? EPL : NE) {
+        if (EPL == 2) {
+          *reinterpret_cast<float2*>(wrs + (e / 2) * QS + c * 2) = make_float2(wv[h][e], wv[h][e + 1]);
+        } else if (EPL == 4) {
+          *reinterpret_cast<float4*>(wrs + (e / 4) * QS + c * 4) =
+              make_float4(wv[h][e], wv[h][e + 1], wv[h][e + 2], wv[h][e + 3]);
+        } else if (EPL > 0) {
+#pragma unroll
+          for (int k = 0; k < EPL; ++k) wrs[(e / EPL) * QS + c * EPL + k] = wv[h][e + k];
         }
       }
     }
   }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+};
+
+// Crate-rounded exp: double-precision exp of the float argument, rounded
+// once to float.
+__device__ __forceinline__ float exp_rounded(float z) { return __double2float_rn(exp((double)z)); }
+
+template <typename T, int NE, bool VEC>
+__global__ void __launch_bounds__(32 * kRtWarps, 6) k_router_stage(
+    const float* __restrict__ x, const T* __restrict__ w, const T* __restrict__ wr,
+    const float* __restrict__ bias, int64_t rows, int D, int E, int K, float eps,
+    T* __restrict__ y, float* __restrict__ inv, float* __restrict__ probs,
+    int* __restrict__ top_i, float* __restrict__ top_p, float* __restrict__ top_w) {
+  constexpr int EPL = NE / kRtLanes;            // logit chains per lane (0 when E == 1)
+  constexpr int QS = TileWeights<T, NE>::QS;    // floats per lane group in wrs
+  __shared__ __align__(16) float tiles_all[kRtWarps][2 * kRtRows * kRtPitch];
+  __shared__ __align__(16) float wr_all[kRtWarps][EPL > 0 ? kRtLanes * QS : 4];
+  __shared__ __align__(16) float w_all[kRtWarps][kRtCols];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int rr = lane / kRtLanes, q = lane % kRtLanes;  // row in the warp, logit group
+  const int64_t r0 = ((int64_t)blockIdx.x * kRtWarps + wid) * kRtRows;
+  if (r0 >= rows) return;  // whole warp
+  const int64_t row = r0 + rr;
+  const bool live = row < rows;
+  float* tiles = tiles_all[wid];
+  float* wrs = wr_all[wid];
+  float* ws = w_all[wid];
+
+  // pass 1: sum of squares in index order (src/mixtral.rs:672-676)
+  float ss = 0.0f;
+  stream_rows<VEC>(x, rows, D, r0, tiles, lane, [&](const float* tile, int, int n) {
+    const float* mine = tile + rr * kRtPitch;
+    if (n == kRtCols) {
 #pragma unroll
-  for (int e = 0; e < kMaxExperts; ++e) {
+      for (int c = 0; c < kRtCols; c += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(mine + c);
+        ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
+        ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
+        ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
+        ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
+      }
+    } else {
+      for (int c = 0; c < n; ++c) ss = __fadd_rn(ss, __fmul_rn(mine[c], mine[c]));
+    }
+  });
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+  if (live && q == 0) inv[row] = r;
+
+  // pass 2: xn = (x * r) * w written out; logits z_e = sum_i xn_i wr[i, e]
+  float z[EPL > 0 ? EPL : 1];
+#pragma unroll
+  for (int k = 0; k < (EPL > 0 ? EPL : 1); ++k) z[k] = 0.0f;
+  TileWeights<T, NE> tw;
+  tw.load(w, wr, E, D, 0, lane);
+  stream_rows<VEC>(x, rows, D, r0, tiles, lane, [&](const float* tile, int c0, int n) {
+    // this tile's weights to shared memory, the next tile's into registers
+    tw.store(ws, wrs, lane);
+    if (c0 + kRtCols < D) tw.load(w, wr, E, D, c0 + kRtCols, lane);
+    __syncwarp();
+    if (VEC && n == kRtCols) {
+      // xn from the tile in its coalesced layout: rows (lane / 16) + 2 j,
+      // columns 4 (lane % 16) .. + 3
+      const float4 wv = *reinterpret_cast<const float4*>(ws + 4 * (lane & 15));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int tr = (lane >> 4) + 2 * j;
+        const float rj = __shfl_sync(0xffffffffu, r, tr * kRtLanes);
+        const float4 xv = *reinterpret_cast<const float4*>(tile + tr * kRtPitch + 4 * (lane & 15));
+        if (r0 + tr < rows)
+          st4(y + (r0 + tr) * D + c0 + 4 * (lane & 15),
+              make_float4(__fmul_rn(__fmul_rn(xv.x, rj), wv.x), __fmul_rn(__fmul_rn(xv.y, rj), wv.y),
+                          __fmul_rn(__fmul_rn(xv.z, rj), wv.z), __fmul_rn(__fmul_rn(xv.w, rj), wv.w)));
+      }
+    } else if (live && q == 0) {
+      const float* mine = tile + rr * kRtPitch;
+      for (int c = 0; c < n; ++c) st(&y[row * D + c0 + c], __fmul_rn(__fmul_rn(mine[c], r), ws[c]));
+    }
+    if (EPL > 0) {
+      const float* mine = tile + rr * kRtPitch;
+      const float* wq = wrs + q * QS;
+      auto step = [&](float xv, float wv, int c) {
+        const float xn = __fmul_rn(__fmul_rn(xv, r), wv);
+        if (EPL == 2) {
+          const float2 g = *reinterpret_cast<const float2*>(wq + c * 2);
+          z[0] = __fadd_rn(z[0], __fmul_rn(xn, g.x));
+          z[EPL > 1 ? 1 : 0] = __fadd_rn(z[EPL > 1 ? 1 : 0], __fmul_rn(xn, g.y));
+        } else if (EPL == 4) {
+          const float4 g = *reinterpret_cast<const float4*>(wq + c * 4);
+          z[0] = __fadd_rn(z[0], __fmul_rn(xn, g.x));
+          z[EPL > 1 ? 1 : 0] = __fadd_rn(z[EPL > 1 ? 1 : 0], __fmul_rn(xn, g.y));
+          z[EPL > 2 ? 2 : 0] = __fadd_rn(z[EPL > 2 ? 2 : 0], __fmul_rn(xn, g.z));
+          z[EPL > 3 ? 3 : 0] = __fadd_rn(z[EPL > 3 ? 3 : 0], __fmul_rn(xn, g.w));
+        } else {
+#pragma unroll
+          for (int k = 0; k < EPL; ++k) z[k] = __fadd_rn(z[k], __fmul_rn(xn, wq[c * EPL + k]));
+        }
+      };
+      if (n == kRtCols) {
+#pragma unroll
+        for (int c = 0; c < kRtCols; c += 4) {
+          const float4 xv = *reinterpret_cast<const float4*>(mine + c);
+          const float4 wv = *reinterpret_cast<const float4*>(ws + c);
+          step(xv.x, wv.x, c);
+          step(xv.y, wv.y, c + 1);
+          step(xv.z, wv.z, c + 2);
+          step(xv.w, wv.w, c + 3);
+        }
+      } else {
+        for (int c = 0; c < n; ++c) step(mine[c], ws[c], c);
+      }
+    }
+    __syncwarp();
+  });
+  // every lane of the row's group gathers the row's E logits
+  float zf[NE];
+#pragma unroll
+  for (int e = 0; e < NE; ++e)
+    zf[e] = EPL > 0 ? __shfl_sync(0xffffffffu, z[EPL > 0 ? e % EPL : 0],
+                                  rr * kRtLanes + (EPL > 0 ? e / EPL : 0))
+                    : 0.0f;
+  if (!live || q != 0) return;
+
+  // bias (skewed routing), softmax (src/mixtral.rs:924-929)
+  float m = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < NE; ++e) {
     if (e < E) {
-      float v = warp_sum(part[e]);
-      if (lane == 0) lg[warp * kMaxExperts + e] = v;
+      if (bias) zf[e] = __fadd_rn(zf[e], bias[e]);
+      m = fmaxf(m, zf[e]);
     }
   }
-  __syncthreads();
-  if (threadIdx.x < 32) router_select_warp(lg, 8, bias, E, K, row, probs, top_i, top_p, top_w);
+  float p[NE];
+  float s = 0.0f;
+#pragma unroll
+  for (int e = 0; e < NE; ++e) {
+    p[e] = e < E ? exp_rounded(__fsub_rn(zf[e], m)) : 0.f;
+    if (e < E) s = __fadd_rn(s, p[e]);
+  }
+#pragma unroll
+  for (int e = 0; e < NE; ++e) {
+    if (e < E) {
+      p[e] = __fdiv_rn(p[e], s);
+      probs[row * E + e] = p[e];
+    }
+  }
+  // topk_renorm (src/mixtral.rs:931-939): probability desc, then index asc
+  unsigned taken = 0;
+  float pk[kMaxTopK];
+  int ik[kMaxTopK];
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) {
+    pk[k] = 0.f;
+    ik[k] = 0;
+    if (k < K) {
+      int best = -1;
+      float bp = 0.f;
+#pragma unroll
+      for (int e = 0; e < NE; ++e) {
+        if (e < E && !((taken >> e) & 1u) && (best < 0 || p[e] > bp)) {
+          best = e;
+          bp = p[e];
+        }
+      }
+      taken |= 1u << best;
+      ik[k] = best;
+      pk[k] = bp;
+    }
+  }
+  float sk = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k)
+    if (k < K) sk = __fadd_rn(sk, pk[k]);
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) {
+    if (k < K) {
+      top_i[row * K + k] = ik[k];
+      top_p[row * K + k] = pk[k];
+      top_w[row * K + k] = __fdiv_rn(pk[k], sk);
+    }
+  }
 }
 
 // Xp[r] = xn[row_token[r]] in 16-byte words (zero rows for padding).
@@ -1057,20 +1150,17 @@ void rmsnorm_router(const float* x, const T* w, const T* wr, const float* bias, 
                     int D, int E, int K, float eps, T* y, float* inv, float* probs, int* top_i,
                     float* top_p, float* top_w, cudaStream_t s, int64_t& launches) {
   DOP_REQUIRE(E <= kMaxExperts && K <= kMaxTopK && K <= E, "experts/top_k out of range");
-  const int nv = row_quads(D);
-  if (nv && aligned4(x) && aligned4(w) && aligned4(y)) {
-    const bool e8 = E == 8 && (uintptr_t)wr % 16 == 0;
-#define DOP_ROUTER_V(NV)                                                              \
-  (e8 ? k_rmsnorm_router_v<T, NV, true> : k_rmsnorm_router_v<T, NV, false>)
-    auto k = nv == 1 ? DOP_ROUTER_V(1) : nv == 2 ? DOP_ROUTER_V(2)
-           : nv == 4 ? DOP_ROUTER_V(4) : DOP_ROUTER_V(8);
-#undef DOP_ROUTER_V
-    k<<<(unsigned)rows, 256, 0, s>>>(x, w, wr, bias, D, E, K, eps, y, inv, probs, top_i, top_p,
-                                     top_w);
-  } else {
-    k_rmsnorm_router<T><<<(unsigned)rows, 256, 0, s>>>(x, w, wr, bias, D, E, K, eps, y, inv,
-                                                       probs, top_i, top_p, top_w);
-  }
+  const bool vec = D % 4 == 0 && aligned4(x) && aligned4(y);
+  const unsigned grid = (unsigned)ceil_div(rows, kRtRows * kRtWarps);
+  const dim3 block(32 * kRtWarps);
+#define DOP_ROUTER(NE)                                                                        \
+  (vec ? k_router_stage<T, NE, true> : k_router_stage<T, NE, false>)<<<grid, block, 0, s>>>( \
+      x, w, wr, bias, rows, D, E, K, eps, y, inv, probs, top_i, top_p, top_w)
+  if (E == 1) DOP_ROUTER(1);
+  else if (E <= 4) DOP_ROUTER(4);
+  else if (E <= 8) DOP_ROUTER(8);
+  else DOP_ROUTER(16);
+#undef DOP_ROUTER
   DOP_LAUNCHED(launches);
 }
 

@@ -72,7 +72,7 @@ def run_and_compare(cfg, batch, seq, seed):
     y = blk.forward(P, X)
     dx = blk.backward(P, DY, dP)
     torch.cuda.synchronize()
-    stage_flips = check_router_stage(cfg, blk, lp)
+    stage_flips, _ = check_router_stage(cfg, blk, lp)
     gpu = dict(y=y.cpu().numpy().reshape(-1), dx=dx.cpu().numpy().reshape(-1),
                dP=dP.cpu().numpy(), top_i=blk.routing()[0].cpu().numpy())
     del dP
@@ -123,6 +123,9 @@ def test_mixtral8x7b_router_stage_at_scale(cuda):
             blk.set_router_bias(torch.tensor(bias, device="cuda"))
         blk.forward(P, X)
         torch.cuda.synchronize()
-        flips = check_router_stage(cfg, blk, lp, bias)
+        flips, exact = check_router_stage(cfg, blk, lp, bias)
         assert flips <= 2, f"{flips} tokens at decision gaps below 1e-6"
+        # the crate's arithmetic: probability rows bit-identical but for a
+        # rare last-bit exp rounding
+        assert exact >= 0.99, f"only {exact:.4f} of the probability rows are bit-identical"
         blk.close()
