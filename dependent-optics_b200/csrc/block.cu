@@ -141,8 +141,12 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
     cv.take(dv_a, a * T * kvd, base_);
     if (ep) {
       cv.take(ep_flags, 4 * kEpBarriers * kEpMaxWorld, base_);
-      cv.take(send_off, 4 * E, base_);
-      cv.take(recv_seg_off, 4 * (ep_local + 1), base_);
+      cv.take(piece_pos, 4 * E, base_);
+      cv.take(ep_bounds, 4 * (kEpMaxWorld + 1), base_);
+      cv.take(recv_seg_off, 4 * (E + 1), base_);
+      cv.take(own_end, 4 * E, base_);
+      cv.take(help_end, 4 * E, base_);
+      cv.take(helpers, 4 * E, base_);
       cv.take(recv_tile_expert, 4 * recv_tiles, base_);
       cv.take(recv_tile_src, 4 * recv_tiles, base_);
       cv.take(recv_tile_row0, 4 * recv_tiles, base_);
@@ -153,6 +157,7 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
       cv.take(dOr, 2 * recv_cap * D, base_);
       cv.take(outr, 4 * recv_cap * D, base_);
       cv.take(dxpr, 4 * recv_cap * D, base_);
+      cv.take(dw_help, 4 * E * off.expert_stride, base_);
     }
     return cv.at;
   };
@@ -182,6 +187,8 @@ Block::~Block() {
   if (ep_stream) cudaStreamDestroy(ep_stream);
   if (ep_ev_dx) cudaEventDestroy(ep_ev_dx);
   if (ep_ev_combined) cudaEventDestroy(ep_ev_combined);
+  if (ep_ev_dw) cudaEventDestroy(ep_ev_dw);
+  if (ep_ev_reduced) cudaEventDestroy(ep_ev_reduced);
   if (expert_adjoint_done) cudaEventDestroy(expert_adjoint_done);
   for (auto& p : phases) {
     cudaEventDestroy(p.a);
@@ -193,14 +200,16 @@ Block::~Block() {
 // ------------------------------------------------------ expert parallelism
 EpView Block::ep_view() const {
   EpView v;
-  v.rank = ep_rank; v.world = ep_world; v.local = ep_local;
+  v.rank = ep_rank; v.world = ep_world; v.local = ep_local; v.E = (int)cfg.experts;
   v.recv_tiles = (int)(recv_cap / kRowAlign);
   v.recv_cap = recv_cap;
+  v.expert_stride = off.expert_stride;
   v.peers = ep_peers_dev; v.flags = ep_flags;
-  v.seg_off = seg_off; v.row_token = row_token; v.send_off = send_off;
-  v.recv_seg_off = recv_seg_off; v.recv_tile_expert = recv_tile_expert;
+  v.seg_off = seg_off; v.row_token = row_token; v.piece_pos = piece_pos; v.bounds = ep_bounds;
+  v.recv_seg_off = recv_seg_off; v.own_end = own_end; v.help_end = help_end; v.helpers = helpers;
+  v.recv_tile_expert = recv_tile_expert;
   v.recv_tile_src = recv_tile_src; v.recv_tile_row0 = recv_tile_row0;
-  v.xr = (bf16*)xr; v.outr = outr; v.dxpr = dxpr;
+  v.xr = (bf16*)xr; v.outr = outr; v.dxpr = dxpr; v.dw_help = dw_help;
   return v;
 }
 
@@ -224,26 +233,29 @@ void Block::ep_barrier_next(int k, cudaStream_t s) {
 }
 
 // Forward experts of an expert-parallel block, after the permutation:
-// gather the receive rows from the sources, gate/up (SwiGLU) and down over
-// this rank's experts, then combine the owners' outputs into y.
+// plan the step (which rank processes which rows), gather this rank's
+// receive rows from the sources, gate/up (SwiGLU) and down over them, then
+// combine the processing ranks' outputs into y.  The grouped GEMMs run over
+// every expert (absolute expert indices; the experts this rank has no rows
+// of are empty segments).
 void Block::ep_fwd_experts(const bf16* P, float* y, cudaStream_t s) {
   const int64_t D = cfg.dim, I = cfg.intermediate, K = cfg.top_k;
-  const int64_t ex0 = (int64_t)ep_rank * ep_local * off.expert_stride;  // first local expert
+  const int E = (int)cfg.experts;
   const EpView v = ep_view();
   ph_begin("ep_wait_rows", s);
   ep_barrier_next(0, s);  // every rank's xn2, row_token, seg_off are written
   ph_end(s);
   ph_begin("ep_dispatch", s);
-  ep_layout(v, (int)cfg.experts, s, launches);
+  ep_layout(v, s, launches);
   ep_gather_tokens(v, (const bf16*)xn2, (int)D, s, launches);
   ph_end(s);
   ph_begin("expert_gate_up", s);
   {
     Gemm gg; gg.M = recv_cap; gg.N = I; gg.K = D; gg.A = xr; gg.lda = D;
-    gg.B = P + off.gate0 + ex0; gg.ldb = I; gg.C = gr; gg.ldc = I; gg.c_f32 = false;
-    gg.group = 1; gg.seg_off = recv_seg_off; gg.tile_expert = recv_tile_expert; gg.G = ep_local;
+    gg.B = P + off.gate0; gg.ldb = I; gg.C = gr; gg.ldc = I; gg.c_f32 = false;
+    gg.group = 1; gg.seg_off = recv_seg_off; gg.tile_expert = recv_tile_expert; gg.G = E;
     gg.b_gs = off.expert_stride;
-    TcEpilogue te; te.kind = kTcSwiGLU; te.up_B = P + off.up0 + ex0;
+    TcEpilogue te; te.kind = kTcSwiGLU; te.up_B = P + off.up0;
     te.g_out = (bf16*)gr; te.u_out = (bf16*)ur; te.h_out = (bf16*)hr; te.ldg = I;
     gemm_tc(gg, nullptr, 0, te, s, launches);
   }
@@ -251,14 +263,14 @@ void Block::ep_fwd_experts(const bf16* P, float* y, cudaStream_t s) {
   ph_begin("expert_down", s);
   {
     Gemm gd; gd.M = recv_cap; gd.N = D; gd.K = I; gd.A = hr; gd.lda = I;
-    gd.B = P + off.down0 + ex0; gd.ldb = D; gd.C = outr; gd.ldc = D;
-    gd.group = 1; gd.seg_off = recv_seg_off; gd.tile_expert = recv_tile_expert; gd.G = ep_local;
+    gd.B = P + off.down0; gd.ldb = D; gd.C = outr; gd.ldc = D;
+    gd.group = 1; gd.seg_off = recv_seg_off; gd.tile_expert = recv_tile_expert; gd.G = E;
     gd.b_gs = off.expert_stride;
     gemm<bf16>(gd, s);
   }
   ph_end(s);
   ph_begin("ep_wait_outputs", s);
-  ep_barrier_next(1, s);  // every owner's expert outputs are written
+  ep_barrier_next(1, s);  // every rank's expert outputs are written
   ph_end(s);
   ph_begin("combine", s);
   ep_combine(v, mid, top_i, slot_row, top_w, T, (int)K, (int)D, out, y, s, launches);
@@ -266,12 +278,15 @@ void Block::ep_fwd_experts(const bf16* P, float* y, cudaStream_t s) {
 }
 
 // Backward experts of an expert-parallel block, after the output cotangent
-// rows dO are written: gather them at the owners, dH with the SwiGLU
-// adjoint, this rank's expert weight adjoints, and dXp for the sources.
+// rows dO are written: gather them for this rank's rows, dH with the SwiGLU
+// adjoint, the weight adjoints of this rank's rows (into dparams for the
+// experts it owns, into dw_help for the others), and dXp for the sources.
+// After the last barrier the owner adds the helpers' partial adjoints.
 void Block::ep_bwd_experts(const bf16* P, float* dP, cudaStream_t s) {
   const int64_t D = cfg.dim, I = cfg.intermediate;
-  const int64_t ex0 = (int64_t)ep_rank * ep_local * off.expert_stride;
+  const int E = (int)cfg.experts;
   const EpView v = ep_view();
+  const int64_t up_at = off.up0 - off.gate0, down_at = off.down0 - off.gate0;
   ph_begin("ep_wait_dO", s);
   ep_barrier_next(2, s);  // every rank's dO is written
   ph_end(s);
@@ -281,8 +296,8 @@ void Block::ep_bwd_experts(const bf16* P, float* dP, cudaStream_t s) {
   ph_begin("expert_dh", s);
   {
     Gemm g1; g1.M = recv_cap; g1.N = I; g1.K = D; g1.A = dOr; g1.lda = D;
-    g1.B = P + off.down0 + ex0; g1.ldb = D; g1.b_t = true; g1.C = dh; g1.ldc = I;
-    g1.group = 1; g1.seg_off = recv_seg_off; g1.tile_expert = recv_tile_expert; g1.G = ep_local;
+    g1.B = P + off.down0; g1.ldb = D; g1.b_t = true; g1.C = dh; g1.ldc = I;
+    g1.group = 1; g1.seg_off = recv_seg_off; g1.tile_expert = recv_tile_expert; g1.G = E;
     g1.b_gs = off.expert_stride;
     // dg, du overwrite g, u in place (each element is read before it is written)
     TcEpilogue te; te.kind = kTcSwiGLUBwd; te.g_in = (const bf16*)gr; te.u_in = (const bf16*)ur;
@@ -290,48 +305,67 @@ void Block::ep_bwd_experts(const bf16* P, float* dP, cudaStream_t s) {
     gemm_tc(g1, nullptr, 0, te, s, launches);
   }
   ph_end(s);
+  // a grouped weight adjoint over this rank's rows: the owned experts'
+  // segments accumulate into dparams, the others' overwrite dw_help
+  auto dw = [&](Gemm g, int64_t at) {
+    Gemm own = g;
+    own.C = dP + off.gate0 + at; own.epi = Epi::Accum; own.seg_end = own_end;
+    gemm<bf16>(own, s);
+    Gemm help = g;
+    help.C = dw_help + at; help.epi = Epi::Store; help.seg_end = help_end;
+    gemm<bf16>(help, s);
+  };
   ph_begin("expert_dw_down", s);
   {
     Gemm g2; g2.M = I; g2.N = D; g2.K = recv_cap; g2.A = hr; g2.lda = I; g2.a_t = true;
-    g2.B = dOr; g2.ldb = D; g2.C = dP + off.down0 + ex0; g2.ldc = D; g2.epi = Epi::Accum;
-    g2.group = 2; g2.seg_off = recv_seg_off; g2.G = ep_local; g2.c_gs = off.expert_stride;
-    gemm<bf16>(g2, s);
+    g2.B = dOr; g2.ldb = D; g2.ldc = D;
+    g2.group = 2; g2.seg_off = recv_seg_off; g2.G = E; g2.c_gs = off.expert_stride;
+    dw(g2, down_at);
   }
   ph_end(s);
   ph_begin("expert_dx", s);
   {
     Gemm g3; g3.M = recv_cap; g3.N = D; g3.K = I; g3.A = gr; g3.lda = I;
-    g3.B = P + off.gate0 + ex0; g3.ldb = I; g3.b_t = true; g3.C = dxpr; g3.ldc = D;
-    g3.group = 1; g3.seg_off = recv_seg_off; g3.tile_expert = recv_tile_expert; g3.G = ep_local;
+    g3.B = P + off.gate0; g3.ldb = I; g3.b_t = true; g3.C = dxpr; g3.ldc = D;
+    g3.group = 1; g3.seg_off = recv_seg_off; g3.tile_expert = recv_tile_expert; g3.G = E;
     g3.b_gs = off.expert_stride;
-    GemmPart up{ur, I, P + off.up0 + ex0, I, I};
+    GemmPart up{ur, I, P + off.up0, I, I};
     gemm<bf16>(g3, s, &up, 1);
   }
   ph_end(s);
-  // The sources' backward combine (wait for every owner's dXp, then read
+  // The sources' backward combine (wait for every rank's dXp, then read
   // this rank's pairs) runs on the exchange stream while this rank computes
-  // its experts' gate/up weight adjoints, which nothing there reads.
+  // its gate/up weight adjoints, which nothing there reads.
   if (!ep_stream) {
     DOP_CHECK_CUDA(cudaStreamCreateWithFlags(&ep_stream, cudaStreamNonBlocking));
     DOP_CHECK_CUDA(cudaEventCreateWithFlags(&ep_ev_dx, cudaEventDisableTiming));
     DOP_CHECK_CUDA(cudaEventCreateWithFlags(&ep_ev_combined, cudaEventDisableTiming));
+    DOP_CHECK_CUDA(cudaEventCreateWithFlags(&ep_ev_dw, cudaEventDisableTiming));
+    DOP_CHECK_CUDA(cudaEventCreateWithFlags(&ep_ev_reduced, cudaEventDisableTiming));
   }
   DOP_CHECK_CUDA(cudaEventRecord(ep_ev_dx, s));
   DOP_CHECK_CUDA(cudaStreamWaitEvent(ep_stream, ep_ev_dx, 0));
-  ep_barrier_next(3, ep_stream);  // every owner's dXp is written
-  ep_unpermute_router_dx<bf16>(v, top_i, slot_row, dz, P + off.router, T, (int)cfg.experts,
-                               (int)cfg.top_k, (int)D, dxn2, ep_stream, launches);
+  ep_barrier_next(3, ep_stream);  // every rank's dXp is written
+  ep_unpermute_router_dx<bf16>(v, top_i, slot_row, dz, P + off.router, T, E, (int)cfg.top_k,
+                               (int)D, dxn2, ep_stream, launches);
   DOP_CHECK_CUDA(cudaEventRecord(ep_ev_combined, ep_stream));
   ph_begin("expert_dw_gate_up", s);
   {
     Gemm g5; g5.M = D; g5.N = I; g5.K = recv_cap; g5.A = xr; g5.lda = D; g5.a_t = true;
-    g5.B = gr; g5.ldb = I; g5.C = dP + off.gate0 + ex0; g5.ldc = I; g5.epi = Epi::Accum;
-    g5.group = 2; g5.seg_off = recv_seg_off; g5.G = ep_local; g5.c_gs = off.expert_stride;
-    gemm<bf16>(g5, s);
-    Gemm g6 = g5; g6.B = ur; g6.C = dP + off.up0 + ex0;
-    gemm<bf16>(g6, s);
+    g5.B = gr; g5.ldb = I; g5.ldc = I;
+    g5.group = 2; g5.seg_off = recv_seg_off; g5.G = E; g5.c_gs = off.expert_stride;
+    dw(g5, 0);
+    Gemm g6 = g5; g6.B = ur;
+    dw(g6, up_at);
   }
   ph_end(s);
+  // every rank's partial adjoints are written: the owners add them (on the
+  // exchange stream, beside the attention half of the backward)
+  DOP_CHECK_CUDA(cudaEventRecord(ep_ev_dw, s));
+  DOP_CHECK_CUDA(cudaStreamWaitEvent(ep_stream, ep_ev_dw, 0));
+  ep_barrier_next(4, ep_stream);
+  ep_reduce_adjoint(v, dP + off.gate0, ep_stream, launches);
+  DOP_CHECK_CUDA(cudaEventRecord(ep_ev_reduced, ep_stream));
 }
 
 void Block::ph_begin(const char* name, cudaStream_t s) {
@@ -589,7 +623,8 @@ void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_
   if (adjoint_stream) {  // the experts' adjoints are final from here on
     if (!expert_adjoint_done)
       DOP_CHECK_CUDA(cudaEventCreateWithFlags(&expert_adjoint_done, cudaEventDisableTiming));
-    DOP_CHECK_CUDA(cudaEventRecord(expert_adjoint_done, s));
+    // expert parallel: final once the owners have added the helpers' partials
+    DOP_CHECK_CUDA(cudaEventRecord(expert_adjoint_done, ep ? ep_stream : s));
     DOP_CHECK_CUDA(cudaStreamWaitEvent(adjoint_stream, expert_adjoint_done, 0));
   }
   // d_xn2 = sum_k dXp[row(t,k)] + dz Wr^T; router weight adjoint
@@ -670,6 +705,9 @@ void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_
   rmsnorm_bwd<Act>(dxn, x_in, inv1, P + off.attn_norm, dmid, T, (int)D, dx, (Act*)nullptr,
                    dP + off.attn_norm, part, part_cap, s, launches);
   ph_end(s);
+  // expert parallel: the call's stream also covers the owners' reduction of
+  // the helpers' partial adjoints (and orders the next step after it)
+  if (ep) DOP_CHECK_CUDA(cudaStreamWaitEvent(s, ep_ev_reduced, 0));
 }
 
 }  // namespace dop

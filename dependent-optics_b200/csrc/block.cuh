@@ -48,12 +48,12 @@ struct Block {
   int64_t split_cap = 0;
   void *dO, *dg, *du, *dmid_a, *dmix, *dq_a, *dk_a, *dv_a;
 
-  // expert parallelism (ep_world > 1, bf16 only; ep.cu): this rank owns
-  // experts [ep_rank * ep_local, (ep_rank + 1) * ep_local) and holds the
-  // receive rows of every rank routed to them (capacity recv_cap =
-  // ep_world * rows_cap, the most any routing can send).  The receive
-  // buffers of g and u are reused for dg and du (the SwiGLU adjoint reads
-  // each element before it writes it).
+  // expert parallelism (ep_world > 1, bf16 only; ep.cu): this rank owns the
+  // adjoint of experts [ep_rank * ep_local, (ep_rank + 1) * ep_local) and
+  // processes the chunk of every rank's routed rows that the step's plan
+  // gives it (capacity recv_cap = ep_world * rows_cap, the most any routing
+  // can send).  The receive buffers of g and u are reused for dg and du (the
+  // SwiGLU adjoint reads each element before it writes it).
   int ep_rank = 0, ep_world = 1, ep_local = 0;
   int64_t recv_cap = 0;
   unsigned ep_epoch = 0;
@@ -62,10 +62,13 @@ struct Block {
   unsigned* ep_flags = nullptr;
   cudaStream_t ep_stream = nullptr;  // the backward combine, beside the dW GEMMs
   cudaEvent_t ep_ev_dx = nullptr, ep_ev_combined = nullptr;
-  int *send_off = nullptr, *recv_seg_off = nullptr, *recv_tile_expert = nullptr;
+  cudaEvent_t ep_ev_dw = nullptr, ep_ev_reduced = nullptr;
+  int *piece_pos = nullptr, *ep_bounds = nullptr, *recv_seg_off = nullptr;
+  int *own_end = nullptr, *help_end = nullptr, *helpers = nullptr, *recv_tile_expert = nullptr;
   int *recv_tile_src = nullptr, *recv_tile_row0 = nullptr;
   void *xr = nullptr, *gr = nullptr, *ur = nullptr, *hr = nullptr, *dOr = nullptr;
   float *outr = nullptr, *dxpr = nullptr;
+  float* dw_help = nullptr;  // [E][expert_stride] partial adjoints of experts owned elsewhere
   EpView ep_view() const;
   void ep_barrier_next(int k, cudaStream_t s);
   // Map the peers' workspaces (handles in rank order; own entry ignored).

@@ -22,14 +22,29 @@
 // one expert and the weight-gradient contraction of expert j runs over one
 // contiguous range.
 //
-// Ordering between ranks uses four flag barriers per step (k_ep_barrier):
+// Which rank processes which rows is decided every step by a plan that every
+// rank computes from the same routing counts (k_ep_layout): the expert-major
+// sequence of (expert, source) pieces is cut into `world` near-equal chunks,
+// snapping a cut to an expert boundary when one lies within a tenth of a
+// chunk.  Balanced routing thus keeps each expert whole on one rank; under
+// skewed routing a hot expert's rows are split over several ranks (its
+// weights are on every rank: the block reads the whole layer slice).  A rank
+// that processes rows of an expert it does not own writes that expert's
+// partial weight adjoint to dw_help; after the last barrier the owner adds
+// the helpers' partials, in rank order, into its dparams.  The split is
+// invisible in y and dx: a row's GEMMs do not depend on where the row runs.
+//
+// Ordering between ranks uses five flag barriers per step (k_ep_barrier):
 // after the permutation (sources' rows readable), after the down projection
 // (expert outputs readable), after the output-cotangent gather source is
 // written (dO readable), after the expert-input cotangent GEMM (dXp
-// readable).  Every buffer a peer reads is next overwritten only after the
-// following barrier, which the reader can only pass after its reads.  Waits
-// are bounded; a wait that runs out records a code in the device error word
-// and the kernels that follow skip their work.
+// readable), after the weight-adjoint GEMMs (partial adjoints readable).
+// Every buffer a peer reads is next overwritten only after a later barrier,
+// which the reader can only pass after its reads.  Waits are bounded; a wait
+// that runs out records a code in the device error word and the kernels that
+// follow skip their work.
+#include <climits>
+
 #include "ep.cuh"
 #include "tc_ptx.cuh"
 
@@ -85,48 +100,77 @@ __global__ void k_ep_barrier(EpView v, int k, unsigned epoch) {
   }
 }
 
-// Receive layout (one CTA): reads every rank's padded segment offsets and
-// writes this rank's receive segments, its tile -> (expert, source, source
-// row) map and, for this rank as a source, where its piece of each expert
-// starts in the owner's receive buffer.
-__global__ void k_ep_layout(EpView v, int E) {
+// The plan and this rank's receive layout (one CTA): reads every rank's
+// padded segment offsets, cuts the expert-major piece sequence into the
+// ranks' chunks, and writes this rank's receive segments per expert, its
+// tile -> (expert, source, source row) map, where this rank's own pieces sit
+// in the global sequence, and which ranks help with each expert.
+__global__ void k_ep_layout(EpView v) {
   if (tc::tc_failed()) return;  // an earlier wait gave up: skip (sticky error)
   __shared__ int so[kEpMaxWorld][kMaxExperts + 1];
-  const int W = v.world, Ed = E / W;
+  __shared__ int pstart[kMaxExperts][kEpMaxWorld];  // global start of piece (e, s)
+  __shared__ int estart[kMaxExperts + 1];
+  __shared__ int bnd[kEpMaxWorld + 1];
+  const int W = v.world, E = v.E;
   for (int i = threadIdx.x; i < W * (E + 1); i += blockDim.x) {
     const int s = i / (E + 1), e = i % (E + 1);
     so[s][e] = __ldcv(peer(v, s, v.seg_off) + e);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    // start of piece (local expert j, source s) in owner d's receive buffer
-    auto start = [&](int d, int j, int s) {
-      int at = 0;
-      for (int jj = 0; jj < j; ++jj)
-        for (int ss = 0; ss < W; ++ss) at += so[ss][d * Ed + jj + 1] - so[ss][d * Ed + jj];
-      for (int ss = 0; ss < s; ++ss) at += so[ss][d * Ed + j + 1] - so[ss][d * Ed + j];
-      return at;
-    };
-    for (int e = 0; e < E; ++e) v.send_off[e] = start(e / Ed, e % Ed, v.rank);
-    for (int j = 0; j < Ed; ++j) v.recv_seg_off[j] = start(v.rank, j, 0);
-    v.recv_seg_off[Ed] = start(v.rank, Ed - 1, W);  // every piece of every local expert
+    int at = 0;
+    for (int e = 0; e < E; ++e) {
+      estart[e] = at;
+      for (int s = 0; s < W; ++s) {
+        pstart[e][s] = at;
+        at += so[s][e + 1] - so[s][e];
+      }
+    }
+    estart[E] = at;
+    const int N = at;  // a multiple of kSegAlign: every piece is
+    bnd[0] = 0;
+    bnd[W] = N;
+    for (int d = 1; d < W; ++d) {
+      int cut = (int)((int64_t)N * d / W / kSegAlign * kSegAlign);
+      int best = cut, dist = INT_MAX;
+      for (int e = 0; e <= E; ++e) {
+        const int dd = abs(estart[e] - cut);
+        if (dd < dist) { dist = dd; best = estart[e]; }
+      }
+      if ((int64_t)dist * 10 * W <= N) cut = best;  // within a tenth of a chunk
+      bnd[d] = min(max(cut, bnd[d - 1]), N);
+    }
+    for (int d = 0; d <= W; ++d) v.bounds[d] = bnd[d];
+    const int lo = bnd[v.rank], hi = bnd[v.rank + 1];
+    for (int e = 0; e < E; ++e) v.piece_pos[e] = pstart[e][v.rank];
+    for (int e = 0; e <= E; ++e) v.recv_seg_off[e] = min(max(estart[e], lo), hi) - lo;
+    for (int e = 0; e < E; ++e) {
+      const int owner = e / v.local;
+      const bool mine = owner == v.rank;
+      v.own_end[e] = mine ? v.recv_seg_off[e + 1] : v.recv_seg_off[e];
+      v.help_end[e] = mine ? v.recv_seg_off[e] : v.recv_seg_off[e + 1];
+      int mask = 0;
+      for (int d = 0; d < W; ++d)
+        if (d != owner && bnd[d] < estart[e + 1] && bnd[d + 1] > estart[e]) mask |= 1 << d;
+      v.helpers[e] = mask;
+    }
   }
   __syncthreads();
   // tile map of this rank's receive buffer
-  const int d = v.rank;
+  const int lo = bnd[v.rank], rows = bnd[v.rank + 1] - lo;
   for (int t = threadIdx.x; t < v.recv_tiles; t += blockDim.x) {
-    const int row = t * kRowAlign;
     int ex = -1, src = -1, srow = 0;
-    int at = 0;
-    for (int j = 0; j < Ed && ex < 0; ++j)
-      for (int s = 0; s < W; ++s) {
-        const int e = d * Ed + j, n = so[s][e + 1] - so[s][e];
-        if (row >= at && row < at + n) {
-          ex = j; src = s; srow = so[s][e] + (row - at);
-          break;
+    if (t * kRowAlign < rows) {
+      const int g = lo + t * kRowAlign;
+      for (int e = 0; e < E && ex < 0; ++e)
+        for (int s = 0; s < W; ++s) {
+          const int n = so[s][e + 1] - so[s][e];
+          if (g >= pstart[e][s] && g < pstart[e][s] + n) {
+            ex = e; src = s; srow = so[s][e] + (g - pstart[e][s]);
+            break;
+          }
         }
-        at += n;
-      }
+    }
     v.recv_tile_expert[t] = ex;
     v.recv_tile_src[t] = src;
     v.recv_tile_row0[t] = srow;
@@ -153,7 +197,7 @@ __device__ __forceinline__ void copy_row16(uint4* dst, const uint4* src, int n16
 __global__ void k_ep_gather_tokens(EpView v, const bf16* xn2, int D) {
   if (tc::tc_failed()) return;
   const int n16 = D * 2 / 16;
-  const int rows = v.recv_seg_off[v.local];
+  const int rows = v.recv_seg_off[v.E];
   const int lane = threadIdx.x & 31;
   for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
        r += (int64_t)gridDim.x * (blockDim.x >> 5)) {
@@ -177,7 +221,7 @@ __global__ void k_ep_gather_tokens(EpView v, const bf16* xn2, int D) {
 __global__ void k_ep_gather_rows(EpView v, const bf16* dO, bf16* dst_rows, int D) {
   if (tc::tc_failed()) return;
   const int n16 = D * 2 / 16;
-  const int rows = v.recv_seg_off[v.local];
+  const int rows = v.recv_seg_off[v.E];
   const int lane = threadIdx.x & 31;
   for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
        r += (int64_t)gridDim.x * (blockDim.x >> 5)) {
@@ -191,10 +235,14 @@ __global__ void k_ep_gather_rows(EpView v, const bf16* dO, bf16* dst_rows, int D
   }
 }
 
-// Where (token, slot) pair p's row sits in its owner's receive buffer,
+// The rank that processed the row of this rank's expert-sorted row
+// `slot_row` (expert e) and where it sits in that rank's receive buffer,
 // clamped into the buffer (it is inside whenever the barriers held).
-__device__ __forceinline__ int64_t owner_row(const EpView& v, int e, int slot_row) {
-  const int64_t r = (int64_t)v.send_off[e] + (slot_row - v.seg_off[e]);
+__device__ __forceinline__ int64_t processed_at(const EpView& v, int e, int slot_row, int& d) {
+  const int pos = v.piece_pos[e] + (slot_row - v.seg_off[e]);
+  d = 0;
+  while (d + 1 < v.world && v.bounds[d + 1] <= pos) ++d;
+  const int64_t r = (int64_t)pos - v.bounds[d];
   return r < 0 ? 0 : (r >= v.recv_cap ? v.recv_cap - 1 : r);
 }
 
@@ -213,8 +261,9 @@ __global__ void k_ep_combine(EpView v, const float* __restrict__ mid, const int*
   if (threadIdx.x < K) {
     const int k = threadIdx.x;
     const int e = top_i[t * K + k], sr = slot_row[t * K + k];
-    const int d = e / v.local;
-    src[k] = reinterpret_cast<const float4*>(peer(v, d, v.outr) + owner_row(v, e, sr) * D);
+    int d;
+    const int64_t row = processed_at(v, e, sr, d);
+    src[k] = reinterpret_cast<const float4*>(peer(v, d, v.outr) + row * D);
     stash[k] = reinterpret_cast<float4*>(out + (int64_t)sr * D);
     ws[k] = top_w[t * K + k];
   }
@@ -262,7 +311,9 @@ __global__ void k_ep_unpermute_router_dx(EpView v, const int* __restrict__ top_i
   if (threadIdx.x < K) {
     const int k = threadIdx.x;
     const int e = top_i[t * K + k], sr = slot_row[t * K + k];
-    src[k] = reinterpret_cast<const float4*>(peer(v, e / v.local, v.dxpr) + owner_row(v, e, sr) * D);
+    int d;
+    const int64_t row = processed_at(v, e, sr, d);
+    src[k] = reinterpret_cast<const float4*>(peer(v, d, v.dxpr) + row * D);
   }
   __syncthreads();
   const int D4 = D / 4;
@@ -304,6 +355,45 @@ __global__ void k_ep_unpermute_router_dx(EpView v, const int* __restrict__ top_i
   }
 }
 
+// Owner side of the adjoint of the experts it owns: dP[e] += the partial
+// adjoints the helper ranks wrote for e, in rank order (VT = float4 when the
+// slices are 16-byte aligned, else float; every helper's load is issued
+// before the sum).
+template <typename VT>
+__global__ void k_ep_reduce_adjoint(EpView v, float* __restrict__ dP) {
+  if (tc::tc_failed()) return;
+  constexpr int W4 = sizeof(VT) / 4;
+  const int64_t nv = v.expert_stride / W4;
+  for (int j = 0; j < v.local; ++j) {
+    const int e = v.rank * v.local + j;
+    const int mask = v.helpers[e];
+    if (!mask) continue;
+    const VT* hp[kEpMaxWorld];
+    int nh = 0;
+    for (int d = 0; d < v.world; ++d)
+      if ((mask >> d) & 1)
+        hp[nh++] = reinterpret_cast<const VT*>(peer(v, d, v.dw_help) + e * v.expert_stride);
+    VT* out = reinterpret_cast<VT*>(dP + e * v.expert_stride);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      VT h[kEpMaxWorld];
+#pragma unroll
+      for (int q = 0; q < kEpMaxWorld; ++q)
+        if (q < nh) h[q] = __ldcv(hp[q] + i);
+      VT a = out[i];
+      float* af = reinterpret_cast<float*>(&a);
+#pragma unroll
+      for (int q = 0; q < kEpMaxWorld; ++q) {
+        if (q >= nh) break;
+        const float* hf = reinterpret_cast<const float*>(&h[q]);
+#pragma unroll
+        for (int c = 0; c < W4; ++c) af[c] += hf[c];
+      }
+      out[i] = a;
+    }
+  }
+}
+
 }  // namespace ep
 
 using namespace ep;
@@ -314,9 +404,20 @@ void ep_barrier(const EpView& v, int k, unsigned epoch, cudaStream_t s, int64_t&
   DOP_LAUNCHED(launches);
 }
 
-void ep_layout(const EpView& v, int E, cudaStream_t s, int64_t& launches) {
+void ep_layout(const EpView& v, cudaStream_t s, int64_t& launches) {
   tc::bind_error_word();
-  k_ep_layout<<<1, 256, 0, s>>>(v, E);
+  DOP_REQUIRE(v.E <= kMaxExperts && v.world <= kEpMaxWorld && v.E % v.world == 0,
+              "expert-parallel plan out of range");
+  k_ep_layout<<<1, 256, 0, s>>>(v);
+  DOP_LAUNCHED(launches);
+}
+
+void ep_reduce_adjoint(const EpView& v, float* dP_experts, cudaStream_t s, int64_t& launches) {
+  tc::bind_error_word();
+  const bool vec = v.expert_stride % 4 == 0 && (uintptr_t)dP_experts % 16 == 0 &&
+                   (uintptr_t)v.dw_help % 16 == 0;
+  if (vec) k_ep_reduce_adjoint<float4><<<sm_count() * 4, 256, 0, s>>>(v, dP_experts);
+  else k_ep_reduce_adjoint<float><<<sm_count() * 4, 256, 0, s>>>(v, dP_experts);
   DOP_LAUNCHED(launches);
 }
 

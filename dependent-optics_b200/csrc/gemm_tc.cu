@@ -58,6 +58,8 @@ struct Params {
   int nparts;       // K segments (A_i, B_i) summed into one accumulator
   int kb[3];        // k-blocks of each part (plain / grouped rows)
   const int* seg_off;
+  const int* seg_end;  // grouped contraction: group g runs over [seg_off[g], seg_end[g])
+                       // (null: [seg_off[g], seg_off[g + 1])); empty groups are skipped
   const int* tile_expert;
   int G;
   int m_tiles, n_tiles;  // n_tiles counts BN-wide (dual: BN/2-wide output) tiles
@@ -127,6 +129,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   // bars: full[STG], empty[STG], acc_full[2], acc_empty[2], drain
   uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STG + 5);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  // grouped contraction: the groups with a non-empty contraction, in order
+  __shared__ int s_groups[kMaxExperts];
+  __shared__ int s_ngroups;
   const uint32_t smem0 = smem_u32(smem);
   const uint32_t bar0 = smem_u32(bars);
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
@@ -148,6 +153,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     mbar_init(drain_bar, 1);
     *abort_flag = failed ? 1 : 0;
+    int ng = 0;
+    if (p.mode == 2) {
+      for (int g = 0; g < p.G && g < kMaxExperts; ++g) {
+        const int lo = p.seg_off[g], hi = p.seg_end ? p.seg_end[g] : p.seg_off[g + 1];
+        if (hi > lo) s_groups[ng++] = g;
+      }
+    }
+    s_ngroups = ng;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -173,12 +186,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   int rows_total = p.M;
   if (p.mode == 1) rows_total = p.seg_off[p.G];
   const int m_tiles = p.mode == 1 ? (rows_total + TM - 1) / TM : p.m_tiles;
-  const int groups = p.mode == 2 ? p.G : 1;
+  const int groups = p.mode == 2 ? s_ngroups : 1;
   const int total = groups * m_tiles * p.n_tiles;
+  // tile id -> tile, with the group index of a grouped contraction mapped
+  // to the non-empty groups
+  auto tile_at = [&](int t) {
+    Tile r = tile_of(t, m_tiles, p.n_tiles);
+    if (p.mode == 2) r.g = s_groups[r.g];
+    return r;
+  };
   auto k_blocks = [&](const Tile& t, int part, int& k0) -> int {
     if (p.mode == 2) {
       k0 = p.seg_off[t.g];
-      return (p.seg_off[t.g + 1] - k0) / BK;
+      return ((p.seg_end ? p.seg_end[t.g] : p.seg_off[t.g + 1]) - k0) / BK;
     }
     k0 = 0;
     return p.kb[part];
@@ -200,7 +220,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         else tma_load_3d(dst, map, full_bar(st), c0, c1, c2);
       };
       for (int t = unit; t < total && ok; t += units) {
-        const Tile tl = tile_of(t, m_tiles, p.n_tiles);
+        const Tile tl = tile_at(t);
         const int m0 = tl.m * TM + (int)rank * BM;  // this CTA's rows
         // expert of the tile (segments are kSegAlign-aligned: one expert per tile)
         const int z = p.mode == 1 ? max(p.tile_expert[tl.m * (TM / BM)], 0) : 0;
@@ -287,7 +307,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       };
       for (int t = unit; t < total && ok; t += units) {
-        const Tile tl = tile_of(t, m_tiles, p.n_tiles);
+        const Tile tl = tile_at(t);
         const bool freed = PAIR ? mbar_wait_cluster(acce_bar(a), aph ^ 1u, abort_flag, 2)
                                 : mbar_wait(acce_bar(a), aph ^ 1u, abort_flag, 2);
         if (!freed) { ok = false; break; }
@@ -336,7 +356,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // the first CTA's barrier that frees accumulator a (a pair frees it from both CTAs)
     auto acce_leader = [&](int ab) { return PAIR ? mapa_shared(acce_bar(ab), 0) : acce_bar(ab); };
     for (int t = unit; t < total && !*abort_flag; t += units) {
-      const Tile tl = tile_of(t, m_tiles, p.n_tiles);
+      const Tile tl = tile_at(t);
       if (!mbar_wait(accf_bar(a), aph, abort_flag, 4)) break;
       tc_fence_after();
       int kbase;
@@ -662,8 +682,10 @@ void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue
   p.N = (int)g.N;
   p.mode = g.group;
   p.seg_off = g.seg_off;
+  p.seg_end = g.seg_end;
   p.tile_expert = g.tile_expert;
   p.G = g.G;
+  DOP_REQUIRE(g.group != 2 || g.G <= kMaxExperts, "grouped contraction: at most kMaxExperts groups");
   if (te.kind >= 0) {
     p.epi = te.kind;
   } else if (g.epi == Epi::Store) {

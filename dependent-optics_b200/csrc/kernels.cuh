@@ -98,6 +98,9 @@ struct Gemm {
   const float* R = nullptr; int64_t ldr = 0;
   const float* bias = nullptr; uint8_t* mask = nullptr; bool relu = false;
   int group = 0; const int* seg_off = nullptr; const int* tile_expert = nullptr; int G = 0;
+  // group == 2 (grouped contraction) on the tensor cores: group g contracts
+  // over rows [seg_off[g], seg_end[g]) instead of [seg_off[g], seg_off[g + 1])
+  const int* seg_end = nullptr;
   int64_t b_gs = 0, c_gs = 0;
   // CUDA-core path: fp32 scratch (ws_cap floats) for split-contraction
   // partials; without it a narrow problem runs unsplit

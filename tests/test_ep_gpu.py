@@ -8,8 +8,11 @@ do not depend on where the row sits, so y and the shared adjoint slice are
 bit-identical and dx agrees to fp32 rounding.  The adjoint of each rank's
 own experts must equal the sum over ranks of the single-GPU adjoints (fp32
 tolerance: the two sum the same products in a different order), and the
-other experts' slices must stay untouched.  Two steps run back to back, the
-second with a router bias that sends most rows to rank 0's experts.
+other experts' slices must stay untouched.  Three steps run back to back:
+balanced routing, a router bias that sends most rows to rank 0's experts,
+and one that sends most rows to expert 0 alone.  Under the skewed steps the
+plan gives part of the hot experts' rows to rank 1, which returns their
+partial weight adjoints to rank 0; the bars are the same.
 """
 import os
 import socket
@@ -64,10 +67,13 @@ def _rank_main(rank: int, port: int) -> None:
         per = cfg.experts // WORLD
         stride = ll.expert_stride
         own = slice(ll.gate0 + rank * per * stride, ll.gate0 + (rank + 1) * per * stride)
-        for step in range(2):
-            if step == 1:
+        for step in range(3):
+            if step >= 1:
                 bias = torch.zeros(cfg.experts, device=dev)
-                bias[:per] = 3.0  # most rows go to rank 0's experts
+                if step == 1:
+                    bias[:per] = 3.0  # most rows go to rank 0's experts
+                else:
+                    bias[0] = 6.0  # one expert takes most rows: split over both ranks
                 ep_blk.set_router_bias(bias)
                 ref_blk.set_router_bias(bias)
             X = torch.randn(T, cfg.dim, generator=gx, device=dev)
