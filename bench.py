@@ -213,14 +213,12 @@ def cpu_oracle_sample(cfg_d, seq, seed, repeats=1, threads=0):
 
 def use_expert_parallel(a, wl, world) -> bool:
     """Expert parallel when the experts split over the ranks (the contract's
-    partitioning of the Mixtral block), else data parallel.  With skewed
-    routing an expert-parallel step waits for the owner of the hottest
-    expert (measured at 8 GPUs: 43% scaling efficiency against 85% for data
-    parallelism), so `auto` runs skewed workloads data-parallel."""
+    partitioning of the Mixtral block), else data parallel.  Skewed routing
+    runs expert-parallel too: the block's per-step plan splits a hot
+    expert's rows over several ranks."""
     from dop import parallel
     return (world > 1 and a.parallel != "dp"
-            and parallel.ep_mode(world, wl["cfg"]["experts"], wl["precision"] == "bf16")
-            and (a.parallel == "ep" or not wl["skew"]))
+            and parallel.ep_mode(world, wl["cfg"]["experts"], wl["precision"] == "bf16"))
 
 
 def arm_config(a, wl, world) -> dict:
@@ -831,7 +829,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--parallel", default="auto", choices=["auto", "dp", "ep"],
                     help="N > 1: expert parallel (auto when the experts split evenly over "
-                         "the ranks, bf16, balanced routing) or data parallel")
+                         "the ranks and the lens is bf16) or data parallel")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="profiler run: no CPU baseline, no e2e, warm-up may be < 3")
