@@ -65,6 +65,13 @@ WORKLOADS = {
                                                sliding_window=4096),
                                       batch=1, seq=1024, precision="bf16", skew=False,
                                       cpu_seq=16),
+    # the Mixtral-8x7B router stage's shape (d_model 4096, 8 experts, top-2,
+    # 32768 tokens) with a small expert hidden size: the profiling case of the
+    # router kernel (a few GB on the device, inputs larger than L2)
+    "router_profile": dict(cfg=dict(vocab=32000, dim=4096, layers=1, heads=32, kv_heads=8,
+                                    head_dim=128, intermediate=128, experts=8, top_k=2,
+                                    rms_eps=1e-5, rope_theta=1e6, sliding_window=4096),
+                           batch=8, seq=4096, precision="bf16", skew=False, cpu_seq=16),
     # staged 4-block stack of Mixtral-8x7B-shaped blocks: global batch 32 at seq
     # 4096 in 8 micro-batches, pipeline-staged over the GPUs (dop.cluster)
     "mixtral8x7b_stack4": dict(cfg=dict(vocab=32000, dim=4096, layers=4, heads=32, kv_heads=8,
