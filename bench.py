@@ -14,8 +14,8 @@ path): matrices ~ N(0, 0.02^2), RMSNorm weights 1, x and dy ~ N(0, 1).
 
 Prints one JSON line (rank 0).  `value` is whole-job tokens/s with inputs
 resident in HBM; `e2e` is the same metric through the public C-ABI call with
-the step's inputs copied from pinned host memory and its input cotangent read
-back every step; `roofline` is the expert gate/up grouped GEMM against the
+the step's inputs copied from pinned host memory and its whole result (y, dx
+and the fp32 parameter adjoint) read back every step; `roofline` is the expert gate/up grouped GEMM against the
 measured bf16 peak; `cpu_baseline` is the CPU oracle (a port of the crate's
 single-threaded CPU lens) on a bounded sample of the same workload.
 
@@ -92,10 +92,13 @@ DEFAULT_WORKLOAD = "mixtral8x7b_block"
 # The CPU sample of a block workload is one sequence of `cpu_seq` tokens at
 # the workload's full widths (batch 1), sized so one oracle fwd+bwd takes
 # seconds on a many-core host; it includes the attention over its positions.
-# DRAM bytes (read + write) of one expert gate/up launch per routed row,
-# from a one-pass ncu capture of the small case (batch 1, seq 1024, 2048
-# routed rows) scaled by rows; a bench run cannot read DRAM counters.
-GATE_UP_TRAFFIC_PER_ROW = (9.78e9 + 6.09e9) / 65536
+# DRAM bytes (read 10.21e9 + write 6.09e9) of one expert gate/up launch of
+# the Mixtral-8x7B block at batch 8, seq 4096: one launch (-s 4 -c 1) of
+# dram__bytes_read/write.sum, which ncu collects in one pass (checked on the
+# batch 1, seq 1024 case first); a bench run cannot read DRAM counters.  The
+# traffic does not scale with the routed rows (the weights are re-read once
+# per band of row tiles), so it is quoted for that workload only.
+GATE_UP_TRAFFIC = 10.21e9 + 6.09e9
 
 
 def flops_per_step(cfg, batch, seq):
@@ -665,11 +668,11 @@ def run_ours(a):
         blk.set_adjoint_stream(side)
     x0 = ll.gate0
 
-    def reduce_dp():
+    def reduce_dp(buf):
         if side is not None:
             with torch.cuda.stream(side):
-                parallel.reduce_adjoint(dP[x0:])
-        parallel.reduce_adjoint(dP[:x0])
+                parallel.reduce_adjoint(buf[x0:])
+        parallel.reduce_adjoint(buf[:x0])
         if side is not None:
             stream.wait_stream(side)
 
@@ -678,7 +681,7 @@ def run_ours(a):
         blk.forward(P, X, Y, stream=stream)
         blk.backward(P, DY, dP, DX, stream=stream)
         if world > 1:
-            reduce_dp()
+            reduce_dp(dP)
 
     _trace("params and inputs ready")
     for _ in range(a.warmup):
@@ -712,18 +715,22 @@ def run_ours(a):
     value = world * T / (ms / 1e3)
 
     # End to end through the public call: every step copies its x and dy from
-    # pinned host memory and reads its dx back.  The copies run on two copy
-    # streams and are double-buffered, so step i+1's inputs travel while step i
-    # computes and step i's dx returns during step i+1.
+    # pinned host memory and reads the step's whole result back: y, dx and
+    # the fp32 parameter adjoint.  The copies run on two copy streams and
+    # every device buffer is double-buffered, so step i+1's inputs travel
+    # while step i computes and step i's results return during step i+1.
     e2e = None
     if not a.no_e2e:
         hx = torch.randn(T, cfg.dim, generator=torch.Generator().manual_seed(7)).pin_memory()
         hdy = torch.randn(T, cfg.dim, generator=torch.Generator().manual_seed(8)).pin_memory()
-        hdx = torch.empty(T, cfg.dim).pin_memory()
+        hy = torch.empty(T, cfg.dim, pin_memory=True)
+        hdx = torch.empty(T, cfg.dim, pin_memory=True)
+        hdP = torch.empty(ll.total, dtype=torch.float32, pin_memory=True)
         Xb, DYb, DXb = [X, torch.empty_like(X)], [DY, torch.empty_like(DY)], [DX, torch.empty_like(DX)]
+        Yb, dPb = [Y, torch.empty_like(Y)], [dP, torch.empty_like(dP)]
         h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         ev = lambda: torch.cuda.Event()
-        in_ready, step_done, dx_out = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+        in_ready, step_done, out_done = [ev(), ev()], [ev(), ev()], [ev(), ev()]
 
         def e2e_run(n, start):
             h2d.wait_event(start)
@@ -741,19 +748,23 @@ def run_ours(a):
                         DYb[1 - b].copy_(hdy, non_blocking=True)
                         in_ready[1 - b].record(h2d)
                 stream.wait_event(in_ready[b])
-                if i >= 2:
-                    stream.wait_event(dx_out[b])
-                dP.zero_()
-                blk.forward(P, Xb[b], Y, stream=stream)
-                blk.backward(P, DYb[b], dP, DXb[b], stream=stream)
+                if i >= 2:  # step i-2's results have left this buffer set
+                    stream.wait_event(out_done[b])
+                dPb[b].zero_()
+                blk.forward(P, Xb[b], Yb[b], stream=stream)
+                blk.backward(P, DYb[b], dPb[b], DXb[b], stream=stream)
                 if world > 1:
-                    reduce_dp()
+                    reduce_dp(dPb[b])
                 step_done[b].record(stream)
                 with torch.cuda.stream(d2h):
                     d2h.wait_event(step_done[b])
+                    hy.copy_(Yb[b], non_blocking=True)
                     hdx.copy_(DXb[b], non_blocking=True)
-                    dx_out[b].record(d2h)
-            stream.wait_event(dx_out[(n - 1) % 2])
+                    hdP.copy_(dPb[b], non_blocking=True)
+                    out_done[b].record(d2h)
+            stream.wait_event(out_done[(n - 1) % 2])
+            if n >= 2:
+                stream.wait_event(out_done[(n - 2) % 2])
 
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -769,8 +780,10 @@ def run_ours(a):
         torch.cuda.synchronize(dev)
         ems = parallel.max_over_ranks(e0.elapsed_time(e1) / n_e2e, device=dev)
         e2e = {"value": world * T / (ems / 1e3), "unit": "tokens/s", "steps": n_e2e,
-               "h2d_bytes_per_step": 2 * T * cfg.dim * 4, "d2h_bytes_per_step": T * cfg.dim * 4,
-               "overlap": "double-buffered copy streams"}
+               "h2d_bytes_per_step": 2 * T * cfg.dim * 4,
+               "d2h_bytes_per_step": 2 * T * cfg.dim * 4 + ll.total * 4,
+               "result": "y, dx and the fp32 parameter adjoint read back every step",
+               "overlap": "double-buffered device buffers and copy streams"}
 
     flops = flops_per_step(wl["cfg"], batch, seq)
     hbm, peak, peak_sus, src = measured_peaks()
@@ -803,13 +816,12 @@ def run_ours(a):
             # the gate/up GEMM is timed inside a long step: sustained peak
             "roofline": {"bound": "tensor", "kernel": "expert_gate_up", "achieved": achieved,
                          "peak": peak_sus, "unit": "TFLOP/s", "frac": achieved / peak_sus,
-                         "traffic": (GATE_UP_TRAFFIC_PER_ROW * T * cfg.top_k
-                                     if wl["cfg"]["dim"] == 4096 and wl["cfg"]["experts"] == 8
-                                     else None),
-                         "traffic_source": ("dram bytes read + written per launch: one-pass ncu "
-                                            "capture of the batch 1, seq 1024 case scaled by "
-                                            "routed rows; algorithmic 8.16e9 B at batch 8, "
-                                            "seq 4096"),
+                         "traffic": (GATE_UP_TRAFFIC
+                                     if a.workload in ("mixtral8x7b_block",
+                                                       "mixtral8x7b_block_skewed") else None),
+                         "traffic_source": ("dram bytes read + written by one launch at batch 8, "
+                                            "seq 4096 (one-pass ncu capture, -c 1); algorithmic "
+                                            "8.16e9 B: rows 0.55, weights 1.88, g/u/h 5.73"),
                          "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside "
                                         "a long step)"},
             "phases_ms": phases,
