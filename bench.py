@@ -72,6 +72,13 @@ WORKLOADS = {
                                     head_dim=128, intermediate=128, experts=8, top_k=2,
                                     rms_eps=1e-5, rope_theta=1e6, sliding_window=4096),
                            batch=8, seq=4096, precision="bf16", skew=False, cpu_seq=16),
+    # the tensor-core GEMM alone on one expert's gate projection at batch 2,
+    # seq 4096 routed rows (16384 x 14336, contraction 4096): the kernel-level
+    # profiling case, timed beside cuBLAS on the same shape
+    "gemm_bf16_expert": dict(gemm=(16384, 14336, 4096, 0), precision="bf16", skew=False),
+    # the expert-input cotangent's shape: 16384 rows, N 4096, contraction
+    # 28672, B read transposed (the crate's [D, I] gate/up weights)
+    "gemm_bf16_dx": dict(gemm=(16384, 4096, 28672, 1), precision="bf16", skew=False),
     # staged 4-block stack of Mixtral-8x7B-shaped blocks: global batch 32 at seq
     # 4096 in 8 micro-batches, pipeline-staged over the GPUs (dop.cluster)
     "mixtral8x7b_stack4": dict(cfg=dict(vocab=32000, dim=4096, layers=4, heads=32, kv_heads=8,
@@ -92,13 +99,13 @@ DEFAULT_WORKLOAD = "mixtral8x7b_block"
 # The CPU sample of a block workload is one sequence of `cpu_seq` tokens at
 # the workload's full widths (batch 1), sized so one oracle fwd+bwd takes
 # seconds on a many-core host; it includes the attention over its positions.
-# DRAM bytes (read 10.21e9 + write 6.09e9) of one expert gate/up launch of
+# DRAM bytes (read 7.43e9 + write 5.80e9) of one expert gate/up launch of
 # the Mixtral-8x7B block at batch 8, seq 4096: one launch (-s 4 -c 1) of
 # dram__bytes_read/write.sum, which ncu collects in one pass (checked on the
 # batch 1, seq 1024 case first); a bench run cannot read DRAM counters.  The
 # traffic does not scale with the routed rows (the weights are re-read once
 # per band of row tiles), so it is quoted for that workload only.
-GATE_UP_TRAFFIC = 10.21e9 + 6.09e9
+GATE_UP_TRAFFIC = 7.43e9 + 5.80e9
 
 
 def flops_per_step(cfg, batch, seq):
@@ -270,6 +277,10 @@ def run_reference(a):
     cores = os.cpu_count() or 1
     if wl.get("program"):
         run_reference_program(a, wl, cores, world)
+        return
+    if wl.get("gemm"):
+        print(json.dumps({"impl": "reference", "unavailable": "a kernel-level profiling workload "
+                          "with no counterpart in the crate's CPU lens"}), flush=True)
         return
     steps = max(1, a.steps)
     seq = wl["cpu_seq"]
@@ -474,6 +485,55 @@ def run_reference_program(a, wl, cores, world):
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"{cores} workers, each 1 s of forward+backward passes"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_gemm(a):
+    """The tensor-core GEMM (dop_gemm_bf16: bf16 A [M, K], the crate's W[k * N
+    + n] layout for B, bf16 C) on one shape, K timed launches between CUDA
+    events, beside torch.matmul (cuBLAS) on the same operands."""
+    import torch
+    from dop._lib import check, lib
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    M, N, K, b_t = WORKLOADS[a.workload]["gemm"]
+    g = torch.Generator(device=dev).manual_seed(0)
+    A = torch.randn(M, K, generator=g, device=dev).bfloat16()
+    # B(k, n) = Bs[k * N + n] (b_t = 0) or Bs[n * K + k] (b_t = 1)
+    Bs = (torch.randn(N if b_t else K, K if b_t else N, generator=g, device=dev) * 0.02).bfloat16()
+    Bm = Bs.t() if b_t else Bs
+    C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+
+    def ours():
+        check(lib().dop_gemm_bf16(M, N, K, A.data_ptr(), K, 0, Bs.data_ptr(), K if b_t else N, b_t,
+                                  C.data_ptr(), N, 0, 0, stream.cuda_stream))
+
+    def timed(fn):
+        for _ in range(max(3, a.warmup)):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(a.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / a.steps
+
+    with ClockSampler(0) as clk:
+        ms = timed(ours)
+        ms_cublas = timed(lambda: torch.matmul(A, Bm, out=C))
+    flops = 2 * M * N * K
+    print(json.dumps({
+        "metric": "bf16 GEMM TFLOP/s (tensor-core kernel alone)", "value": flops / ms / 1e9,
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": a.workload, "M": M, "N": N, "K": K, "b_t": b_t},
+        "cublas_same_shape": {"ms": ms_cublas, "tflops": flops / ms_cublas / 1e9},
+        "clocks": clk.summary(),
     }), flush=True)
 
 
@@ -861,6 +921,8 @@ def main():
         run_reference(a)
     elif WORKLOADS[a.workload].get("program"):
         run_program(a)
+    elif WORKLOADS[a.workload].get("gemm"):
+        run_gemm(a)
     elif WORKLOADS[a.workload].get("stack"):
         run_stack(a)
     else:

@@ -26,6 +26,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <map>
 #include <mutex>
 #include <type_traits>
 
@@ -63,6 +64,8 @@ struct Params {
   const int* tile_expert;
   int G;
   int m_tiles, n_tiles;  // n_tiles counts BN-wide (dual: BN/2-wide output) tiles
+  int* tile_ctr;         // non-null: tiles are taken in order from this counter (zeroed
+                         // before the launch); null: CTA (pair) u takes u, u + units, ...
   int epi;
   void* C;
   int64_t ldc, c_gs;
@@ -132,6 +135,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   // grouped contraction: the groups with a non-empty contraction, in order
   __shared__ int s_groups[kMaxExperts];
   __shared__ int s_ngroups;
+  // Dynamic tile order (p.tile_ctr): the first CTA's producer takes the next
+  // tile id from the counter and publishes it in a ring in both CTAs' shared
+  // memory (tid_full); every role reads the ids in ring order and releases
+  // the slot on the first CTA's tid_empty.  Tiles in flight therefore stay
+  // consecutive in tile order however the CTAs drift, so tiles that share
+  // an operand run close together and share it in L2.
+  constexpr int TR = 4;
+  __shared__ int s_tid[TR];
+  __shared__ __align__(8) uint64_t s_tbar[2 * TR];
+  const bool dyn = p.tile_ctr != nullptr;
   const uint32_t smem0 = smem_u32(smem);
   const uint32_t bar0 = smem_u32(bars);
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
@@ -139,6 +152,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   auto accf_bar = [&](int a) { return bar0 + 8u * (2 * STG + a); };
   auto acce_bar = [&](int a) { return bar0 + 8u * (2 * STG + 2 + a); };
   const uint32_t drain_bar = bar0 + 8u * (2 * STG + 4);
+  auto tid_full = [&](int r) { return smem_u32(&s_tbar[r]); };
+  auto tid_empty = [&](int r) { return smem_u32(&s_tbar[TR + r]); };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -152,6 +167,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(acce_bar(a), PAIR ? 16 : 8);
     }
     mbar_init(drain_bar, 1);
+    for (int r = 0; r < TR; ++r) {
+      mbar_init(tid_full(r), 1);
+      // readers of a slot: the MMA thread and 8 epilogue warps of the first
+      // CTA, the producer and 8 epilogue warps of the second
+      mbar_init(tid_empty(r), PAIR ? 18 : 9);
+    }
     *abort_flag = failed ? 1 : 0;
     int ng = 0;
     if (p.mode == 2) {
@@ -195,6 +216,48 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (p.mode == 2) r.g = s_groups[r.g];
     return r;
   };
+  // Next tile id of a reader of the ring (dynamic order) or of the static
+  // walk: >= 0 a tile, -1 no more tiles, -2 a bounded wait ran out.  A
+  // whole warp (warp_wide: every lane reads, lane 0 releases the slot) or a
+  // single thread (the producer of the second CTA, the MMA thread) reads.
+  auto next_tile = [&](int& it, int& rs, uint32_t& rph, int code, bool warp_wide) -> int {
+    if (!dyn) {
+      const int t = unit + (it++) * units;
+      return t < total ? t : -1;
+    }
+    const bool got = leader ? mbar_wait(tid_full(rs), rph, abort_flag, code)
+                            : mbar_wait_cluster(tid_full(rs), rph, abort_flag, code);
+    if (warp_wide) {
+      // the same answer on every lane: the slot is released once
+      if (!__all_sync(0xffffffffu, got)) return -2;
+    } else if (!got) {
+      return -2;
+    }
+    const int t = *(volatile int*)&s_tid[rs];
+    if (warp_wide) __syncwarp();
+    if (!warp_wide || (threadIdx.x & 31) == 0) {
+      if (leader) mbar_arrive(tid_empty(rs));
+      else mbar_arrive_cluster(mapa_shared(tid_empty(rs), 0));
+    }
+    if (++rs == TR) { rs = 0; rph ^= 1u; }
+    return t;
+  };
+  // The first CTA's producer: take the next id and publish it to both CTAs.
+  auto take_tile = [&](int& rs, uint32_t& rph) -> int {
+    if (!mbar_wait(tid_empty(rs), rph ^ 1u, abort_flag, 5)) return -2;
+    int t = atomicAdd(p.tile_ctr, 1);
+    if (t >= total) t = -1;
+    s_tid[rs] = t;
+    if (PAIR) {
+      asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(mapa_shared(smem_u32(&s_tid[rs]), 1)),
+                   "r"(t)
+                   : "memory");
+      mbar_arrive_cluster(mapa_shared(tid_full(rs), 1));
+    }
+    mbar_arrive(tid_full(rs));
+    if (++rs == TR) { rs = 0; rph ^= 1u; }
+    return t;
+  };
   auto k_blocks = [&](const Tile& t, int part, int& k0) -> int {
     if (p.mode == 2) {
       k0 = p.seg_off[t.g];
@@ -219,7 +282,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (PAIR) tma_load_3d_pair(dst, map, fullb(st), c0, c1, c2);
         else tma_load_3d(dst, map, full_bar(st), c0, c1, c2);
       };
-      for (int t = unit; t < total && ok; t += units) {
+      int it = 0, rs = 0;
+      uint32_t rph = 0;
+      while (ok) {
+        const int t = (dyn && leader) ? take_tile(rs, rph) : next_tile(it, rs, rph, 6, false);
+        if (t == -2) ok = false;
+        if (t < 0 || !ok) break;
         const Tile tl = tile_at(t);
         const int m0 = tl.m * TM + (int)rank * BM;  // this CTA's rows
         // expert of the tile (segments are kSegAlign-aligned: one expert per tile)
@@ -279,6 +347,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (++s == STG) { s = 0; ph ^= 1u; }
           }
         }
+        if (!ok) break;
       }
       if (!ok && leader) {
         // drain: wait (bounded) for the copies of the stages still in flight
@@ -306,7 +375,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           mma_commit(bar);
         }
       };
-      for (int t = unit; t < total && ok; t += units) {
+      int it = 0, rs = 0;
+      uint32_t rph = 0;
+      while (ok) {
+        const int t = next_tile(it, rs, rph, 7, false);
+        if (t == -2) ok = false;
+        if (t < 0 || !ok) break;
         const Tile tl = tile_at(t);
         const bool freed = PAIR ? mbar_wait_cluster(acce_bar(a), aph ^ 1u, abort_flag, 2)
                                 : mbar_wait(acce_bar(a), aph ^ 1u, abort_flag, 2);
@@ -355,7 +429,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t aph = 0;
     // the first CTA's barrier that frees accumulator a (a pair frees it from both CTAs)
     auto acce_leader = [&](int ab) { return PAIR ? mapa_shared(acce_bar(ab), 0) : acce_bar(ab); };
-    for (int t = unit; t < total && !*abort_flag; t += units) {
+    int it = 0, rs = 0;
+    uint32_t rph = 0;
+    for (;;) {
+      if (*abort_flag) break;
+      const int t = next_tile(it, rs, rph, 8, true);
+      if (t < 0) break;
       const Tile tl = tile_at(t);
       if (!mbar_wait(accf_bar(a), aph, abort_flag, 4)) break;
       tc_fence_after();
@@ -666,6 +745,33 @@ int pair_slots() {
   return slots[dev];
 }
 
+// Tile counter of the dynamic tile order for launches on stream `s`: one int
+// per (device, stream) from a per-device pool; launches on one stream are
+// serialised, so they can share it (each zeroes it first).  Null (static
+// order) when the pool is used up, or when the stream is being captured and
+// has no counter yet (the pool is allocated outside captures).
+int* tile_counter(cudaStream_t s) {
+  constexpr int kPool = 1024;
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, int*> ctr;
+  static int* pool[16] = {nullptr};
+  static int used[16] = {0};
+  int dev = 0;
+  DOP_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 16) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = ctr.find({dev, s});
+  if (it != ctr.end()) return it->second;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  DOP_CHECK_CUDA(cudaStreamIsCapturing(s, &cap));
+  if (cap != cudaStreamCaptureStatusNone) return nullptr;
+  if (!pool[dev]) DOP_CHECK_CUDA(cudaMalloc(&pool[dev], sizeof(int) * kPool));
+  if (used[dev] == kPool) return nullptr;
+  int* c = pool[dev] + used[dev]++;
+  ctr[{dev, s}] = c;
+  return c;
+}
+
 }  // namespace tc
 
 // One tensor-core GEMM.  `parts` are (A, lda, B, ldb, K) triples summed into
@@ -754,6 +860,9 @@ void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue
   for (int i = p.nparts; i < 3; ++i) ma[i] = ma[0];
   for (int i = (dual ? 2 : p.nparts); i < 3; ++i) mb[i] = mb[0];
   const int64_t tiles = (int64_t)(g.group == 2 ? g.G : 1) * p.m_tiles * p.n_tiles;
+  // dynamic tile order: the stream's counter, zeroed before the launch
+  p.tile_ctr = tile_counter(s);
+  if (p.tile_ctr) DOP_CHECK_CUDA(cudaMemsetAsync(p.tile_ctr, 0, sizeof(int), s));
   const bool A = g.a_t, B = !g.b_t;  // MN-major flags
   if (dual && A) throw Error(-4, "SwiGLU GEMM needs a K-major A");
   auto go = [&](auto a_mn, auto b_mn, auto du, auto pr) {
