@@ -4,6 +4,7 @@
 // backward = src/mixtral.rs:434-598 (backward_layer)
 // with the crate's per-token expert loop replaced by the deterministic
 // expert permutation and grouped GEMMs over the expert-sorted rows.
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -86,6 +87,14 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
   part_cap = std::max<int64_t>((int64_t)sm_count() * 4 * D, 64 * D * E);
   part_cap = std::max<int64_t>(part_cap, 64 * std::max(qd, D));
   split_cap = prec == DOP_F32 ? std::min<int64_t>(1 << 22, 16 * D * std::max(qd, D)) : 0;
+  // fp32 lens: tf32 hi / lo operands of the largest contraction on the
+  // tensor cores (3xTF32): experts (grouped over E), their weight adjoints
+  // (contraction over every expert-sorted row), the attention projections
+  if (prec == DOP_F32) {
+    const int64_t W = std::max(D, qd);
+    tf32_cap = 2 * std::max({rows_cap * D + E * I * D, rows_cap * I + E * D * I,
+                             (I + D) * rows_cap, T * W + W * W, 2 * W * T});
+  }
 
   auto carve = [&](char* base_) {
     Carver cv;
@@ -131,6 +140,7 @@ Block::Block(const dop_mixtral_cfg& c, int64_t batch, int64_t seq, int precision
     cv.take(delta, 4 * T * c.heads, base_);
     cv.take(part, 4 * part_cap, base_);
     cv.take(split_ws, 4 * split_cap, base_);
+    cv.take(tf32_ws, 4 * tf32_cap, base_);
     cv.take(dO, a * rows_cap * D, base_);
     cv.take(dg, xe * a * rows_cap * I, base_);
     cv.take(du, xe * a * rows_cap * I, base_);
@@ -401,6 +411,28 @@ template <typename Act>
 void Block::gemm(const Gemm& g, cudaStream_t s, const GemmPart* extra, int n_extra) {
   if (std::is_same<Act, bf16>::value) {
     gemm_tc(g, extra, n_extra, TcEpilogue{}, s, launches);
+    return;
+  }
+  // fp32 contractions on the tensor cores as three tf32 products when the
+  // shape allows (fp32 C, 16-byte rows), on the CUDA cores otherwise
+  auto tf32_part = [&](const Gemm& gp) {
+    return gemm_tc_f32_ok(gp) && gemm_tc_f32_scratch(gp) <= tf32_cap;
+  };
+  bool tc = tf32_part(g);
+  for (int i = 0; i < n_extra && tc; ++i) {
+    Gemm gi = g;
+    gi.A = extra[i].A; gi.lda = extra[i].lda; gi.B = extra[i].B; gi.ldb = extra[i].ldb;
+    gi.K = extra[i].K; gi.epi = Epi::Accum;
+    tc = tf32_part(gi);
+  }
+  if (tc) {
+    gemm_tc_f32(g, tf32_ws, tf32_cap, s, launches);
+    for (int i = 0; i < n_extra; ++i) {
+      Gemm gi = g;
+      gi.A = extra[i].A; gi.lda = extra[i].lda; gi.B = extra[i].B; gi.ldb = extra[i].ldb;
+      gi.K = extra[i].K; gi.epi = Epi::Accum;
+      gemm_tc_f32(gi, tf32_ws, tf32_cap, s, launches);
+    }
     return;
   }
   Gemm gs = g;

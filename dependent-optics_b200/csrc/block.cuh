@@ -46,6 +46,8 @@ struct Block {
   int64_t part_cap;
   float* split_ws = nullptr;  // fp32 lens: split-contraction partials (gemm_simt)
   int64_t split_cap = 0;
+  float* tf32_ws = nullptr;   // fp32 lens: tf32 hi / lo operands (gemm_tc_f32)
+  int64_t tf32_cap = 0;
   void *dO, *dg, *du, *dmid_a, *dmix, *dq_a, *dk_a, *dv_a;
 
   // expert parallelism (ep_world > 1, bf16 only; ep.cu): this rank owns the

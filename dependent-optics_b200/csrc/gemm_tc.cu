@@ -64,6 +64,7 @@ struct Params {
   const int* tile_expert;
   int G;
   int m_tiles, n_tiles;  // n_tiles counts BN-wide (dual: BN/2-wide output) tiles
+  int gm;               // row tiles walked before the next column tile
   int* tile_ctr;         // non-null: tiles are taken in order from this counter (zeroed
                          // before the launch); null: CTA (pair) u takes u, u + units, ...
   int epi;
@@ -79,12 +80,11 @@ struct Params {
   int rope_seq;
 };
 
-// Tile id -> (group, m tile, n tile).  Consecutive ids walk 16 row tiles
+// Tile id -> (group, m tile, n tile).  Consecutive ids walk GM row tiles
 // before moving to the next column tile, so a wave of CTAs shares A and B
 // tiles in L2.
 struct Tile { int g, m, n; };
-__device__ __forceinline__ Tile tile_of(int t, int m_tiles, int n_tiles) {
-  constexpr int GM = 16;
+__device__ __forceinline__ Tile tile_of(int t, int m_tiles, int n_tiles, int GM) {
   Tile r;
   const int per_g = m_tiles * n_tiles;
   r.g = t / per_g;
@@ -103,7 +103,9 @@ __device__ __forceinline__ Tile tile_of(int t, int m_tiles, int n_tiles) {
 // CTA 0's MMA thread issues for both, and each CTA's epilogue drains the 128
 // accumulator rows in its own TMEM.  Per FLOP this reads a third less
 // operand data from L2 and shared memory than one CTA per 128-row tile.
-template <bool A_MN, bool B_MN, int BN, bool DUAL, bool PAIR>
+// TF: tf32 operands (fp32 bit patterns, 32 per 128-byte K-major row, both
+// operands K-major): the 3xTF32 products of the fp32 lens (gemm_tc_f32).
+template <bool A_MN, bool B_MN, int BN, bool DUAL, bool PAIR, bool TF = false>
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mA1,
               const __grid_constant__ CUtensorMap mA2, const __grid_constant__ CUtensorMap mB0,
@@ -115,7 +117,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BNL * BK * 2;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((A_MN ? 1u : 0u) << 15) |
+  static_assert(!TF || (!A_MN && !B_MN && !DUAL), "tf32 operands are K-major, no SwiGLU");
+  constexpr int BKE = TF ? 32 : BK;             // elements of a 128-byte k-block row
+  constexpr uint32_t FMT = TF ? 2u : 1u;        // operand format: BF16 1, TF32 2
+  constexpr uint32_t IDESC = (1u << 4) | (FMT << 7) | (FMT << 10) | ((A_MN ? 1u : 0u) << 15) |
                              ((B_MN ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
                              ((uint32_t)(TM >> 4) << 24);
   // An earlier wait failed (sticky error): do no work.  A CTA of a pair
@@ -212,7 +217,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   // tile id -> tile, with the group index of a grouped contraction mapped
   // to the non-empty groups
   auto tile_at = [&](int t) {
-    Tile r = tile_of(t, m_tiles, p.n_tiles);
+    Tile r = tile_of(t, m_tiles, p.n_tiles, p.gm);
     if (p.mode == 2) r.g = s_groups[r.g];
     return r;
   };
@@ -261,7 +266,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   auto k_blocks = [&](const Tile& t, int part, int& k0) -> int {
     if (p.mode == 2) {
       k0 = p.seg_off[t.g];
-      return ((p.seg_end ? p.seg_end[t.g] : p.seg_off[t.g + 1]) - k0) / BK;
+      return ((p.seg_end ? p.seg_end[t.g] : p.seg_off[t.g + 1]) - k0) / BKE;
     }
     k0 = 0;
     return p.kb[part];
@@ -301,7 +306,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, 1)) { ok = false; break; }
             const uint32_t sa = smem0 + s * STAGE_BYTES, sb = sa + A_BYTES;
             if (leader) mbar_expect_tx(full_bar(s), PAIR ? 2 * STAGE_BYTES : STAGE_BYTES);
-            const int k0 = kbase + kb * BK;
+            const int k0 = kbase + kb * BKE;
             if (!A_MN) {
               load(sa, ma, s, k0, m0, 0);
             } else {
@@ -401,8 +406,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                                        : sdesc(sa + ks * 32, 16, 1024);
               const uint64_t bd = B_MN ? sdesc(sb + ks * 2048, 8192, 1024)
                                        : sdesc(sb + ks * 32, 16, 1024);
-              if (PAIR) mma_bf16_pair(d, ad, bd, IDESC, accum);
-              else mma_bf16(d, ad, bd, IDESC, accum);
+              if (TF) {
+                if (PAIR) mma_tf32_pair(d, ad, bd, IDESC, accum);
+                else mma_tf32(d, ad, bd, IDESC, accum);
+              } else {
+                if (PAIR) mma_bf16_pair(d, ad, bd, IDESC, accum);
+                else mma_bf16(d, ad, bd, IDESC, accum);
+              }
               accum = 1;
             }
             commit_both(empty_bar(s));
@@ -682,13 +692,13 @@ CUtensorMap make_map(const void* base, int64_t inner, int64_t outer, int64_t dep
   return make_map3(base, dims, strides, box);
 }
 
-template <bool A_MN, bool B_MN, int BN, bool DUAL, bool PAIR>
+template <bool A_MN, bool B_MN, int BN, bool DUAL, bool PAIR, bool TF = false>
 void launch(const CUtensorMap* ma, const CUtensorMap* mb, const Params& p, int grid,
             cudaStream_t s) {
   constexpr int STG = PAIR ? PAIR_STAGES : STAGES;
   constexpr int BNL = PAIR ? BN / 2 : BN;
   constexpr size_t smem = (size_t)STG * (BM * BK * 2 + BNL * BK * 2) + 1024 + 256;
-  auto kern = k_gemm_tc<A_MN, B_MN, BN, DUAL, PAIR>;
+  auto kern = k_gemm_tc<A_MN, B_MN, BN, DUAL, PAIR, TF>;
   bind_error_word();
   static bool attr = false;
   if (!attr) {
@@ -717,7 +727,7 @@ void launch(const CUtensorMap* ma, const CUtensorMap* mb, const Params& p, int g
 
 // Pairs of CTAs of this kernel that can be resident at once on the current
 // device (cudaOccupancyMaxActiveClusters, clusters of two), cached.
-template <bool A_MN, bool B_MN, int BN, bool DUAL>
+template <bool A_MN, bool B_MN, int BN, bool DUAL, bool TF = false>
 int pair_slots() {
   static int slots[16] = {0};
   int dev = 0;
@@ -725,7 +735,7 @@ int pair_slots() {
   if (dev < 0 || dev >= 16) dev = 0;
   if (!slots[dev]) {
     constexpr size_t smem = (size_t)PAIR_STAGES * (BM * BK * 2 + (BN / 2) * BK * 2) + 1024 + 256;
-    auto kern = k_gemm_tc<A_MN, B_MN, BN, DUAL, true>;
+    auto kern = k_gemm_tc<A_MN, B_MN, BN, DUAL, true, TF>;
     DOP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (unsigned)sm_count(), 1, 1);
@@ -860,6 +870,11 @@ void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue
   for (int i = p.nparts; i < 3; ++i) ma[i] = ma[0];
   for (int i = (dual ? 2 : p.nparts); i < 3; ++i) mb[i] = mb[0];
   const int64_t tiles = (int64_t)(g.group == 2 ? g.G : 1) * p.m_tiles * p.n_tiles;
+  // Row tiles walked before the next column tile: 8 for long contractions
+  // (>= 8192; an operand tile there is >= 4 MB and must be reused by tiles
+  // that run close together), else 16.  Measured on the Mixtral-8x7B step:
+  // 57.6 ms of GEMMs against 59.4 (16 everywhere), 58.1 (4) and 59.0 (2).
+  p.gm = (int64_t)(n_extra + 1) * g.K >= 8192 ? 8 : 16;
   // dynamic tile order: the stream's counter, zeroed before the launch
   p.tile_ctr = tile_counter(s);
   if (p.tile_ctr) DOP_CHECK_CUDA(cudaMemsetAsync(p.tile_ctr, 0, sizeof(int), s));
@@ -891,6 +906,147 @@ void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue
     else if (!A && !B) go(F_{}, F_{}, F_{}, F_{});
     else if (A && B) go(T_{}, T_{}, F_{}, F_{});
     else go(T_{}, F_{}, F_{}, F_{});
+  }
+  DOP_LAUNCHED(launches);
+}
+
+// ------------------------------------------------------ 3xTF32 (fp32 lens)
+// The fp32 lens's contractions on the tensor cores: each fp32 operand x is
+// split into hi = x rounded to tf32 and lo = x - hi (exact in fp32), and
+// C = A_hi B_hi + A_hi B_lo + A_lo B_hi is accumulated in fp32 TMEM as the
+// three K parts of one tf32 GEMM (the dropped lo x lo term is ~2^-22 of the
+// product; the tensor core reads lo to tf32 precision, ~2^-11 of lo).  The
+// split also lays both operands out K-major, which the tf32 path requires.
+
+namespace {
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// out[z][o][i] = split(src(z, o, i)), src(z, o, i) = src[z zs + o ld + i]
+// (TR = false) or src[z zs + i ld + o] (TR = true); a 32 x 32 tile per CTA
+// of 32 x 8 threads, transposed through shared memory when TR.
+template <bool TR>
+__global__ void k_split_tf32(const float* __restrict__ src, int64_t O, int64_t Ki, int64_t ld,
+                             int64_t zs, float* __restrict__ hi, float* __restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int64_t z = blockIdx.z;
+  const int64_t o0 = (int64_t)blockIdx.y * 32, i0 = (int64_t)blockIdx.x * 32;
+  const float* sz = src + z * zs;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  if (TR) {
+    for (int r = ty; r < 32; r += 8) {  // read along o (contiguous in src)
+      const int64_t i = i0 + r, o = o0 + tx;
+      tile[r][tx] = (i < Ki && o < O) ? sz[i * ld + o] : 0.f;
+    }
+    __syncthreads();
+  }
+  for (int r = ty; r < 32; r += 8) {  // write along i
+    const int64_t o = o0 + r, i = i0 + tx;
+    if (o >= O || i >= Ki) continue;
+    const float x = TR ? tile[tx][r] : sz[o * ld + i];
+    const float h = tf32_rna(x);
+    const int64_t at = (z * O + o) * Ki + i;
+    hi[at] = h;
+    lo[at] = x - h;
+  }
+}
+
+void split_tf32(const float* src, int64_t Z, int64_t O, int64_t Ki, int64_t ld, int64_t zs, bool tr,
+                float* hi, float* lo, cudaStream_t s, int64_t& launches) {
+  const dim3 grid((unsigned)ceil_div(Ki, 32), (unsigned)ceil_div(O, 32), (unsigned)Z);
+  const dim3 block(32, 8);
+  if (tr) k_split_tf32<true><<<grid, block, 0, s>>>(src, O, Ki, ld, zs, hi, lo);
+  else k_split_tf32<false><<<grid, block, 0, s>>>(src, O, Ki, ld, zs, hi, lo);
+  DOP_LAUNCHED(launches);
+}
+
+// 3-D fp32 (tf32) tensor map with 128-byte swizzle, box {32, box_outer, 1}.
+CUtensorMap make_map3_f32(const float* base, int64_t inner, int64_t outer, int64_t depth,
+                          int64_t row_stride, int64_t depth_stride, int box_outer) {
+  DOP_REQUIRE((uintptr_t)base % 16 == 0, "TMA base must be 16-byte aligned");
+  DOP_REQUIRE(row_stride % 4 == 0 && depth_stride % 4 == 0,
+              "TMA strides must be multiples of 16 bytes (4 floats)");
+  CUtensorMap m;
+  cuuint64_t gd[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)depth};
+  cuuint64_t gs[2] = {(cuuint64_t)row_stride * 4, (cuuint64_t)depth_stride * 4};
+  cuuint32_t bx[3] = {32, (cuuint32_t)box_outer, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = tc::encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), gd,
+                               gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw Error(-2, "cuTensorMapEncodeTiled (fp32) failed (" + std::to_string((int)r) + ")");
+  return m;
+}
+}  // namespace
+
+int64_t gemm_tc_f32_scratch(const Gemm& g) {
+  const int64_t Gb = g.group == 1 ? g.G : 1;
+  return 2 * (g.M * g.K + Gb * g.N * g.K);
+}
+
+bool gemm_tc_f32_ok(const Gemm& g) {
+  return g.M >= 128 && g.N >= 64 && g.K >= 32 && g.K % 4 == 0 && g.c_f32 &&
+         (g.epi == Epi::Store || g.epi == Epi::Accum || g.epi == Epi::AddRes) && !g.relu &&
+         !g.bias && !g.mask && g.ldc % 4 == 0 && (uintptr_t)g.C % 16 == 0;
+}
+
+void gemm_tc_f32(const Gemm& g, float* ws, int64_t ws_cap, cudaStream_t s, int64_t& launches) {
+  using namespace tc;
+  constexpr int BN = 256;
+  DOP_REQUIRE(gemm_tc_f32_ok(g), "shape or epilogue outside the 3xTF32 path");
+  DOP_REQUIRE(ws && gemm_tc_f32_scratch(g) <= ws_cap, "3xTF32 scratch too small");
+  const int64_t M = g.M, N = g.N, K = g.K;
+  const int64_t Gb = g.group == 1 ? g.G : 1;
+  float* a_hi = ws;
+  float* a_lo = a_hi + M * K;
+  float* b_hi = a_lo + M * K;
+  float* b_lo = b_hi + Gb * N * K;
+  // A(m, k) = A[m lda + k] or A[k lda + m] (a_t) -> [M][K]
+  split_tf32((const float*)g.A, 1, M, K, g.lda, 0, g.a_t, a_hi, a_lo, s, launches);
+  // B(k, n) = B[k ldb + n] or B[n ldb + k] (b_t), per expert z -> [Gb][N][K]
+  split_tf32((const float*)g.B, Gb, N, K, g.ldb, Gb > 1 ? g.b_gs : 0, !g.b_t, b_hi, b_lo, s,
+             launches);
+  Params p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.mode = g.group;
+  p.seg_off = g.seg_off;
+  p.seg_end = g.seg_end;
+  p.tile_expert = g.tile_expert;
+  p.G = g.G;
+  p.epi = g.epi == Epi::Store ? kStoreF32 : (g.epi == Epi::Accum ? kAccumF32 : kAddResF32);
+  p.C = g.C;
+  p.ldc = g.ldc;
+  p.c_gs = g.c_gs;
+  p.R = g.R;
+  p.ldr = g.ldr;
+  p.n_tiles = (int)ceil_div(N, BN);
+  const bool pair = M >= 2 * BM;
+  p.m_tiles = (int)ceil_div(M, pair ? 2 * BM : BM);
+  p.nparts = 3;
+  for (int i = 0; i < 3; ++i) p.kb[i] = (int)ceil_div(K, 32);
+  p.gm = 3 * K >= 8192 ? 8 : 16;
+  const int box_n = pair ? BN / 2 : BN;
+  CUtensorMap ma[3], mb[3];
+  ma[0] = ma[1] = make_map3_f32(a_hi, K, M, 1, K, K * M, BM);
+  ma[2] = make_map3_f32(a_lo, K, M, 1, K, K * M, BM);
+  mb[0] = mb[2] = make_map3_f32(b_hi, K, N, Gb, K, N * K, box_n);
+  mb[1] = make_map3_f32(b_lo, K, N, Gb, K, N * K, box_n);
+  const int64_t tiles = (int64_t)(g.group == 2 ? g.G : 1) * p.m_tiles * p.n_tiles;
+  p.tile_ctr = tile_counter(s);
+  if (p.tile_ctr) DOP_CHECK_CUDA(cudaMemsetAsync(p.tile_ctr, 0, sizeof(int), s));
+  if (pair) {
+    const int units = pair_slots<false, false, BN, false, true>();
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, units));
+    launch<false, false, BN, false, true, true>(ma, mb, p, 2 * grid, s);
+  } else {
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, sm_count()));
+    launch<false, false, BN, false, false, true>(ma, mb, p, grid, s);
   }
   DOP_LAUNCHED(launches);
 }

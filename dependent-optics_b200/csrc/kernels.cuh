@@ -132,6 +132,13 @@ struct TcEpilogue {
 constexpr int kTcSwiGLU = 4, kTcSwiGLUBwd = 5, kTcRope = 6;
 void gemm_tc(const Gemm& g, const GemmPart* extra, int n_extra, const TcEpilogue& te,
              cudaStream_t s, int64_t& launches);
+// The fp32 lens's contraction on the tensor cores as three tf32 products
+// (3xTF32, gemm_tc.cu): g's fp32 operands are split into tf32 hi / lo parts
+// in `ws` (gemm_tc_f32_scratch(g) floats).  gemm_tc_f32_ok: shapes and
+// epilogues it takes (fp32 C; store, accumulate or residual add).
+bool gemm_tc_f32_ok(const Gemm& g);
+int64_t gemm_tc_f32_scratch(const Gemm& g);
+void gemm_tc_f32(const Gemm& g, float* ws, int64_t ws_cap, cudaStream_t s, int64_t& launches);
 // 3-D bf16 TMA descriptor, 128-byte swizzle: extents dims (dims[0]
 // contiguous), strides of dims 1 and 2 in elements, box extents.
 CUtensorMap make_map3(const void* base, const int64_t dims[3], const int64_t strides[2],

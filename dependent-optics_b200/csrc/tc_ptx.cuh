@@ -376,6 +376,24 @@ __device__ __forceinline__ void mma_bf16_pair(uint32_t d, uint64_t a, uint64_t b
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc));
 }
+// The same MMAs on tf32 operands (32-bit elements in shared memory, K = 8
+// per instruction: 32 bytes of a K-major row, as K = 16 of bf16).
+__device__ __forceinline__ void mma_tf32(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                              uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
 // Arrive once on `bar` (shared::cluster address, either CTA of the pair)
 // when the pair MMAs issued so far have completed.
 __device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
