@@ -64,8 +64,17 @@ def test_gqa_tensor_core_matches_float64(cuda, B, S, H, KV, W, qs):
     assert rel(dv, dv_r) < 2e-2
 
 
-def test_gqa_f32_cuda_core_matches_float64(cuda):
-    B, S, H, KV, hd, W = 2, 70, 4, 2, 64, 33
+@pytest.mark.parametrize("B,S,H,KV,hd,W", [(2, 70, 4, 2, 64, 33), (1, 200, 6, 2, 128, 150),
+                                             (2, 130, 8, 1, 16, 1000), (1, 96, 2, 2, 38, 50),
+                                             (3, 64, 12, 3, 64, 64), (1, 300, 10, 1, 64, 200)],
+                         ids=["gqa2-hd64", "gqa3-hd128", "mqa8-hd16", "mha-hd38", "gqa4-one-tile",
+                              "mqa10-hd64"])
+def test_gqa_f32_cuda_core_matches_float64(cuda, B, S, H, KV, hd, W):
+    """fp32 CUDA-core attention: padded head dims 32 / 64 / 128, a head_dim
+    that is not a multiple of 4 (scalar loads), dK/dV clusters of 1, 2, 3, 4,
+    5 and 8 CTAs (10 query heads on one KV head: 5 CTAs of 2 heads each),
+    ragged last tiles.  Bar 1e-5 against float64; the backward is bitwise
+    reproducible."""
     g = torch.Generator(device="cuda").manual_seed(1)
     q = torch.randn(B * S, H, hd, generator=g, device="cuda")
     k = torch.randn(B * S, KV, hd, generator=g, device="cuda")
@@ -74,13 +83,20 @@ def test_gqa_f32_cuda_core_matches_float64(cuda):
     o, lse = torch.empty_like(q), torch.empty(B, H, S, device="cuda")
     check(lib().dop_gqa_forward(B, S, H, KV, hd, W, DOP_F32, q.data_ptr(), k.data_ptr(),
                                 v.data_ptr(), o.data_ptr(), lse.data_ptr(), None))
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    delta = torch.empty(B * H * S, device="cuda")
-    check(lib().dop_gqa_backward(B, S, H, KV, hd, W, DOP_F32, q.data_ptr(), k.data_ptr(),
-                                 v.data_ptr(), o.data_ptr(), dout.data_ptr(), lse.data_ptr(),
-                                 delta.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
-                                 None))
+    outs = []
+    for _ in range(2):
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        delta = torch.empty(B * H * S, device="cuda")
+        check(lib().dop_gqa_backward(B, S, H, KV, hd, W, DOP_F32, q.data_ptr(), k.data_ptr(),
+                                     v.data_ptr(), o.data_ptr(), dout.data_ptr(), lse.data_ptr(),
+                                     delta.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                     dv.data_ptr(), None))
+        outs.append((dq, dk, dv))
     torch.cuda.synchronize()
     o_r, lse_r, dq_r, dk_r, dv_r = reference(q, k, v, dout, B, S, H, KV, hd, W)
+    dq, dk, dv = outs[0]
     for a, b in ((o, o_r), (dq, dq_r), (dk, dk_r), (dv, dv_r)):
         assert rel(a, b) < 1e-5
+    assert (lse.double() - lse_r).abs().max().item() < 1e-5
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a, b)
