@@ -78,6 +78,9 @@ struct Params {
   int64_t ldg;
   const float *rope_cos, *rope_sin;  // [seq][64] tables of kRopeBF16
   int rope_seq;
+  // mode 2 with kchunk > 0: split contraction of a plain product, group g
+  // contracting over [g kchunk, min(ktot, (g + 1) kchunk)) into C + g c_gs
+  int kchunk, ktot;
 };
 
 // Tile id -> (group, m tile, n tile).  Consecutive ids walk GM row tiles
@@ -182,7 +185,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     int ng = 0;
     if (p.mode == 2) {
       for (int g = 0; g < p.G && g < kMaxExperts; ++g) {
-        const int lo = p.seg_off[g], hi = p.seg_end ? p.seg_end[g] : p.seg_off[g + 1];
+        const int lo = p.kchunk ? g * p.kchunk : p.seg_off[g];
+        const int hi = p.kchunk ? min(p.ktot, lo + p.kchunk)
+                                : (p.seg_end ? p.seg_end[g] : p.seg_off[g + 1]);
         if (hi > lo) s_groups[ng++] = g;
       }
     }
@@ -264,6 +269,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     return t;
   };
   auto k_blocks = [&](const Tile& t, int part, int& k0) -> int {
+    if (p.mode == 2 && p.kchunk) {
+      k0 = t.g * p.kchunk;
+      return (min(p.ktot, k0 + p.kchunk) - k0 + BKE - 1) / BKE;
+    }
     if (p.mode == 2) {
       k0 = p.seg_off[t.g];
       return ((p.seg_end ? p.seg_end[t.g] : p.seg_off[t.g + 1]) - k0) / BKE;
@@ -963,6 +972,43 @@ void split_tf32(const float* src, int64_t Z, int64_t O, int64_t Ki, int64_t ld, 
   DOP_LAUNCHED(launches);
 }
 
+// C (epi) = sum over s < S of part[s] (M x N, row-major), summed in s order:
+// the split contraction's partial products.  VEC: 4 columns a thread.
+template <bool VEC>
+__global__ void k_sum_chunks_f32(const float* __restrict__ part, int S, int64_t M, int64_t N,
+                                 float* __restrict__ C, int64_t ldc, int epi,
+                                 const float* __restrict__ R, int64_t ldr) {
+  constexpr int W = VEC ? 4 : 1;
+  const int64_t cols = N / W, total = M * cols, MN = M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / cols, n = (i % cols) * W;
+    float v[W];
+#pragma unroll
+    for (int e = 0; e < W; ++e) v[e] = 0.f;
+    for (int c = 0; c < S; ++c) {
+      const float* src = part + c * MN + m * N + n;
+      if constexpr (VEC) {
+        const float4 x = *(const float4*)src;
+        v[0] += x.x;
+        v[1] += x.y;
+        v[2] += x.z;
+        v[3] += x.w;
+      } else {
+        v[0] += src[0];
+      }
+    }
+    float* out = C + m * ldc + n;
+    const float* r = R ? R + m * ldr + n : nullptr;
+#pragma unroll
+    for (int e = 0; e < W; ++e) {
+      if (epi == tc::kAccumF32) out[e] += v[e];
+      else if (epi == tc::kAddResF32) out[e] = v[e] + r[e];
+      else out[e] = v[e];
+    }
+  }
+}
+
 // 3-D fp32 (tf32) tensor map with 128-byte swizzle, box {32, box_outer, 1}.
 CUtensorMap make_map3_f32(const float* base, int64_t inner, int64_t outer, int64_t depth,
                           int64_t row_stride, int64_t depth_stride, int box_outer) {
@@ -1031,13 +1077,41 @@ void gemm_tc_f32(const Gemm& g, float* ws, int64_t ws_cap, cudaStream_t s, int64
   p.nparts = 3;
   for (int i = 0; i < 3; ++i) p.kb[i] = (int)ceil_div(K, 32);
   p.gm = 3 * K >= 8192 ? 8 : 16;
+  // A plain product with too few output tiles to fill the GPU splits its
+  // contraction: chunk g of S (a multiple of 4 k-blocks) runs as group g of
+  // a grouped contraction into partials after the operands in `ws`, summed
+  // in chunk order by k_sum_chunks_f32 (deterministic).
+  int S = 1;
+  float* part = b_lo + Gb * N * K;
+  if (g.group == 0) {
+    const int64_t tiles0 = (int64_t)p.m_tiles * p.n_tiles;
+    const int64_t units = pair ? pair_slots<false, false, BN, false, true>() : sm_count();
+    const int64_t kb = ceil_div(K, 32);
+    const int64_t room = (ws_cap - gemm_tc_f32_scratch(g)) / (M * N);
+    const int64_t want = std::min<int64_t>({units / std::max<int64_t>(tiles0, 1), kb / 4,
+                                            (int64_t)kMaxExperts, room});
+    if (want >= 2) S = (int)want;
+  }
+  if (S > 1) {
+    const int64_t kb = ceil_div(K, 32);
+    p.mode = 2;
+    p.G = S;
+    p.kchunk = (int)(ceil_div(kb, S) * 32);
+    p.ktot = (int)K;
+    S = (int)ceil_div(K, p.kchunk);  // every chunk non-empty
+    p.G = S;
+    p.C = part;
+    p.ldc = N;
+    p.c_gs = M * N;
+    p.epi = kStoreF32;
+  }
   const int box_n = pair ? BN / 2 : BN;
   CUtensorMap ma[3], mb[3];
   ma[0] = ma[1] = make_map3_f32(a_hi, K, M, 1, K, K * M, BM);
   ma[2] = make_map3_f32(a_lo, K, M, 1, K, K * M, BM);
   mb[0] = mb[2] = make_map3_f32(b_hi, K, N, Gb, K, N * K, box_n);
   mb[1] = make_map3_f32(b_lo, K, N, Gb, K, N * K, box_n);
-  const int64_t tiles = (int64_t)(g.group == 2 ? g.G : 1) * p.m_tiles * p.n_tiles;
+  const int64_t tiles = (int64_t)(p.mode == 2 ? p.G : 1) * p.m_tiles * p.n_tiles;
   p.tile_ctr = tile_counter(s);
   if (p.tile_ctr) DOP_CHECK_CUDA(cudaMemsetAsync(p.tile_ctr, 0, sizeof(int), s));
   if (pair) {
@@ -1049,6 +1123,18 @@ void gemm_tc_f32(const Gemm& g, float* ws, int64_t ws_cap, cudaStream_t s, int64
     launch<false, false, BN, false, false, true>(ma, mb, p, grid, s);
   }
   DOP_LAUNCHED(launches);
+  if (S > 1) {
+    const int epi = g.epi == Epi::Store ? kStoreF32 : (g.epi == Epi::Accum ? kAccumF32 : kAddResF32);
+    const bool vec = N % 4 == 0 && g.ldc % 4 == 0 && (uintptr_t)g.C % 16 == 0 &&
+                     (g.epi != Epi::AddRes || (g.ldr % 4 == 0 && (uintptr_t)g.R % 16 == 0));
+    const int64_t items = M * N / (vec ? 4 : 1);
+    const int grid = (int)std::min<int64_t>(ceil_div(items, 256), 8 * sm_count());
+    if (vec)
+      k_sum_chunks_f32<true><<<grid, 256, 0, s>>>(part, S, M, N, (float*)g.C, g.ldc, epi, g.R, g.ldr);
+    else
+      k_sum_chunks_f32<false><<<grid, 256, 0, s>>>(part, S, M, N, (float*)g.C, g.ldc, epi, g.R, g.ldr);
+    DOP_LAUNCHED(launches);
+  }
 }
 
 int* tc_error_word() {
