@@ -58,6 +58,10 @@ __device__ __forceinline__ void st_tile_row32(uint8_t* tile, int r, int c0, cons
 // units), so O is rescaled in TMEM rarely.  The tensor core alternates
 // between the tiles: PV_A, S_A(next) run while B's softmax works and back.
 constexpr float kRescale = 8.0f;
+// kPolyPairs of every 16 exponential pairs of the forward softmax (spread
+// evenly) are evaluated by exp2_poly2 on the FMA pipe instead of the MUFU.
+constexpr int kPolyPairs = 4;
+__device__ __forceinline__ constexpr bool poly_pair(int i) { return (i * kPolyPairs) % 16 < kPolyPairs; }
 
 __global__ void __launch_bounds__(320, 1)
     k_attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
@@ -288,7 +292,10 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float2 x = ffma2(make_float2(sv[qq * 32 + 2 * i], sv[qq * 32 + 2 * i + 1]), sl2v, nmv);
-          const float2 e = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          // kPolyPairs of the 16 pairs on the FMA pipe, the rest on the MUFU
+          const float2 e = poly_pair(i)
+                               ? exp2_poly2(x)
+                               : make_float2(fast_exp2(x.x), fast_exp2(x.y));
           acc[i & 3] = fadd2(acc[i & 3], e);
           pk[i] = pack_bf16(e.x, e.y);
         }
@@ -344,36 +351,12 @@ __global__ void __launch_bounds__(320, 1)
 constexpr size_t kFwdSmem = 6 * TILE + 1024 + 256;  // Q x2, K x2, V x2
 
 // ------------------------------------------------------------------ backward
-// delta[b, h, i] = sum_d dO[i, d] O[i, d]  (= sum_j P_ij dA_ij of gqa_backward)
-__global__ void k_attn_delta_bf16(const bf16* __restrict__ o, const bf16* __restrict__ dout,
-                                  int64_t rows, int H, int S, float* __restrict__ delta) {
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;  // rows = T * H, row = t * H + h
-  const uint2 a = reinterpret_cast<const uint2*>(o + row * HD)[lane];
-  const uint2 g = reinterpret_cast<const uint2*>(dout + row * HD)[lane];
-  const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-  const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
-  float sacc = 0.f;
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    float2 x = __bfloat1622float2(a2[i]), y = __bfloat1622float2(g2[i]);
-    sacc += x.x * y.x + x.y * y.y;
-  }
-  sacc = warp_sum(sacc);
-  if (lane == 0) {
-    const int64_t t = row / H;
-    const int h = (int)(row % H);
-    const int64_t b = t / S, i = t % S;
-    delta[(b * H + h) * S + i] = sacc;
-  }
-}
-
 struct BwdParams {
   int S, H, KV, group, window, n_tiles;
   float sl2, scale;
   const float* lse;
   const float* delta;
+  float* delta_out;  // written by the dQ kernel
   float* dq;
   float* dk;
   float* dv;
@@ -426,30 +409,39 @@ constexpr uint32_t QHALF = 8192;     // [64 rows][64 cols] bf16 box
 constexpr uint32_t QTILE = 2 * QHALF;
 constexpr int BSTAGES = 4;
 
-// dQ: one CTA per (128-query tile, head, sequence), 64-key tiles.
+// dQ: one CTA per (128-query tile, head, sequence), 64-key tiles, 448
+// threads: warp 0 TMA, warp 1 MMA, warps 2-13 three elementwise groups of
+// four warps taking key tiles in turn (tile j to group j mod 3).
 // TMEM: dQ 0-127; group g: S_g 128+128g (dS_g packed in its first 32
-// columns), dP_g 192+128g.  Per key tile j (group j & 1):
-// S = Q K_j^T, dP = dO V_j^T, dS = P (dP - delta) scale, dQ += dS K_j.
-__global__ void __launch_bounds__(320, 1)
+// columns), dP_g 192+128g.  Per key tile j: S = Q K_j^T, dP = dO V_j^T,
+// dS = P (dP - delta) scale, dQ += dS K_j.  The MMA thread issues dQ_j after
+// S_{j+2} and dP_{j+2}, so a group has two tiles of tensor-core work to turn
+// S_j into dS_j.  The prologue also computes delta = rowsum(dO o O) from the
+// dO and O tiles in shared memory (O loaded with Q and dO) and writes it for
+// the dK/dV kernel, which runs next.
+constexpr int DQ_GROUPS = 3;
+constexpr int DQ_THREADS = 64 + DQ_GROUPS * 128;
+__global__ void __launch_bounds__(DQ_THREADS, 1)
     k_attn_dq_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                  const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
-                 const BwdParams p) {
+                 const __grid_constant__ CUtensorMap mo, const BwdParams p) {
   if (tc_failed()) return;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sQ = smem;
   uint8_t* sDO = smem + TILE;
-  uint8_t* sK = smem + 2 * TILE;              // BSTAGES x [64 keys][128 d]
+  uint8_t* sO = smem + 2 * TILE;
+  uint8_t* sK = smem + 3 * TILE;              // BSTAGES x [64 keys][128 d]
   uint8_t* sV = sK + BSTAGES * QTILE;
   uint64_t* bars = (uint64_t*)(sV + BSTAGES * QTILE);
-  uint32_t* tmem_slot = (uint32_t*)(bars + 16);
+  uint32_t* tmem_slot = (uint32_t*)(bars + 24);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   const uint32_t b0 = smem_u32(bars);
   const uint32_t q_full = b0, dq_done = b0 + 8, drain = b0 + 16;
   auto kv_full = [&](int st) { return b0 + 24 + 8u * st; };
   auto kv_empty = [&](int st) { return b0 + 56 + 8u * st; };
   auto sd_full = [&](int g) { return b0 + 88 + 8u * g; };
-  auto ds_full = [&](int g) { return b0 + 104 + 8u * g; };
+  auto ds_full = [&](int g) { return b0 + 112 + 8u * g; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = p.n_tiles - 1 - (int)blockIdx.x;
@@ -468,7 +460,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(kv_full(st), 1);
       mbar_init(kv_empty(st), 1);
     }
-    for (int g = 0; g < 2; ++g) {
+    for (int g = 0; g < DQ_GROUPS; ++g) {
       mbar_init(sd_full(g), 1);
       mbar_init(ds_full(g), 4);
     }
@@ -483,12 +475,14 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t qs = smem_u32(sQ), dos = smem_u32(sDO);
-      mbar_expect_tx(q_full, 2 * TILE);
+      const uint32_t qs = smem_u32(sQ), dos = smem_u32(sDO), os = smem_u32(sO);
+      mbar_expect_tx(q_full, 3 * TILE);
       tma_load_3d(qs, &mq, q_full, 0, h, row0 + q0);
       tma_load_3d(qs + HALF, &mq, q_full, 64, h, row0 + q0);
       tma_load_3d(dos, &mdo, q_full, 0, h, row0 + q0);
       tma_load_3d(dos + HALF, &mdo, q_full, 64, h, row0 + q0);
+      tma_load_3d(os, &mo, q_full, 0, h, row0 + q0);
+      tma_load_3d(os + HALF, &mo, q_full, 64, h, row0 + q0);
       int issued = 0;
       bool ok = true;
       for (int j = 0; j < nt; ++j) {
@@ -515,11 +509,11 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t ID_DQ = idesc_bf16(128, 128, false, true);   // dS K (K N-major)
       const uint32_t qs = smem_u32(sQ), dos = smem_u32(sDO);
       bool ok = mbar_wait(q_full, 0, abort_flag, 22);
-      // dQ += dS_i K_i (dS from TMEM); it precedes S of tile i+2, which
-      // overwrites dS_i's columns
+      // dQ += dS_i K_i (dS from TMEM); it precedes S of tile i + 3, which
+      // overwrites dS_i's columns (one thread's MMAs run in order)
       auto issue_dq = [&](int i) -> bool {
-        const int gi = i & 1;
-        if (!mbar_wait(ds_full(gi), (i >> 1) & 1, abort_flag, 23)) return false;
+        const int gi = i % DQ_GROUPS;
+        if (!mbar_wait(ds_full(gi), (i / DQ_GROUPS) & 1, abort_flag, 23)) return false;
         tc_fence_after();
         const uint32_t ks = smem_u32(sK + (i % BSTAGES) * QTILE);
 #pragma unroll
@@ -530,7 +524,7 @@ __global__ void __launch_bounds__(320, 1)
         return true;
       };
       for (int j = 0; j < nt && ok; ++j) {
-        const int g = j & 1, st = j % BSTAGES;
+        const int g = j % DQ_GROUPS, st = j % BSTAGES;
         if (!mbar_wait(kv_full(st), (j / BSTAGES) & 1, abort_flag, 24)) { ok = false; break; }
         tc_fence_after();
         const uint32_t ks = smem_u32(sK + st * QTILE), vs = smem_u32(sV + st * QTILE);
@@ -542,9 +536,11 @@ __global__ void __launch_bounds__(320, 1)
           mma_bf16(tmem + 192 + g * 128, kmajor_desc(dos + oa), kmajor_desc(vs + ob), ID_SD, k > 0);
         }
         mma_commit(sd_full(g));
-        if (j >= 1 && !issue_dq(j - 1)) { ok = false; break; }
+        if (j >= 2 && !issue_dq(j - 2)) { ok = false; break; }
       }
-      if (ok && issue_dq(nt - 1)) mma_commit(dq_done);
+      for (int i = std::max(0, nt - 2); i < nt && ok; ++i)
+        if (!issue_dq(i)) ok = false;
+      if (ok) mma_commit(dq_done);
       mma_commit(drain);
       mbar_wait_drain(drain, 0);
     }
@@ -558,14 +554,35 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t td = tmem + 192 + g * 128 + lane_off;  // dP_g
     const bool row_ok = qi < p.S;
     const float lse2 = row_ok ? p.lse[((int64_t)b * p.H + h) * p.S + qi] * kLog2e : 0.f;
-    const float dlt = row_ok ? p.delta[((int64_t)b * p.H + h) * p.S + qi] : 0.f;
+    bool ok = mbar_wait(q_full, 0, abort_flag, 25);
+    // delta = sum_d dO[r, d] O[r, d] (= sum_j P_rj dA_rj of gqa_backward),
+    // columns in order; both tiles are 128B-swizzled alike (16-byte chunk c
+    // of row r at chunk c ^ (r & 7)), so the lanes of a phase read distinct
+    // banks.
+    float dlt = 0.f;
+    if (ok) {
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint32_t off = (c >> 3) * HALF + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+        const uint4 ov = *reinterpret_cast<const uint4*>(sO + off);
+        const uint4 gv = *reinterpret_cast<const uint4*>(sDO + off);
+        const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
+        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float2 x = __bfloat1622float2(o2[u]), y = __bfloat1622float2(g2[u]);
+          dlt += x.x * y.x;
+          dlt += x.y * y.y;
+        }
+      }
+      if (g == 0 && row_ok) p.delta_out[((int64_t)b * p.H + h) * p.S + qi] = dlt;
+    }
     // P = 2^(s sl2 - lse2), dS = P (dP scale - delta scale), as paired FMAs
     const float2 sl2v = make_float2(p.sl2, p.sl2), scv = make_float2(p.scale, p.scale);
     const float2 nl2 = make_float2(-lse2, -lse2);
     const float2 nd2 = make_float2(-dlt * p.scale, -dlt * p.scale);
-    bool ok = true;
     int cnt = 0;
-    for (int j = g; j < nt; j += 2, ++cnt) {
+    for (int j = g; j < nt && ok; j += DQ_GROUPS, ++cnt) {
       if (!mbar_wait(sd_full(g), cnt & 1, abort_flag, 26)) { ok = false; break; }
       tc_fence_after();
       const int k0 = (lo + j) * QB;
@@ -628,7 +645,8 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-constexpr size_t kDqSmem = 2 * TILE + 2 * BSTAGES * QTILE + 1024 + 256;
+constexpr size_t kDqSmem = 3 * TILE + 2 * BSTAGES * QTILE + 1024 + 256;
+static_assert(kDqSmem <= 232448, "dQ kernel shared memory above the per-CTA limit");
 
 // dK, dV: one CTA per (128-key tile, kv head, sequence), looping over the
 // query heads of the group and the 64-query tiles that see the keys (tile i
@@ -770,18 +788,33 @@ __global__ void __launch_bounds__(320, 1)
     const float2 sl2v = make_float2(p.sl2, p.sl2), scv = make_float2(p.scale, p.scale);
     bool ok = true;
     int cnt = 0;
+    // -lse2 and -delta scale of the 64 queries of pair i (lane: queries lane
+    // and lane + 32), fetched one group tile ahead so that the global load
+    // latency overlaps the previous tile's work
+    float nl_pre[2], nd_pre[2];
+    auto fetch = [&](int i) {
+      const int hf = kvh * p.group + i / nq;
+      const int qf = (qt0 + i % nq) * QB;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int qi = qf + lane + 32 * u;
+        const bool in = qi < p.S;
+        const int64_t at = ((int64_t)b * p.H + hf) * p.S + qi;
+        nl_pre[u] = in ? -p.lse[at] * kLog2e : 0.f;
+        nd_pre[u] = in ? -p.delta[at] * p.scale : 0.f;
+      }
+    };
+    if (g < total) fetch(g);
     for (int i = g; i < total; i += 2, ++cnt) {
-      const int h = kvh * p.group + i / nq;
       const int qq0 = (qt0 + i % nq) * QB;
       __syncwarp();
-      for (int e = lane; e < QB; e += 32) {
-        const int qi = qq0 + e;
-        const bool in = qi < p.S;
-        const int64_t at = ((int64_t)b * p.H + h) * p.S + qi;
-        ld[e] = in ? -p.lse[at] * kLog2e : 0.f;           // -lse2
-        ld[QB + e] = in ? -p.delta[at] * p.scale : 0.f;    // -delta scale
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        ld[lane + 32 * u] = nl_pre[u];       // -lse2
+        ld[QB + lane + 32 * u] = nd_pre[u];  // -delta scale
       }
       __syncwarp();
+      if (i + 2 < total) fetch(i + 2);
       if (!mbar_wait(sd_full(g), cnt & 1, abort_flag, 36)) { ok = false; break; }
       tc_fence_after();
       // every (key, query) pair of the 128 x 64 tile is visible: no masks
@@ -867,6 +900,24 @@ __global__ void __launch_bounds__(320, 1)
 constexpr size_t kDkdvSmem = 2 * TILE + 2 * BSTAGES * QTILE + 8 * 128 * 4 + 1024 + 256;
 
 
+// y = exp2_poly2(x) elementwise: the softmax's FMA-pipe exponential, for
+// checking its error bound against exp2.
+__global__ void k_exp2_poly(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+  for (int64_t i = 2 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x); i < n;
+       i += 2 * (int64_t)gridDim.x * blockDim.x) {
+    const float2 r = exp2_poly2(make_float2(x[i], i + 1 < n ? x[i + 1] : 0.f));
+    y[i] = r.x;
+    if (i + 1 < n) y[i + 1] = r.y;
+  }
+}
+
+void exp2_poly(const float* x, float* y, int64_t n, cudaStream_t s, int64_t& launches) {
+  if (n <= 0) return;
+  const int grid = (int)std::min<int64_t>(ceil_div(ceil_div(n, 2), 256), 1024);
+  k_exp2_poly<<<grid, 256, 0, s>>>(x, y, n);
+  DOP_LAUNCHED(launches);
+}
+
 }  // namespace tc
 
 static void check_tc(const Attn& a) {
@@ -912,9 +963,6 @@ void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, con
   check_tc(a);
   bind_error_word();
   const int64_t T = a.B * a.S;
-  const int64_t rows = T * a.H;
-  k_attn_delta_bf16<<<(unsigned)ceil_div(rows, 8), 256, 0, s>>>(o, dout, rows, a.H, (int)a.S, delta);
-  DOP_LAUNCHED(launches);
   const int64_t dq_[3] = {HD, a.H, T}, sq[2] = {HD, (int64_t)a.H * HD};
   const int64_t dk_[3] = {HD, a.KV, T}, sk[2] = {HD, (int64_t)a.KV * HD};
   const int box128[3] = {64, 1, AT}, box64[3] = {64, 1, QB};
@@ -923,7 +971,7 @@ void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, con
   p.window = (int)std::min<int64_t>(a.window, a.S + 1);
   p.sl2 = a.scale * kLog2e;
   p.scale = a.scale;
-  p.lse = lse; p.delta = delta; p.dq = dq; p.dk = dk; p.dv = dv;
+  p.lse = lse; p.delta = delta; p.delta_out = delta; p.dq = dq; p.dk = dk; p.dv = dv;
   if (out16) {
     DOP_REQUIRE(out16->dq && out16->dk && out16->dv, "bf16 gradient outputs need dq, dk and dv");
     DOP_REQUIRE(!out16->cs || out16->sn, "RoPE adjoint needs both tables");
@@ -933,6 +981,7 @@ void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, con
   }
   {
     CUtensorMap mq = make_map3(q, dq_, sq, box128), mdo = make_map3(dout, dq_, sq, box128);
+    CUtensorMap mo = make_map3(o, dq_, sq, box128);
     CUtensorMap mk = make_map3(k, dk_, sk, box64), mv = make_map3(v, dk_, sk, box64);
     p.n_tiles = (int)ceil_div(a.S, AT);
     static bool attr = false;
@@ -942,7 +991,7 @@ void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, con
       attr = true;
     }
     dim3 grid((unsigned)p.n_tiles, (unsigned)a.H, (unsigned)a.B);
-    k_attn_dq_tc<<<grid, 320, kDqSmem, s>>>(mq, mk, mv, mdo, p);
+    k_attn_dq_tc<<<grid, DQ_THREADS, kDqSmem, s>>>(mq, mk, mv, mdo, mo, p);
     DOP_LAUNCHED(launches);
   }
   {

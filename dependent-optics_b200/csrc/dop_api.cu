@@ -663,6 +663,14 @@ int dop_f32_to_bf16(const float* src, uint16_t* dst, int64_t n, void* s) {
   });
 }
 
+int dop_exp2_poly(const float* x, float* y, int64_t n, void* s) {
+  return guarded([&] {
+    DOP_REQUIRE(x && y && n >= 0, "bad exp2 arguments");
+    int64_t l = 0;
+    dop::tc::exp2_poly(x, y, n, as_stream(s), l);
+  });
+}
+
 int dop_sgd_step(float* params, const float* grad, int64_t n, float lr, void* s) {
   return guarded([&] {
     DOP_REQUIRE(params && grad && n >= 0, "bad sgd arguments");

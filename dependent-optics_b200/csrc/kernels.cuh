@@ -172,6 +172,11 @@ struct AttnBwdBf16 {
 void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, const bf16* o,
                  const bf16* dout, const float* lse, float* delta, float* dq, float* dk, float* dv,
                  cudaStream_t s, int64_t& launches, const AttnBwdBf16* out16 = nullptr);
+// y = 2^x by the polynomial the tensor-core softmax evaluates on the FMA
+// pipe for part of its exponentials (attn_tc.cu); x < 128.
+namespace tc {
+void exp2_poly(const float* x, float* y, int64_t n, cudaStream_t s, int64_t& launches);
+}
 template <typename T>
 void attn_bwd_simt(const Attn& a, const T* q, const T* k, const T* v, const T* o, const T* dout,
                    const float* lse, float* delta, float* dq, float* dk, float* dv,

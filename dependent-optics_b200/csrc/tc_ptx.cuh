@@ -284,6 +284,35 @@ __device__ __forceinline__ float fast_exp2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 2^x for a pair on the FMA and integer pipes, for the share of a softmax's
+// exponentials taken off the MUFU unit (whose ex2 rate is a quarter of the
+// FMA rate and is the tensor core's equal at head_dim 128).  Range reduction
+// after Cody and Waite (Software Manual for the Elementary Functions, 1980):
+// x = n + f with n = rint(x) (the 1.5 * 2^23 rounding constant) and f in
+// [-1/2, 1/2]; 2^f by a degree-3 polynomial whose coefficients are this
+// file's own relative-error minimax fit on [-1/2, 1/2] (Lawson's iteratively
+// reweighted least squares, csrc/exp2_poly_fit.py), max relative error
+// 7.6e-5; 2^n enters as n added to the exponent field.  Domain x < 128
+// (the softmax's x never exceeds +8); x is clamped below at -126, where the
+// result is ~1e-38 and ex2.approx.ftz gives 0 (both vanish in a bf16
+// probability and in a row sum).
+constexpr float kExp2C3 = 0.05516975373029709f;
+constexpr float kExp2C2 = 0.24260854721069336f;
+constexpr float kExp2C1 = 0.6932610869407654f;
+constexpr float kExp2C0 = 0.9999282360076904f;
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  const float2 xc = make_float2(fmaxf(x.x, -126.0f), fmaxf(x.y, -126.0f));
+  const float2 t = fadd2(xc, make_float2(kRound, kRound));         // low bits: rint(xc)
+  const float2 n = fadd2(t, make_float2(-kRound, -kRound));        // rint(xc) as float
+  const float2 f = fadd2(xc, make_float2(-n.x, -n.y));             // in [-1/2, 1/2]
+  float2 p = ffma2(make_float2(kExp2C3, kExp2C3), f, make_float2(kExp2C2, kExp2C2));
+  p = ffma2(p, f, make_float2(kExp2C1, kExp2C1));
+  p = ffma2(p, f, make_float2(kExp2C0, kExp2C0));
+  // (bits(t) << 23) mod 2^32 = n << 23: the rounding constant's bits shift out
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
 // Store 32 packed 32-bit words to the warp's 32 TMEM lanes, columns taddr..+31.
 __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
   asm volatile(

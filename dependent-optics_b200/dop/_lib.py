@@ -117,6 +117,7 @@ SIGNATURES = [
     ("dop_clear_device_status", C.c_int, []),
     ("dop_set_wait_limits", C.c_int, [_I64, _I64]),
     ("dop_selftest_wait_expiry", C.c_int, [C.c_int, _P]),
+    ("dop_exp2_poly", C.c_int, [_P, _P, C.c_int64, _P]),
     ("dop_gqa_forward", C.c_int, [_I64, _I64, _I64, _I64, _I64, _I64, C.c_int, _P, _P, _P, _P,
                                   _P, _P]),
     ("dop_gqa_backward", C.c_int, [_I64, _I64, _I64, _I64, _I64, _I64, C.c_int, _P, _P, _P, _P,

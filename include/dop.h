@@ -327,6 +327,11 @@ int dop_selftest_wait_expiry(int which, void* stream);
 /* ----------------------------------------------------------- utilities */
 /* fp32 -> bf16 (round to nearest even), device arrays. */
 int dop_f32_to_bf16(const float* src, uint16_t* dst, int64_t n, void* stream);
+/* y = 2^x (device arrays, x < 128) by the polynomial the tensor-core
+ * attention softmax evaluates on the FMA pipe for a quarter of its
+ * exponentials; for checking its error bound.  No counterpart in the crate,
+ * whose softmax calls exp (src/mixtral.rs:924-929). */
+int dop_exp2_poly(const float* x, float* y, int64_t n, void* stream);
 /* p <- p - lr * g, returns nothing; `sgd_step` (src/mixtral.rs:994-1001). */
 int dop_sgd_step(float* params, const float* grad, int64_t n, float lr,
                  void* stream);

@@ -100,3 +100,24 @@ def test_gqa_f32_cuda_core_matches_float64(cuda, B, S, H, KV, hd, W):
     assert (lse.double() - lse_r).abs().max().item() < 1e-5
     for a, b in zip(outs[0], outs[1]):
         assert torch.equal(a, b)
+
+
+def test_exp2_polynomial_error_bound(cuda):
+    """The FMA-pipe exponential of the forward softmax (dop_exp2_poly, a
+    quarter of its exponentials) against exp2 in float64: relative error
+    below 1e-4 over [-125, 100) (the fit's bound is 7.6e-5; a bf16
+    probability rounds at 3.9e-3), and below -125 a value under 2e-38, where
+    the MUFU's flush-to-zero exp2 gives 0."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.cat([torch.linspace(-125.0, 99.99, 1_000_001, device="cuda"),
+                   torch.rand(1_000_000, generator=g, device="cuda") * -20.0,
+                   torch.tensor([0.0, -0.5, 0.5, 8.0, -1e-30], device="cuda")])
+    y = torch.empty_like(x)
+    check(lib().dop_exp2_poly(x.data_ptr(), y.data_ptr(), x.numel(), None))
+    ref = torch.exp2(x.double())
+    assert ((y.double() - ref).abs() / ref).max().item() < 1e-4
+    lo = torch.tensor([-125.5, -126.0, -200.0, -1e30, float("-inf")], device="cuda")
+    ylo = torch.empty_like(lo)
+    check(lib().dop_exp2_poly(lo.data_ptr(), ylo.data_ptr(), lo.numel(), None))
+    torch.cuda.synchronize()
+    assert bool(((ylo >= 0) & (ylo < 2e-38)).all())
