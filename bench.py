@@ -75,6 +75,12 @@ WORKLOADS = {
     # the tensor-core GEMM alone on one expert's gate projection at batch 2,
     # seq 4096 routed rows (16384 x 14336, contraction 4096): the kernel-level
     # profiling case, timed beside cuBLAS on the same shape
+    # the Mixtral-8x7B block's attention alone (32 / 8 heads, head_dim 128,
+    # causal, window 4096) through dop_gqa_forward / dop_gqa_backward
+    "mixtral8x7b_attention": dict(attention=(8, 4096, 32, 8, 128, 4096), precision="bf16",
+                                  skew=False),
+    "mixtral8x7b_attention_profile": dict(attention=(2, 4096, 32, 8, 128, 4096),
+                                          precision="bf16", skew=False),
     "gemm_bf16_expert": dict(gemm=(16384, 14336, 4096, 0), precision="bf16", skew=False),
     # the expert-input cotangent's shape: 16384 rows, N 4096, contraction
     # 28672, B read transposed (the crate's [D, I] gate/up weights)
@@ -278,7 +284,7 @@ def run_reference(a):
     if wl.get("program"):
         run_reference_program(a, wl, cores, world)
         return
-    if wl.get("gemm"):
+    if wl.get("gemm") or wl.get("attention"):
         print(json.dumps({"impl": "reference", "unavailable": "a kernel-level profiling workload "
                           "with no counterpart in the crate's CPU lens"}), flush=True)
         return
@@ -533,6 +539,77 @@ def run_gemm(a):
         "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": a.workload, "M": M, "N": N, "K": K, "b_t": b_t},
         "cublas_same_shape": {"ms": ms_cublas, "tflops": flops / ms_cublas / 1e9},
+        "clocks": clk.summary(),
+    }), flush=True)
+
+
+def run_attention(a):
+    """The tensor-core flash attention alone: dop_gqa_forward and
+    dop_gqa_backward (bf16 q, k, v, o, dO; fp32 lse, delta, dq, dk, dv) on
+    one shape, K timed calls of each between CUDA events; a step is one
+    forward and one backward.  FLOPs count the visible (query, key) pairs:
+    4 hd per pair forward, 2.5 times that backward."""
+    import numpy as np
+    import torch
+    from dop._lib import DOP_BF16, check, lib
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, S, H, KV, hd, W = WORKLOADS[a.workload]["attention"]
+    T = B * S
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(T, H, hd, generator=g, device=dev).bfloat16()
+    k = torch.randn(T, KV, hd, generator=g, device=dev).bfloat16()
+    v = torch.randn(T, KV, hd, generator=g, device=dev).bfloat16()
+    do = torch.randn(T, H, hd, generator=g, device=dev).bfloat16()
+    o, lse = torch.empty_like(q), torch.empty(B, H, S, device=dev)
+    dq = torch.empty(T, H, hd, device=dev)
+    dk, dv = torch.empty(T, KV, hd, device=dev), torch.empty(T, KV, hd, device=dev)
+    delta = torch.empty(B * H * S, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def fwd():
+        check(lib().dop_gqa_forward(B, S, H, KV, hd, W, DOP_BF16, q.data_ptr(), k.data_ptr(),
+                                    v.data_ptr(), o.data_ptr(), lse.data_ptr(), sp))
+
+    def bwd():
+        check(lib().dop_gqa_backward(B, S, H, KV, hd, W, DOP_BF16, q.data_ptr(), k.data_ptr(),
+                                     v.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(),
+                                     delta.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                     dv.data_ptr(), sp))
+
+    def timed(fn):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(a.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / a.steps
+
+    for _ in range(max(1, a.warmup)):
+        fwd()
+        bwd()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(0) as clk:
+        ms_f = timed(fwd)
+        ms_b = timed(bwd)
+    pairs = float(np.minimum(np.arange(S) + 1, W).sum()) * B * H
+    ff = 4 * hd * pairs
+    hbm, peak, peak_sus, src = measured_peaks()
+    print(json.dumps({
+        "metric": "attention fwd+bwd tokens/s (tensor-core kernels alone)",
+        "value": T / ((ms_f + ms_b) / 1e3), "unit": "tokens/s", "n_gpus": 1, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": ms_f + ms_b, "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic N(0,1) q, k, v, dO",
+        "config": {"workload": a.workload, "batch": B, "seq": S, "heads": H, "kv_heads": KV,
+                   "head_dim": hd, "window": W},
+        "phases_ms": {"attn_fwd": ms_f, "attn_bwd": ms_b},
+        "tflops": {"fwd": ff / ms_f / 1e9, "bwd": 2.5 * ff / ms_b / 1e9},
+        "frac_of_bf16_peak": {"fwd": ff / ms_f / 1e9 / peak, "bwd": 2.5 * ff / ms_b / 1e9 / peak},
+        "peak_source": f"{src} bf16_tflops (burst; kernels timed alone)",
         "clocks": clk.summary(),
     }), flush=True)
 
@@ -929,6 +1006,8 @@ def main():
         run_program(a)
     elif WORKLOADS[a.workload].get("gemm"):
         run_gemm(a)
+    elif WORKLOADS[a.workload].get("attention"):
+        run_attention(a)
     elif WORKLOADS[a.workload].get("stack"):
         run_stack(a)
     else:
