@@ -116,90 +116,111 @@ __global__ void __launch_bounds__(256) k_rmsnorm_fwd_v(const float* __restrict__
 // the crate's to the bit (an exp result can differ in its last bit only
 // where the libm's own result is not the correctly rounded one).
 //
-// Sequential sums leave one dependent chain per row and expert, so four
-// lanes share a row: each sums the squares of the whole row (the same chain,
-// so the same value) and then owns E / 4 of the router's logit chains.  A
-// warp takes 8 rows, which stream through a per-warp shared tile of 8 rows x
-// 64 columns (row pitch 68 floats: the coalesced 16-byte stores and the
-// rows' 16-byte reads are bank-conflict free), two tiles ahead in registers.
-// Pass 1 sums the squares; pass 2 writes xn = (x * r) * w from the tile in
-// its coalesced layout and accumulates the logits.
-constexpr int kRtLanes = 4;               // lanes per row
-constexpr int kRtRows = 32 / kRtLanes;    // rows per warp
-constexpr int kRtCols = 64;               // columns per tile
-constexpr int kRtPitch = kRtCols + 4;     // floats per tile row in shared memory
-constexpr int kRtWarps = 4;               // warps per CTA
+// Sequential sums leave one dependent chain per row (the sum of squares)
+// and per row and expert (the logits), and the norm's sum must finish before
+// the first logit term, so the stage is two kernels over the rows:
+//   k_router_rms     one lane per row: r = 1 / sqrt(sum x^2 / D + eps), the
+//                    row read in 16-byte pieces (a lane's 64-column run of
+//                    its row is 256 contiguous bytes, reused from L1);
+//   k_router_logits  two lanes per row, each owning half of the expert
+//                    chains; rows stream through a per-warp shared tile of 16
+//                    rows x 64 columns (read coalesced, one tile ahead in
+//                    registers), xn = (x r) w is written from the tile in its
+//                    coalesced layout, and the lane that owns expert 0 runs
+//                    softmax and top-k.
+constexpr int kRtCols = 64;                // columns per tile
+constexpr int kRtPitch = kRtCols + 4;      // floats per tile row in shared memory
+constexpr int kRtRows = 16;                // rows per warp (two lanes a row)
+constexpr int kRtWarps = 1;                // warps per CTA (one: the SMs' shares differ by a warp)
+
+// Crate-rounded exp: double-precision exp of the float argument, rounded
+// once to float.
+__device__ __forceinline__ float exp_rounded(float z) { return __double2float_rn(exp((double)z)); }
 
 template <bool VEC>
-struct RowTile {
-  float v[16];
-  // columns [c0, c0 + 64) of rows r0 .. r0 + 7 (zeros outside the matrix)
+__global__ void __launch_bounds__(32) k_router_rms(const float* __restrict__ x, int64_t rows,
+                                                    int D, float eps, float* __restrict__ inv) {
+  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const float* xr = x + row * D;
+  float ss = 0.0f;
+  if (VEC) {
+    // 64-column runs, the next run's loads in flight while this one is summed
+    constexpr int J = kRtCols / 4;
+    auto fetch = [&](int c0, float4 (&v)[J]) {
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int c = c0 + 4 * j;
+        v[j] = c < D ? __ldg(reinterpret_cast<const float4*>(xr + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    };
+    float4 a[J], b[J];
+    fetch(0, a);
+    for (int c0 = 0; c0 < D; c0 += 2 * kRtCols) {
+      if (c0 + kRtCols < D) fetch(c0 + kRtCols, b);
+      // zeros past D add nothing: ss + 0 * 0 = ss exactly
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        ss = __fadd_rn(ss, __fmul_rn(a[j].x, a[j].x));
+        ss = __fadd_rn(ss, __fmul_rn(a[j].y, a[j].y));
+        ss = __fadd_rn(ss, __fmul_rn(a[j].z, a[j].z));
+        ss = __fadd_rn(ss, __fmul_rn(a[j].w, a[j].w));
+      }
+      if (c0 + kRtCols >= D) break;
+      if (c0 + 2 * kRtCols < D) fetch(c0 + 2 * kRtCols, a);
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        ss = __fadd_rn(ss, __fmul_rn(b[j].x, b[j].x));
+        ss = __fadd_rn(ss, __fmul_rn(b[j].y, b[j].y));
+        ss = __fadd_rn(ss, __fmul_rn(b[j].z, b[j].z));
+        ss = __fadd_rn(ss, __fmul_rn(b[j].w, b[j].w));
+      }
+    }
+  } else {
+    for (int c = 0; c < D; ++c) ss = __fadd_rn(ss, __fmul_rn(xr[c], xr[c]));
+  }
+  inv[row] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
+}
+
+// Columns [c0, c0 + 64) of the warp's 16 rows (zeros outside the matrix):
+// lane l holds rows (l / 16) + 2 j, columns 4 (l % 16) .. + 3.
+template <bool VEC>
+struct RtTile {
+  float v[32];
   __device__ __forceinline__ void load(const float* __restrict__ x, int64_t rows, int D,
                                        int64_t r0, int c0, int lane) {
-    if (VEC) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t row = r0 + (lane >> 4) + 2 * j;
-        const int col = c0 + 4 * (lane & 15);
-        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (row < rows && col < D) t = *reinterpret_cast<const float4*>(x + row * D + col);
-        v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
+    for (int j = 0; j < 8; ++j) {
+      const int64_t row = r0 + (lane >> 4) + 2 * j;
+      const int col = c0 + 4 * (lane & 15);
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (row < rows) {
+        const float* p = x + row * D + col;
+        if (VEC) {
+          if (col < D) t = *reinterpret_cast<const float4*>(p);
+        } else {
+          if (col < D) t.x = p[0];
+          if (col + 1 < D) t.y = p[1];
+          if (col + 2 < D) t.z = p[2];
+          if (col + 3 < D) t.w = p[3];
+        }
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int64_t row = r0 + (j >> 1);
-        const int col = c0 + 32 * (j & 1) + lane;
-        v[j] = (row < rows && col < D) ? x[row * D + col] : 0.f;
-      }
+      v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
     }
   }
   __device__ __forceinline__ void store(float* tile, int lane) const {
-    if (VEC) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        *reinterpret_cast<float4*>(tile + ((lane >> 4) + 2 * j) * kRtPitch + 4 * (lane & 15)) =
-            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) tile[(j >> 1) * kRtPitch + 32 * (j & 1) + lane] = v[j];
-    }
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<float4*>(tile + ((lane >> 4) + 2 * j) * kRtPitch + 4 * (lane & 15)) =
+          make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   }
 };
 
-// Stream columns [0, D) of the warp's rows through its two shared tiles;
-// f(tile, c0, ncols) runs once per tile on every lane.
-template <bool VEC, class F>
-__device__ __forceinline__ void stream_rows(const float* __restrict__ x, int64_t rows, int D,
-                                            int64_t r0, float* tiles, int lane, F&& f) {
-  const int nt = (D + kRtCols - 1) / kRtCols;
-  RowTile<VEC> a, b;
-  a.load(x, rows, D, r0, 0, lane);
-  if (nt > 1) b.load(x, rows, D, r0, kRtCols, lane);
-  for (int t = 0; t < nt; ++t) {
-    __syncwarp();
-    float* slot = tiles + (t & 1) * kRtRows * kRtPitch;
-    if (t & 1) {
-      b.store(slot, lane);
-      if (t + 2 < nt) b.load(x, rows, D, r0, kRtCols * (t + 2), lane);
-    } else {
-      a.store(slot, lane);
-      if (t + 2 < nt) a.load(x, rows, D, r0, kRtCols * (t + 2), lane);
-    }
-    __syncwarp();
-    f(slot, kRtCols * t, min(kRtCols, D - kRtCols * t));
-  }
-}
-
-// The norm weights and router rows of one tile (64 model rows), loaded one
-// tile ahead into registers (lane l: model rows l and l + 32) and stored in
-// fp32 for the lane groups: the norm weights at ws[c], the router weights of
-// group q (experts q * EPL .. + EPL - 1) at wrs[q * QS + c * EPL + k].
+// The norm weights and router rows of one tile (64 model rows), in registers
+// one tile ahead (lane l: model rows l and l + 32), stored to shared memory
+// in fp32: ws[c] and wrs[c * NE + e] (zeros past D and past E).
 template <typename T, int NE>
-struct TileWeights {
-  static constexpr int EPL = NE / kRtLanes;
-  static constexpr int QS = kRtCols * EPL + 4;
-  static constexpr bool WIDE = NE == 8;  // a router row is 16 (bf16) or 32 (fp32) bytes
+struct RtWeights {
   float wn[2];
   float wv[2][NE];
   __device__ __forceinline__ void load(const T* __restrict__ w, const T* __restrict__ wr, int E,
@@ -209,8 +230,7 @@ struct TileWeights {
       const int c = c0 + lane + 32 * h;
       const bool in = c < D;
       wn[h] = in ? ld(&w[c]) : 0.f;
-      if (EPL == 0) continue;
-      if (WIDE && in) {
+      if (NE == 8 && E == 8 && in) {
         if (sizeof(T) == 2) {
           ld_row8(wr + (int64_t)c * 8, wv[h]);
         } else {
@@ -230,118 +250,110 @@ struct TileWeights {
     for (int h = 0; h < 2; ++h) {
       const int c = lane + 32 * h;
       ws[c] = wn[h];
+      if (NE % 4 == 0) {
 #pragma unroll
-      for (int e = 0; e < NE; e += EPL > 0 ? EPL : NE) {
-        if (EPL == 2) {
-          *reinterpret_cast<float2*>(wrs + (e / 2) * QS + c * 2) = make_float2(wv[h][e], wv[h][e + 1]);
-        } else if (EPL == 4) {
-          *reinterpret_cast<float4*>(wrs + (e / 4) * QS + c * 4) =
+        for (int e = 0; e < NE; e += 4)
+          *reinterpret_cast<float4*>(wrs + c * NE + e) =
               make_float4(wv[h][e], wv[h][e + 1], wv[h][e + 2], wv[h][e + 3]);
-        } else if (EPL > 0) {
+      } else {
 #pragma unroll
-          for (int k = 0; k < EPL; ++k) wrs[(e / EPL) * QS + c * EPL + k] = wv[h][e + k];
-        }
+        for (int e = 0; e < NE; ++e) wrs[c * NE + e] = wv[h][e];
       }
     }
   }
 };
 
-// Crate-rounded exp: double-precision exp of the float argument, rounded
-// once to float.
-__device__ __forceinline__ float exp_rounded(float z) { return __double2float_rn(exp((double)z)); }
-
 template <typename T, int NE, bool VEC>
-__global__ void __launch_bounds__(32 * kRtWarps, 6) k_router_stage(
+__global__ void __launch_bounds__(32 * kRtWarps, 16 / kRtWarps) k_router_logits(
     const float* __restrict__ x, const T* __restrict__ w, const T* __restrict__ wr,
-    const float* __restrict__ bias, int64_t rows, int D, int E, int K, float eps,
-    T* __restrict__ y, float* __restrict__ inv, float* __restrict__ probs,
+    const float* __restrict__ bias, int64_t rows, int D, int E, int K,
+    const float* __restrict__ inv, T* __restrict__ y, float* __restrict__ probs,
     int* __restrict__ top_i, float* __restrict__ top_p, float* __restrict__ top_w) {
-  constexpr int EPL = NE / kRtLanes;            // logit chains per lane (0 when E == 1)
-  constexpr int QS = TileWeights<T, NE>::QS;    // floats per lane group in wrs
-  __shared__ __align__(16) float tiles_all[kRtWarps][2 * kRtRows * kRtPitch];
-  __shared__ __align__(16) float wr_all[kRtWarps][EPL > 0 ? kRtLanes * QS : 4];
-  __shared__ __align__(16) float w_all[kRtWarps][kRtCols];
+  constexpr int EPL = NE / 2;  // logit chains per lane (0 when E == 1)
+  __shared__ __align__(16) float tile_all[kRtWarps][kRtRows * kRtPitch];
+  __shared__ __align__(16) float wrs_all[kRtWarps][kRtCols * NE];
+  __shared__ __align__(16) float ws_all[kRtWarps][kRtCols];
+  __shared__ float r_all[kRtWarps][kRtRows];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int rr = lane / kRtLanes, q = lane % kRtLanes;  // row in the warp, logit group
+  const int rr = lane >> 1, q = lane & 1;  // row in the warp, expert half
   const int64_t r0 = ((int64_t)blockIdx.x * kRtWarps + wid) * kRtRows;
   if (r0 >= rows) return;  // whole warp
   const int64_t row = r0 + rr;
   const bool live = row < rows;
-  float* tiles = tiles_all[wid];
-  float* wrs = wr_all[wid];
-  float* ws = w_all[wid];
+  float* tile = tile_all[wid];
+  float* wrs = wrs_all[wid];
+  float* ws = ws_all[wid];
+  float* rs = r_all[wid];
+  const float r = live ? inv[row] : 0.f;
+  if (q == 0) rs[rr] = r;
 
-  // pass 1: sum of squares in index order (src/mixtral.rs:672-676)
-  float ss = 0.0f;
-  stream_rows<VEC>(x, rows, D, r0, tiles, lane, [&](const float* tile, int, int n) {
-    const float* mine = tile + rr * kRtPitch;
-    if (n == kRtCols) {
-#pragma unroll
-      for (int c = 0; c < kRtCols; c += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(mine + c);
-        ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
-        ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
-        ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
-        ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
-      }
-    } else {
-      for (int c = 0; c < n; ++c) ss = __fadd_rn(ss, __fmul_rn(mine[c], mine[c]));
-    }
-  });
-  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
-  if (live && q == 0) inv[row] = r;
-
-  // pass 2: xn = (x * r) * w written out; logits z_e = sum_i xn_i wr[i, e]
   float z[EPL > 0 ? EPL : 1];
 #pragma unroll
   for (int k = 0; k < (EPL > 0 ? EPL : 1); ++k) z[k] = 0.0f;
-  TileWeights<T, NE> tw;
-  tw.load(w, wr, E, D, 0, lane);
-  stream_rows<VEC>(x, rows, D, r0, tiles, lane, [&](const float* tile, int c0, int n) {
-    // this tile's weights to shared memory, the next tile's into registers
-    tw.store(ws, wrs, lane);
-    if (c0 + kRtCols < D) tw.load(w, wr, E, D, c0 + kRtCols, lane);
+  const int nt = (D + kRtCols - 1) / kRtCols;
+  RtTile<VEC> cur, nxt;
+  RtWeights<T, NE> wcur, wnxt;
+  cur.load(x, rows, D, r0, 0, lane);
+  wcur.load(w, wr, E, D, 0, lane);
+  for (int t = 0; t < nt; ++t) {
+    const int c0 = t * kRtCols, n = min(kRtCols, D - c0);
     __syncwarp();
-    if (VEC && n == kRtCols) {
-      // xn from the tile in its coalesced layout: rows (lane / 16) + 2 j,
-      // columns 4 (lane % 16) .. + 3
-      const float4 wv = *reinterpret_cast<const float4*>(ws + 4 * (lane & 15));
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int tr = (lane >> 4) + 2 * j;
-        const float rj = __shfl_sync(0xffffffffu, r, tr * kRtLanes);
-        const float4 xv = *reinterpret_cast<const float4*>(tile + tr * kRtPitch + 4 * (lane & 15));
-        if (r0 + tr < rows)
-          st4(y + (r0 + tr) * D + c0 + 4 * (lane & 15),
-              make_float4(__fmul_rn(__fmul_rn(xv.x, rj), wv.x), __fmul_rn(__fmul_rn(xv.y, rj), wv.y),
-                          __fmul_rn(__fmul_rn(xv.z, rj), wv.z), __fmul_rn(__fmul_rn(xv.w, rj), wv.w)));
-      }
-    } else if (live && q == 0) {
-      const float* mine = tile + rr * kRtPitch;
-      for (int c = 0; c < n; ++c) st(&y[row * D + c0 + c], __fmul_rn(__fmul_rn(mine[c], r), ws[c]));
+    cur.store(tile, lane);
+    wcur.store(ws, wrs, lane);
+    if (t + 1 < nt) {
+      nxt.load(x, rows, D, r0, c0 + kRtCols, lane);
+      wnxt.load(w, wr, E, D, c0 + kRtCols, lane);
     }
+    __syncwarp();
+    // xn = (x r) w from the tile in its coalesced layout: rows (lane / 16) + 2 j
+    {
+      const int col = 4 * (lane & 15);
+      if (col < n) {
+        const float4 wv = *reinterpret_cast<const float4*>(ws + col);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int tr = (lane >> 4) + 2 * j;
+          if (r0 + tr >= rows) continue;
+          const float rj = rs[tr];
+          const float4 xv = *reinterpret_cast<const float4*>(tile + tr * kRtPitch + col);
+          const float4 o = make_float4(__fmul_rn(__fmul_rn(xv.x, rj), wv.x),
+                                       __fmul_rn(__fmul_rn(xv.y, rj), wv.y),
+                                       __fmul_rn(__fmul_rn(xv.z, rj), wv.z),
+                                       __fmul_rn(__fmul_rn(xv.w, rj), wv.w));
+          T* dst = y + (r0 + tr) * D + c0 + col;
+          if (VEC && col + 4 <= n) {
+            st4(dst, o);
+          } else {
+            const float ov[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (col + e < n) st(dst + e, ov[e]);
+          }
+        }
+      }
+    }
+    // this lane's logit chains over the tile's columns, in index order
     if (EPL > 0) {
       const float* mine = tile + rr * kRtPitch;
-      const float* wq = wrs + q * QS;
-      auto step = [&](float xv, float wv, int c) {
-        const float xn = __fmul_rn(__fmul_rn(xv, r), wv);
-        if (EPL == 2) {
-          const float2 g = *reinterpret_cast<const float2*>(wq + c * 2);
-          z[0] = __fadd_rn(z[0], __fmul_rn(xn, g.x));
-          z[EPL > 1 ? 1 : 0] = __fadd_rn(z[EPL > 1 ? 1 : 0], __fmul_rn(xn, g.y));
-        } else if (EPL == 4) {
-          const float4 g = *reinterpret_cast<const float4*>(wq + c * 4);
-          z[0] = __fadd_rn(z[0], __fmul_rn(xn, g.x));
-          z[EPL > 1 ? 1 : 0] = __fadd_rn(z[EPL > 1 ? 1 : 0], __fmul_rn(xn, g.y));
-          z[EPL > 2 ? 2 : 0] = __fadd_rn(z[EPL > 2 ? 2 : 0], __fmul_rn(xn, g.z));
-          z[EPL > 3 ? 3 : 0] = __fadd_rn(z[EPL > 3 ? 3 : 0], __fmul_rn(xn, g.w));
+      const float* wq = wrs + q * EPL;
+      auto step = [&](float xv, float wn, int c) {
+        const float xn = __fmul_rn(__fmul_rn(xv, r), wn);
+        if (EPL % 4 == 0) {
+#pragma unroll
+          for (int k = 0; k < EPL; k += 4) {
+            const float4 g = *reinterpret_cast<const float4*>(wq + c * NE + k);
+            z[k] = __fadd_rn(z[k], __fmul_rn(xn, g.x));
+            z[k + 1] = __fadd_rn(z[k + 1], __fmul_rn(xn, g.y));
+            z[k + 2] = __fadd_rn(z[k + 2], __fmul_rn(xn, g.z));
+            z[k + 3] = __fadd_rn(z[k + 3], __fmul_rn(xn, g.w));
+          }
         } else {
 #pragma unroll
-          for (int k = 0; k < EPL; ++k) z[k] = __fadd_rn(z[k], __fmul_rn(xn, wq[c * EPL + k]));
+          for (int k = 0; k < EPL; ++k) z[k] = __fadd_rn(z[k], __fmul_rn(xn, wq[c * NE + k]));
         }
       };
       if (n == kRtCols) {
-#pragma unroll
+#pragma unroll 4
         for (int c = 0; c < kRtCols; c += 4) {
           const float4 xv = *reinterpret_cast<const float4*>(mine + c);
           const float4 wv = *reinterpret_cast<const float4*>(ws + c);
@@ -354,14 +366,14 @@ __global__ void __launch_bounds__(32 * kRtWarps, 6) k_router_stage(
         for (int c = 0; c < n; ++c) step(mine[c], ws[c], c);
       }
     }
-    __syncwarp();
-  });
-  // every lane of the row's group gathers the row's E logits
+    cur = nxt;
+    wcur = wnxt;
+  }
+  // the row's E logits to the lane that owns expert 0
   float zf[NE];
 #pragma unroll
   for (int e = 0; e < NE; ++e)
-    zf[e] = EPL > 0 ? __shfl_sync(0xffffffffu, z[EPL > 0 ? e % EPL : 0],
-                                  rr * kRtLanes + (EPL > 0 ? e / EPL : 0))
+    zf[e] = EPL > 0 ? __shfl_sync(0xffffffffu, z[EPL > 0 ? e % EPL : 0], 2 * rr + (EPL > 0 ? e / EPL : 0))
                     : 0.0f;
   if (!live || q != 0) return;
 
@@ -871,35 +883,45 @@ __global__ void k_unpermute_router_dx(const float* __restrict__ dxp,
   }
 }
 
-// k_router_bwd with 4-wide dot products (D % 4 == 0, aligned rows).
-__global__ void k_router_bwd_v(const float* __restrict__ dy, const float* __restrict__ out,
-                               const int* __restrict__ slot_row, const int* __restrict__ top_i,
-                               const float* __restrict__ top_p, const float* __restrict__ top_w,
-                               const float* __restrict__ probs, int E, int K, int D,
-                               float* __restrict__ dz) {
+// k_router_bwd with 4-wide dot products (D % 4 == 0, aligned rows): a thread
+// takes the NV quads threadIdx.x + 256 j of the row and issues all of their
+// loads (dy and the KK <= kMaxTopK expert-output rows) before the first
+// product, so that NV (1 + K) 16-byte loads are in flight.
+template <int NV, int KK>
+__global__ void __launch_bounds__(256) k_router_bwd_v(
+    const float* __restrict__ dy, const float* __restrict__ out, const int* __restrict__ slot_row,
+    const int* __restrict__ top_i, const float* __restrict__ top_p, const float* __restrict__ top_w,
+    const float* __restrict__ probs, int E, int K, int D, float* __restrict__ dz) {
   const int64_t t = blockIdx.x;
   __shared__ float red[kMaxTopK][32];
   __shared__ float dv[kMaxTopK];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float acc[kMaxTopK];
-  int64_t rows[kMaxTopK];
+  const int D4 = D / 4;
+  int64_t rows[KK];
 #pragma unroll
-  for (int k = 0; k < kMaxTopK; ++k) {
-    acc[k] = 0.f;
-    rows[k] = k < K ? slot_row[t * K + k] : 0;
-  }
-  for (int i = threadIdx.x * 4; i < D; i += blockDim.x * 4) {
-    const float4 g = ld4(dy + t * D + i);
+  for (int k = 0; k < KK; ++k) rows[k] = k < K ? slot_row[t * K + k] : 0;
+  float4 g[NV], o[NV][KK];
 #pragma unroll
-    for (int k = 0; k < kMaxTopK; ++k) {
-      if (k < K) {
-        const float4 o = ld4(out + rows[k] * D + i);
-        acc[k] += g.x * o.x + g.y * o.y + g.z * o.z + g.w * o.w;
-      }
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + 256 * j;
+    g[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < D4) g[j] = ld4(dy + t * D + 4 * i);
+#pragma unroll
+    for (int k = 0; k < KK; ++k) {
+      o[j][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k < K && i < D4) o[j][k] = ld4(out + rows[k] * D + 4 * i);
     }
   }
+  float acc[KK];
 #pragma unroll
-  for (int k = 0; k < kMaxTopK; ++k) {
+  for (int k = 0; k < KK; ++k) {
+    acc[k] = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+      acc[k] += g[j].x * o[j][k].x + g[j].y * o[j][k].y + g[j].z * o[j][k].z + g[j].w * o[j][k].w;
+  }
+#pragma unroll
+  for (int k = 0; k < KK; ++k) {
     if (k < K) {
       const float v = warp_sum(acc[k]);
       if (lane == 0) red[k][warp] = v;
@@ -924,29 +946,44 @@ __global__ void k_router_bwd_v(const float* __restrict__ dy, const float* __rest
   }
 }
 
-// k_unpermute_router_dx with 4-wide accesses; E8: 8 experts, router rows
-// read 16 or 32 bytes at a time.
-template <typename T, bool E8>
-__global__ void k_unpermute_router_dx_v(const float* __restrict__ dxp,
-                                        const int* __restrict__ slot_row,
-                                        const float* __restrict__ dz, const T* __restrict__ wr,
-                                        int E, int K, int D, float* __restrict__ dxn) {
+// k_unpermute_router_dx with 4-wide accesses: a thread takes the NV quads
+// threadIdx.x + 256 j of the token's row and issues every expert-row load
+// (KK >= K of them per quad) before the first sum, so that NV K 16-byte loads
+// are in flight; the router rows (E8: 8 experts, 16 or 32 bytes a row) come
+// from L1.  Per element the sums run in the same order as
+// k_unpermute_router_dx's.
+template <typename T, bool E8, int NV, int KK>
+__global__ void __launch_bounds__(256) k_unpermute_router_dx_v(
+    const float* __restrict__ dxp, const int* __restrict__ slot_row, const float* __restrict__ dz,
+    const T* __restrict__ wr, int E, int K, int D, float* __restrict__ dxn) {
   const int64_t t = blockIdx.x;
   __shared__ float dzs[kMaxExperts];
   __shared__ int64_t rows[kMaxTopK];
   if (threadIdx.x < E) dzs[threadIdx.x] = dz[t * E + threadIdx.x];
   if (threadIdx.x < K) rows[threadIdx.x] = slot_row[t * K + threadIdx.x];
   __syncthreads();
-  for (int i = threadIdx.x * 4; i < D; i += blockDim.x * 4) {
+  const int D4 = D / 4;
+  float4 v[NV][KK];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + 256 * j;
+#pragma unroll
+    for (int k = 0; k < KK; ++k)
+      v[j][k] = (i < D4 && k < K) ? ld4(dxp + rows[k] * D + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + 256 * j;
+    if (i >= D4) continue;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < K; ++k) {
-      const float4 v = ld4(dxp + rows[k] * D + i);
-      a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+#pragma unroll
+    for (int k = 0; k < KK; ++k) {
+      if (k < K) { a.x += v[j][k].x; a.y += v[j][k].y; a.z += v[j][k].z; a.w += v[j][k].w; }
     }
     float rr[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const T* wrow = wr + (int64_t)(i + u) * E;
+      const T* wrow = wr + (int64_t)(4 * i + u) * E;
       float acc = 0.f;
       if (E8) {
         float wv8[8];
@@ -958,7 +995,7 @@ __global__ void k_unpermute_router_dx_v(const float* __restrict__ dxp,
       }
       rr[u] = acc;
     }
-    st4(dxn + t * D + i, make_float4(a.x + rr[0], a.y + rr[1], a.z + rr[2], a.w + rr[3]));
+    st4(dxn + t * D + 4 * i, make_float4(a.x + rr[0], a.y + rr[1], a.z + rr[2], a.w + rr[3]));
   }
 }
 
@@ -988,59 +1025,68 @@ __global__ void k_router_dw(const float* __restrict__ mid, const float* __restri
     if (e < E) part[((int64_t)c * D + i) * E + e] = acc[e];
 }
 
-// k_router_dw for 8 experts with four columns a thread and eight rows' loads
-// in flight (the scalar kernel has one 4-byte load in flight per thread and
-// is latency-bound).  Same products summed in the same row order per
-// element, so the partials are bit-identical to k_router_dw's.
+// k_router_dw for 8 experts with two columns a thread and sixteen rows'
+// loads in flight (the scalar kernel has one 4-byte load in flight per
+// thread and is latency-bound); the rows' dz and inv are staged in shared
+// memory 256 rows at a time.  Same products summed in the same row order
+// per element, so the partials are bit-identical to k_router_dw's.
+constexpr int kRdwRows = 256;
 template <typename T>
-__global__ void __launch_bounds__(128) k_router_dw_v(const float* __restrict__ mid,
+__global__ void __launch_bounds__(128, 5) k_router_dw_v(const float* __restrict__ mid,
                                                      const float* __restrict__ inv,
                                                      const T* __restrict__ w,
                                                      const float* __restrict__ dz, int64_t rows,
                                                      int D, int rows_per_chunk,
                                                      float* __restrict__ part) {
-  constexpr int E = 8, U = 8;
-  const int i4 = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  constexpr int E = 8, U = 16;
+  __shared__ __align__(16) float dzs[kRdwRows][E];
+  __shared__ float ivs[kRdwRows];
+  const int i2 = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+  const bool col_ok = i2 < D;
   const int c = blockIdx.y;
-  if (i4 >= D) return;
   const int64_t t0 = (int64_t)c * rows_per_chunk;
   const int64_t t1 = ::min((int64_t)rows, t0 + rows_per_chunk);
-  float acc[4][E];
+  float acc[2][E];
 #pragma unroll
-  for (int q = 0; q < 4; ++q)
+  for (int q = 0; q < 2; ++q)
 #pragma unroll
     for (int e = 0; e < E; ++e) acc[q][e] = 0.f;
-  const float4 wv = ld4(w + i4);
-  const float wq[4] = {wv.x, wv.y, wv.z, wv.w};
-  for (int64_t t = t0; t < t1; t += U) {
-    float4 mv[U];
-    float iv[U];
+  const float wq[2] = {col_ok ? ld(&w[i2]) : 0.f, col_ok ? ld(&w[i2 + 1]) : 0.f};
+  for (int64_t p0 = t0; p0 < t1; p0 += kRdwRows) {
+    const int np = (int)::min((int64_t)kRdwRows, t1 - p0);
+    __syncthreads();
+    for (int k = threadIdx.x; k < np * E; k += blockDim.x) dzs[k / E][k % E] = dz[p0 * E + k];
+    for (int k = threadIdx.x; k < np; k += blockDim.x) ivs[k] = inv[p0 + k];
+    __syncthreads();
+    if (!col_ok) continue;
+    for (int r = 0; r < np; r += U) {
+      float2 mv[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (t + u < t1) {
-        mv[u] = ld4(mid + (t + u) * D + i4);
-        iv[u] = inv[t + u];
-      }
-    }
+      for (int u = 0; u < U; ++u)
+        if (r + u < np) mv[u] = *reinterpret_cast<const float2*>(mid + (p0 + r + u) * D + i2);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (t + u < t1) {
-        const float4 d0 = ld4(dz + (t + u) * E), d1 = ld4(dz + (t + u) * E + 4);
-        const float dv[E] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-        const float mq[4] = {mv[u].x, mv[u].y, mv[u].z, mv[u].w};
+      for (int u = 0; u < U; ++u) {
+        if (r + u < np) {
+          const float4 d0 = *reinterpret_cast<const float4*>(&dzs[r + u][0]);
+          const float4 d1 = *reinterpret_cast<const float4*>(&dzs[r + u][4]);
+          const float dv[E] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+          const float mq[2] = {mv[u].x, mv[u].y};
+          const float iv = ivs[r + u];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float xn = mq[q] * iv[u] * wq[q];
+          for (int q = 0; q < 2; ++q) {
+            const float xn = mq[q] * iv * wq[q];
 #pragma unroll
-          for (int e = 0; e < E; ++e) acc[q][e] += xn * dv[e];
+            for (int e = 0; e < E; ++e) acc[q][e] += xn * dv[e];
+          }
         }
       }
     }
   }
+  if (!col_ok) return;
 #pragma unroll
-  for (int q = 0; q < 4; ++q)
+  for (int q = 0; q < 2; ++q)
 #pragma unroll
-    for (int e = 0; e < E; ++e) part[((int64_t)c * D + i4 + q) * E + e] = acc[q][e];
+    for (int e = 0; e < E; ++e) part[((int64_t)c * D + i2 + q) * E + e] = acc[q][e];
 }
 
 // --------------------------------------------------------------- misc
@@ -1151,11 +1197,15 @@ void rmsnorm_router(const float* x, const T* w, const T* wr, const float* bias, 
                     float* top_p, float* top_w, cudaStream_t s, int64_t& launches) {
   DOP_REQUIRE(E <= kMaxExperts && K <= kMaxTopK && K <= E, "experts/top_k out of range");
   const bool vec = D % 4 == 0 && aligned4(x) && aligned4(y);
+  // one row a thread, one-warp CTAs so that the SMs' shares differ by at most a warp
+  if (vec) k_router_rms<true><<<(unsigned)ceil_div(rows, 32), 32, 0, s>>>(x, rows, D, eps, inv);
+  else k_router_rms<false><<<(unsigned)ceil_div(rows, 32), 32, 0, s>>>(x, rows, D, eps, inv);
+  DOP_LAUNCHED(launches);
   const unsigned grid = (unsigned)ceil_div(rows, kRtRows * kRtWarps);
   const dim3 block(32 * kRtWarps);
 #define DOP_ROUTER(NE)                                                                        \
-  (vec ? k_router_stage<T, NE, true> : k_router_stage<T, NE, false>)<<<grid, block, 0, s>>>( \
-      x, w, wr, bias, rows, D, E, K, eps, y, inv, probs, top_i, top_p, top_w)
+  (vec ? k_router_logits<T, NE, true> : k_router_logits<T, NE, false>)<<<grid, block, 0, s>>>( \
+      x, w, wr, bias, rows, D, E, K, inv, y, probs, top_i, top_p, top_w)
   if (E == 1) DOP_ROUTER(1);
   else if (E <= 4) DOP_ROUTER(4);
   else if (E <= 8) DOP_ROUTER(8);
@@ -1275,10 +1325,19 @@ void combine(const float* mid, const float* out, const int* slot_row, const floa
 void router_bwd(const float* dy, const float* out, const int* slot_row, const int* top_i,
                 const float* top_p, const float* top_w, const float* probs, int64_t Tn, int E,
                 int K, int D, float* dz, cudaStream_t s, int64_t& launches) {
-  if (D % 4 == 0 && aligned4(dy) && aligned4(out))
-    k_router_bwd_v<<<(unsigned)Tn, 256, 0, s>>>(dy, out, slot_row, top_i, top_p, top_w, probs, E,
-                                                K, D, dz);
-  else
+  const int nv = row_quads(D);
+  if (nv && aligned4(dy) && aligned4(out)) {
+#define DOP_RBWD(NV, KK) k_router_bwd_v<NV, KK><<<(unsigned)Tn, 256, 0, s>>>( \
+    dy, out, slot_row, top_i, top_p, top_w, probs, E, K, D, dz)
+    if (K <= 2) {
+      if (nv == 1) DOP_RBWD(1, 2); else if (nv == 2) DOP_RBWD(2, 2);
+      else if (nv == 4) DOP_RBWD(4, 2); else DOP_RBWD(8, 2);
+    } else {
+      if (nv == 1) DOP_RBWD(1, 4); else if (nv == 2) DOP_RBWD(2, 4);
+      else if (nv == 4) DOP_RBWD(4, 4); else DOP_RBWD(8, 4);
+    }
+#undef DOP_RBWD
+  } else
     k_router_bwd<<<(unsigned)Tn, 256, 0, s>>>(dy, out, slot_row, top_i, top_p, top_w, probs, E, K,
                                               D, dz);
   DOP_LAUNCHED(launches);
@@ -1288,13 +1347,22 @@ template <typename T>
 void unpermute_router_dx(const float* dxp, const int* slot_row, const float* dz, const T* wr,
                          int64_t Tn, int E, int K, int D, float* dxn, cudaStream_t s,
                          int64_t& launches) {
-  if (D % 4 == 0 && aligned4(dxp) && aligned4(dxn)) {
-    if (E == 8 && (uintptr_t)wr % 16 == 0)
-      k_unpermute_router_dx_v<T, true><<<(unsigned)Tn, 256, 0, s>>>(dxp, slot_row, dz, wr, E, K, D,
-                                                                    dxn);
-    else
-      k_unpermute_router_dx_v<T, false><<<(unsigned)Tn, 256, 0, s>>>(dxp, slot_row, dz, wr, E, K,
-                                                                     D, dxn);
+  const int nv = row_quads(D);
+  if (nv && aligned4(dxp) && aligned4(dxn)) {
+    const bool e8 = E == 8 && (uintptr_t)wr % 16 == 0;
+#define DOP_UPDX(E8, NV, KK) k_unpermute_router_dx_v<T, E8, NV, KK><<<(unsigned)Tn, 256, 0, s>>>( \
+    dxp, slot_row, dz, wr, E, K, D, dxn)
+#define DOP_UPDX_NV(E8, KK)                          \
+  if (nv == 1) DOP_UPDX(E8, 1, KK);                  \
+  else if (nv == 2) DOP_UPDX(E8, 2, KK);             \
+  else if (nv == 4) DOP_UPDX(E8, 4, KK);             \
+  else DOP_UPDX(E8, 8, KK)
+    if (e8 && K <= 2) { DOP_UPDX_NV(true, 2); }
+    else if (e8) { DOP_UPDX_NV(true, 4); }
+    else if (K <= 2) { DOP_UPDX_NV(false, 2); }
+    else { DOP_UPDX_NV(false, 4); }
+#undef DOP_UPDX_NV
+#undef DOP_UPDX
   } else {
     k_unpermute_router_dx<T><<<(unsigned)Tn, 256, 0, s>>>(dxp, slot_row, dz, wr, E, K, D, dxn);
   }
@@ -1305,12 +1373,17 @@ template <typename T>
 void router_dw(const float* mid, const float* inv, const T* w, const float* dz, int64_t rows,
                int D, int E, float* dwr_accum, float* part_buf, int64_t part_cap,
                cudaStream_t s, int64_t& launches) {
-  int64_t chunks = std::min<int64_t>(rows, 64);
+  const bool vec = E == 8 && D % 4 == 0 && aligned4(mid) && aligned4(w) && aligned4(dz);
+  // the 4-wide kernel: as many row chunks as fill one wave of resident CTAs
+  // (five per SM) over the column blocks, at most 64
+  const int64_t col_blocks = ceil_div(D / 2, 128);
+  int64_t chunks = vec ? std::max<int64_t>(1, std::min<int64_t>(64, 5 * sm_count() / col_blocks)) : 64;
+  chunks = std::min<int64_t>(rows, chunks);
   int rows_per_chunk = (int)ceil_div(rows, chunks);
   chunks = ceil_div(rows, rows_per_chunk);
   DOP_REQUIRE(chunks * D * E <= part_cap, "partial buffer too small");
-  if (E == 8 && D % 4 == 0 && aligned4(mid) && aligned4(w) && aligned4(dz)) {
-    dim3 grid((unsigned)ceil_div(D / 4, 128), (unsigned)chunks);
+  if (vec) {
+    dim3 grid((unsigned)col_blocks, (unsigned)chunks);
     k_router_dw_v<T><<<grid, 128, 0, s>>>(mid, inv, w, dz, rows, D, rows_per_chunk, part_buf);
   } else {
     dim3 grid((unsigned)ceil_div(D, 128), (unsigned)chunks);

@@ -230,6 +230,22 @@ def test_bf16_block_matches_oracle_on_rounded_inputs(cuda, kind):
         assert np.all(gpu["dP"][a:b] == 0.0)
 
 
+@pytest.mark.parametrize("dim, experts, top_k", [(100, 12, 3), (98, 6, 2), (256, 16, 4)],
+                         ids=["d100-e12-k3", "d98-e6-k2", "d256-e16-k4"])
+def test_router_stage_odd_widths(cuda, dim, experts, top_k):
+    """The router stage's two kernels off the Mixtral shape: a model width
+    that is not a multiple of the 64-column tile (100), one that is not a
+    multiple of 4 (98: scalar loads), and 12 / 6 / 16 experts (16 logit
+    chains per row, 8 with unused ones).  Same 1e-6 gap bar on the lens's own
+    feed-forward input, probability rows bit-identical but for rare
+    last-bit exp roundings (at most 4 of the 160 rows)."""
+    cfg = small_cfg(dim=dim, experts=experts, top_k=top_k)
+    lp, x, dy = make_inputs(cfg, 2, 80, seed=7)
+    gpu = run_gpu(cfg, 2, 80, lp, x, dy, DOP_F32)
+    _, exact = check_router_stage(cfg, gpu["blk"], lp)
+    assert exact >= 156 / 160, f"only {exact:.4f} of the probability rows are bit-identical"
+
+
 def test_permutation_is_the_stable_expert_sort(cuda):
     cfg = small_cfg(experts=8, top_k=2)
     batch, seq = 4, 100
