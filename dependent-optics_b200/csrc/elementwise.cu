@@ -128,6 +128,18 @@ __global__ void __launch_bounds__(256) k_rmsnorm_fwd_v(const float* __restrict__
 //                    registers), xn = (x r) w is written from the tile in its
 //                    coalesced layout, and the lane that owns expert 0 runs
 //                    softmax and top-k.
+// Two IEEE round-to-nearest products in one instruction (PTX mul.rn.f32x2,
+// sm_100): each lane of the pair is rounded exactly as __fmul_rn would.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  uint64_t d, ua, ub;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ua) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ub) : "f"(b.x), "f"(b.y));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(ua), "l"(ub));
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+  return r;
+}
+
 constexpr int kRtCols = 64;                // columns per tile
 constexpr int kRtPitch = kRtCols + 4;      // floats per tile row in shared memory
 constexpr int kRtRows = 16;                // rows per warp (two lanes a row)
@@ -316,10 +328,10 @@ __global__ void __launch_bounds__(32 * kRtWarps, 16 / kRtWarps) k_router_logits(
           if (r0 + tr >= rows) continue;
           const float rj = rs[tr];
           const float4 xv = *reinterpret_cast<const float4*>(tile + tr * kRtPitch + col);
-          const float4 o = make_float4(__fmul_rn(__fmul_rn(xv.x, rj), wv.x),
-                                       __fmul_rn(__fmul_rn(xv.y, rj), wv.y),
-                                       __fmul_rn(__fmul_rn(xv.z, rj), wv.z),
-                                       __fmul_rn(__fmul_rn(xv.w, rj), wv.w));
+          const float2 r2 = make_float2(rj, rj);
+          const float2 o01 = mul2_rn(mul2_rn(make_float2(xv.x, xv.y), r2), make_float2(wv.x, wv.y));
+          const float2 o23 = mul2_rn(mul2_rn(make_float2(xv.z, xv.w), r2), make_float2(wv.z, wv.w));
+          const float4 o = make_float4(o01.x, o01.y, o23.x, o23.y);
           T* dst = y + (r0 + tr) * D + c0 + col;
           if (VEC && col + 4 <= n) {
             st4(dst, o);
@@ -336,20 +348,16 @@ __global__ void __launch_bounds__(32 * kRtWarps, 16 / kRtWarps) k_router_logits(
     if (EPL > 0) {
       const float* mine = tile + rr * kRtPitch;
       const float* wq = wrs + q * EPL;
-      auto step = [&](float xv, float wn, int c) {
-        const float xn = __fmul_rn(__fmul_rn(xv, r), wn);
-        if (EPL % 4 == 0) {
+      const float2 r2 = make_float2(r, r);
+      // products in pairs (exact), the sums one chain per expert in column
+      // order; EPL is even
+      auto step = [&](float xn, int c) {
+        const float2 xx = make_float2(xn, xn);
 #pragma unroll
-          for (int k = 0; k < EPL; k += 4) {
-            const float4 g = *reinterpret_cast<const float4*>(wq + c * NE + k);
-            z[k] = __fadd_rn(z[k], __fmul_rn(xn, g.x));
-            z[k + 1] = __fadd_rn(z[k + 1], __fmul_rn(xn, g.y));
-            z[k + 2] = __fadd_rn(z[k + 2], __fmul_rn(xn, g.z));
-            z[k + 3] = __fadd_rn(z[k + 3], __fmul_rn(xn, g.w));
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < EPL; ++k) z[k] = __fadd_rn(z[k], __fmul_rn(xn, wq[c * NE + k]));
+        for (int k = 0; k < EPL; k += 2) {
+          const float2 pr = mul2_rn(xx, *reinterpret_cast<const float2*>(wq + c * NE + k));
+          z[k] = __fadd_rn(z[k], pr.x);
+          z[k + 1] = __fadd_rn(z[k + 1], pr.y);
         }
       };
       if (n == kRtCols) {
@@ -357,13 +365,15 @@ __global__ void __launch_bounds__(32 * kRtWarps, 16 / kRtWarps) k_router_logits(
         for (int c = 0; c < kRtCols; c += 4) {
           const float4 xv = *reinterpret_cast<const float4*>(mine + c);
           const float4 wv = *reinterpret_cast<const float4*>(ws + c);
-          step(xv.x, wv.x, c);
-          step(xv.y, wv.y, c + 1);
-          step(xv.z, wv.z, c + 2);
-          step(xv.w, wv.w, c + 3);
+          const float2 x01 = mul2_rn(mul2_rn(make_float2(xv.x, xv.y), r2), make_float2(wv.x, wv.y));
+          const float2 x23 = mul2_rn(mul2_rn(make_float2(xv.z, xv.w), r2), make_float2(wv.z, wv.w));
+          step(x01.x, c);
+          step(x01.y, c + 1);
+          step(x23.x, c + 2);
+          step(x23.y, c + 3);
         }
       } else {
-        for (int c = 0; c < n; ++c) step(mine[c], ws[c], c);
+        for (int c = 0; c < n; ++c) step(__fmul_rn(__fmul_rn(mine[c], r), ws[c]), c);
       }
     }
     cur = nxt;
