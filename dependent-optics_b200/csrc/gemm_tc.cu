@@ -934,28 +934,53 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
-// out[z][o][i] = split(src(z, o, i)), src(z, o, i) = src[z zs + o ld + i]
-// (TR = false) or src[z zs + i ld + o] (TR = true); a 32 x 32 tile per CTA
-// of 32 x 8 threads, transposed through shared memory when TR.
-template <bool TR>
-__global__ void k_split_tf32(const float* __restrict__ src, int64_t O, int64_t Ki, int64_t ld,
-                             int64_t zs, float* __restrict__ hi, float* __restrict__ lo) {
+// out[z][o][i] = split(src(z, o, i)) with src(z, o, i) = src[z zs + o ld + i]:
+// an elementwise map, four elements (16-byte loads, two 16-byte stores) a
+// thread when the rows allow it.
+template <bool VEC>
+__global__ void k_split_tf32_rows(const float* __restrict__ src, int64_t Z, int64_t O, int64_t Ki,
+                                  int64_t ld, int64_t zs, float* __restrict__ hi,
+                                  float* __restrict__ lo) {
+  constexpr int W = VEC ? 4 : 1;
+  const int64_t per_row = Ki / W, total = Z * O * per_row;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = e / per_row, i = (e % per_row) * W;
+    const int64_t z = row / O, o = row % O;
+    const float* sp = src + z * zs + o * ld + i;
+    const int64_t at = row * Ki + i;
+    if (VEC) {
+      const float4 x = *reinterpret_cast<const float4*>(sp);
+      const float4 h = make_float4(tf32_rna(x.x), tf32_rna(x.y), tf32_rna(x.z), tf32_rna(x.w));
+      *reinterpret_cast<float4*>(hi + at) = h;
+      *reinterpret_cast<float4*>(lo + at) = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+    } else {
+      const float x = sp[0], h = tf32_rna(x);
+      hi[at] = h;
+      lo[at] = x - h;
+    }
+  }
+}
+
+// out[z][o][i] = split(src[z zs + i ld + o]): a transposition through a
+// 32 x 32 shared tile per CTA of 32 x 8 threads, read along o and written
+// along i, both coalesced.
+__global__ void k_split_tf32_tr(const float* __restrict__ src, int64_t O, int64_t Ki, int64_t ld,
+                                int64_t zs, float* __restrict__ hi, float* __restrict__ lo) {
   __shared__ float tile[32][33];
   const int64_t z = blockIdx.z;
   const int64_t o0 = (int64_t)blockIdx.y * 32, i0 = (int64_t)blockIdx.x * 32;
   const float* sz = src + z * zs;
   const int tx = threadIdx.x, ty = threadIdx.y;
-  if (TR) {
-    for (int r = ty; r < 32; r += 8) {  // read along o (contiguous in src)
-      const int64_t i = i0 + r, o = o0 + tx;
-      tile[r][tx] = (i < Ki && o < O) ? sz[i * ld + o] : 0.f;
-    }
-    __syncthreads();
+  for (int r = ty; r < 32; r += 8) {  // rows i, columns o (contiguous in src)
+    const int64_t i = i0 + r, o = o0 + tx;
+    tile[r][tx] = (i < Ki && o < O) ? sz[i * ld + o] : 0.f;
   }
-  for (int r = ty; r < 32; r += 8) {  // write along i
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {  // rows o, columns i
     const int64_t o = o0 + r, i = i0 + tx;
     if (o >= O || i >= Ki) continue;
-    const float x = TR ? tile[tx][r] : sz[o * ld + i];
+    const float x = tile[tx][r];
     const float h = tf32_rna(x);
     const int64_t at = (z * O + o) * Ki + i;
     hi[at] = h;
@@ -965,10 +990,16 @@ __global__ void k_split_tf32(const float* __restrict__ src, int64_t O, int64_t K
 
 void split_tf32(const float* src, int64_t Z, int64_t O, int64_t Ki, int64_t ld, int64_t zs, bool tr,
                 float* hi, float* lo, cudaStream_t s, int64_t& launches) {
-  const dim3 grid((unsigned)ceil_div(Ki, 32), (unsigned)ceil_div(O, 32), (unsigned)Z);
-  const dim3 block(32, 8);
-  if (tr) k_split_tf32<true><<<grid, block, 0, s>>>(src, O, Ki, ld, zs, hi, lo);
-  else k_split_tf32<false><<<grid, block, 0, s>>>(src, O, Ki, ld, zs, hi, lo);
+  if (tr) {
+    const dim3 grid((unsigned)ceil_div(Ki, 32), (unsigned)ceil_div(O, 32), (unsigned)Z);
+    k_split_tf32_tr<<<grid, dim3(32, 8), 0, s>>>(src, O, Ki, ld, zs, hi, lo);
+  } else {
+    const bool vec = Ki % 4 == 0 && ld % 4 == 0 && zs % 4 == 0 && (uintptr_t)src % 16 == 0;
+    const int64_t items = Z * O * (vec ? Ki / 4 : Ki);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(items, 256), 16 * sm_count()));
+    if (vec) k_split_tf32_rows<true><<<grid, 256, 0, s>>>(src, Z, O, Ki, ld, zs, hi, lo);
+    else k_split_tf32_rows<false><<<grid, 256, 0, s>>>(src, Z, O, Ki, ld, zs, hi, lo);
+  }
   DOP_LAUNCHED(launches);
 }
 
