@@ -420,7 +420,7 @@ constexpr int BSTAGES = 4;
 // dO and O tiles in shared memory (O loaded with Q and dO) and writes it for
 // the dK/dV kernel, which runs next.
 constexpr int DQ_GROUPS = 3;
-constexpr int DQ_THREADS = 64 + DQ_GROUPS * 128;
+constexpr int DQ_THREADS = 64 + DQ_GROUPS * 128 + 32;  // + the dQ MMA issuer (warp 14)
 __global__ void __launch_bounds__(DQ_THREADS, 1)
     k_attn_dq_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                  const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
@@ -442,6 +442,9 @@ __global__ void __launch_bounds__(DQ_THREADS, 1)
   auto kv_empty = [&](int st) { return b0 + 56 + 8u * st; };
   auto sd_full = [&](int g) { return b0 + 88 + 8u * g; };
   auto ds_full = [&](int g) { return b0 + 112 + 8u * g; };
+  // group g's dS columns have been read by the dQ MMAs
+  auto dq_free = [&](int g) { return b0 + 136 + 8u * g; };
+  const uint32_t drain2 = b0 + 160;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = p.n_tiles - 1 - (int)blockIdx.x;
@@ -463,7 +466,9 @@ __global__ void __launch_bounds__(DQ_THREADS, 1)
     for (int g = 0; g < DQ_GROUPS; ++g) {
       mbar_init(sd_full(g), 1);
       mbar_init(ds_full(g), 4);
+      mbar_init(dq_free(g), 1);
     }
+    mbar_init(drain2, 1);
     *abort_flag = 0;
     mbar_init_fence();
   }
@@ -504,28 +509,18 @@ __global__ void __launch_bounds__(DQ_THREADS, 1)
       }
     }
   } else if (warp == 1) {
+    // S and dP: this thread.  dQ += dS K is issued by warp 14, so that the
+    // two instruction streams are issued in parallel; S of tile j waits
+    // until the dQ MMAs of tile j - 3 (same group columns) have run.
     if (lane == 0) {
       constexpr uint32_t ID_SD = idesc_bf16(128, 64, false, false);   // Q K^T, dO V^T
-      constexpr uint32_t ID_DQ = idesc_bf16(128, 128, false, true);   // dS K (K N-major)
       const uint32_t qs = smem_u32(sQ), dos = smem_u32(sDO);
       bool ok = mbar_wait(q_full, 0, abort_flag, 22);
-      // dQ += dS_i K_i (dS from TMEM); it precedes S of tile i + 3, which
-      // overwrites dS_i's columns (one thread's MMAs run in order)
-      auto issue_dq = [&](int i) -> bool {
-        const int gi = i % DQ_GROUPS;
-        if (!mbar_wait(ds_full(gi), (i / DQ_GROUPS) & 1, abort_flag, 23)) return false;
-        tc_fence_after();
-        const uint32_t ks = smem_u32(sK + (i % BSTAGES) * QTILE);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_bf16_ts(tmem, tmem + 128 + gi * 128 + k * 8, mnmajor_desc(ks + k * 2048, QHALF),
-                      ID_DQ, (i > 0 || k > 0) ? 1u : 0u);
-        mma_commit(kv_empty(i % BSTAGES));
-        return true;
-      };
       for (int j = 0; j < nt && ok; ++j) {
         const int g = j % DQ_GROUPS, st = j % BSTAGES;
         if (!mbar_wait(kv_full(st), (j / BSTAGES) & 1, abort_flag, 24)) { ok = false; break; }
+        if (j >= DQ_GROUPS &&
+            !mbar_wait(dq_free(g), ((j - DQ_GROUPS) / DQ_GROUPS) & 1, abort_flag, 27)) { ok = false; break; }
         tc_fence_after();
         const uint32_t ks = smem_u32(sK + st * QTILE), vs = smem_u32(sV + st * QTILE);
 #pragma unroll
@@ -536,13 +531,29 @@ __global__ void __launch_bounds__(DQ_THREADS, 1)
           mma_bf16(tmem + 192 + g * 128, kmajor_desc(dos + oa), kmajor_desc(vs + ob), ID_SD, k > 0);
         }
         mma_commit(sd_full(g));
-        if (j >= 2 && !issue_dq(j - 2)) { ok = false; break; }
       }
-      for (int i = std::max(0, nt - 2); i < nt && ok; ++i)
-        if (!issue_dq(i)) ok = false;
-      if (ok) mma_commit(dq_done);
       mma_commit(drain);
       mbar_wait_drain(drain, 0);
+    }
+  } else if (warp == 14) {
+    if (lane == 0) {
+      constexpr uint32_t ID_DQ = idesc_bf16(128, 128, false, true);   // dS K (K N-major)
+      bool ok = true;
+      for (int i = 0; i < nt && ok; ++i) {
+        const int gi = i % DQ_GROUPS;
+        if (!mbar_wait(ds_full(gi), (i / DQ_GROUPS) & 1, abort_flag, 23)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ks = smem_u32(sK + (i % BSTAGES) * QTILE);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_bf16_ts(tmem, tmem + 128 + gi * 128 + k * 8, mnmajor_desc(ks + k * 2048, QHALF),
+                      ID_DQ, (i > 0 || k > 0) ? 1u : 0u);
+        mma_commit(kv_empty(i % BSTAGES));
+        mma_commit(dq_free(gi));
+      }
+      if (ok && nt > 0) mma_commit(dq_done);
+      mma_commit(drain2);
+      mbar_wait_drain(drain2, 0);
     }
   } else {
     const int g = (warp - 2) >> 2;
@@ -653,7 +664,8 @@ static_assert(kDqSmem <= 232448, "dQ kernel shared memory above the per-CTA limi
 // to group i & 1).  TMEM: dV 0-127, dK 128-255; group g: S^T_g 256+128g
 // (P^T packed in its first 32 columns), dP^T_g 320+128g (dS^T packed).
 // S^T = K Q^T, dP^T = V dO^T, dV += P^T dO, dK += dS^T Q.
-__global__ void __launch_bounds__(320, 1)
+constexpr int DKDV_THREADS = 352;  // TMA, S MMA issuer, 2 x 4 elementwise, accumulate MMA issuer
+__global__ void __launch_bounds__(DKDV_THREADS, 1)
     k_attn_dkdv_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
                    const BwdParams p) {
@@ -674,6 +686,9 @@ __global__ void __launch_bounds__(320, 1)
   auto q_empty = [&](int st) { return b0 + 56 + 8u * st; };
   auto sd_full = [&](int g) { return b0 + 88 + 8u * g; };
   auto pd_full = [&](int g) { return b0 + 104 + 8u * g; };
+  // group g's P^T / dS^T columns have been read by the accumulating MMAs
+  auto acc_free = [&](int g) { return b0 + 136 + 8u * g; };
+  const uint32_t drain2 = b0 + 152;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = (int)blockIdx.x;
@@ -695,7 +710,9 @@ __global__ void __launch_bounds__(320, 1)
     for (int g = 0; g < 2; ++g) {
       mbar_init(sd_full(g), 1);
       mbar_init(pd_full(g), 4);
+      mbar_init(acc_free(g), 1);
     }
+    mbar_init(drain2, 1);
     *abort_flag = 0;
     mbar_init_fence();
   }
@@ -735,14 +752,40 @@ __global__ void __launch_bounds__(320, 1)
       }
     }
   } else if (warp == 1) {
+    // S^T and dP^T: this thread.  The accumulating MMAs (dV += P^T dO,
+    // dK += dS^T Q) are issued by warp 10, so that the two streams of
+    // instructions are issued in parallel; S^T of pair i waits until the
+    // accumulating MMAs of pair i - 2 (same group columns) have run.
     if (lane == 0) {
       constexpr uint32_t ID_ST = idesc_bf16(128, 64, false, false);   // K Q^T, V dO^T
-      constexpr uint32_t ID_ACC = idesc_bf16(128, 128, false, true);  // P^T dO, dS^T Q
       const uint32_t ks = smem_u32(sK), vs = smem_u32(sV);
       bool ok = mbar_wait(kv_full, 0, abort_flag, 32);
-      auto issue_acc = [&](int i) -> bool {
+      for (int i = 0; i < total && ok; ++i) {
+        const int g = i & 1, st = i % BSTAGES;
+        if (!mbar_wait(q_full(st), (i / BSTAGES) & 1, abort_flag, 34)) { ok = false; break; }
+        if (i >= 2 && !mbar_wait(acc_free(g), ((i - 2) >> 1) & 1, abort_flag, 35)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t qs = smem_u32(sQ + st * QTILE), dos = smem_u32(sDO + st * QTILE);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t ka = (k >> 2) * HALF + (k & 3) * 32;   // K/V: two 16 KB d-boxes
+          const uint32_t kb = (k >> 2) * QHALF + (k & 3) * 32;  // Q/dO: two 8 KB d-boxes
+          mma_bf16(tmem + 256 + g * 128, kmajor_desc(ks + ka), kmajor_desc(qs + kb), ID_ST, k > 0);
+          mma_bf16(tmem + 320 + g * 128, kmajor_desc(vs + ka), kmajor_desc(dos + kb), ID_ST, k > 0);
+        }
+        mma_commit(sd_full(g));
+      }
+      mma_commit(drain);
+      mbar_wait_drain(drain, 0);
+    }
+  } else if (warp == 10) {
+    if (lane == 0) {
+      constexpr uint32_t ID_ACC = idesc_bf16(128, 128, false, true);  // P^T dO, dS^T Q
+      bool ok = true;
+      int i = 0;
+      for (; i < total && ok; ++i) {
         const int gi = i & 1, st = i % BSTAGES;
-        if (!mbar_wait(pd_full(gi), (i >> 1) & 1, abort_flag, 33)) return false;
+        if (!mbar_wait(pd_full(gi), (i >> 1) & 1, abort_flag, 33)) { ok = false; break; }
         tc_fence_after();
         const uint32_t qs = smem_u32(sQ + st * QTILE), dos = smem_u32(sDO + st * QTILE);
 #pragma unroll
@@ -754,26 +797,11 @@ __global__ void __launch_bounds__(320, 1)
                       ID_ACC, acc);
         }
         mma_commit(q_empty(st));
-        return true;
-      };
-      for (int i = 0; i < total && ok; ++i) {
-        const int g = i & 1, st = i % BSTAGES;
-        if (!mbar_wait(q_full(st), (i / BSTAGES) & 1, abort_flag, 34)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t qs = smem_u32(sQ + st * QTILE), dos = smem_u32(sDO + st * QTILE);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t ka = (k >> 2) * HALF + (k & 3) * 32;   // K/V: two 16 KB d-boxes
-          const uint32_t kb = (k >> 2) * QHALF + (k & 3) * 32;  // Q/dO: two 8 KB d-boxes
-          mma_bf16(tmem + 256 + g * 128, kmajor_desc(ks + ka), kmajor_desc(qs + kb), ID_ST, k > 0);
-          mma_bf16(tmem + 320 + g * 128, kmajor_desc(vs + ka), kmajor_desc(dos + kb), ID_ST, k > 0);
-        }
-        mma_commit(sd_full(g));
-        if (i >= 1 && !issue_acc(i - 1)) { ok = false; break; }
+        mma_commit(acc_free(gi));
       }
-      if (ok && issue_acc(total - 1)) mma_commit(acc_done);
-      mma_commit(drain);
-      mbar_wait_drain(drain, 0);
+      if (ok && total > 0) mma_commit(acc_done);
+      mma_commit(drain2);
+      mbar_wait_drain(drain2, 0);
     }
   } else {
     const int g = (warp - 2) >> 2;
@@ -1005,7 +1033,7 @@ void attn_bwd_tc(const Attn& a, const bf16* q, const bf16* k, const bf16* v, con
       attr = true;
     }
     dim3 grid((unsigned)p.n_tiles, (unsigned)a.KV, (unsigned)a.B);
-    k_attn_dkdv_tc<<<grid, 320, kDkdvSmem, s>>>(mq, mk, mv, mdo, p);
+    k_attn_dkdv_tc<<<grid, DKDV_THREADS, kDkdvSmem, s>>>(mq, mk, mv, mdo, p);
     DOP_LAUNCHED(launches);
   }
 }
