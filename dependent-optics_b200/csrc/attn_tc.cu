@@ -420,7 +420,7 @@ constexpr int BSTAGES = 4;
 // dO and O tiles in shared memory (O loaded with Q and dO) and writes it for
 // the dK/dV kernel, which runs next.
 constexpr int DQ_GROUPS = 3;
-constexpr int DQ_THREADS = 64 + DQ_GROUPS * 128 + 32;  // + the dQ MMA issuer (warp 14)
+constexpr int DQ_THREADS = 64 + DQ_GROUPS * 128 + 64;  // + the dQ (warp 14) and dP (warp 15) MMA issuers
 __global__ void __launch_bounds__(DQ_THREADS, 1)
     k_attn_dq_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                  const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
@@ -444,7 +444,7 @@ __global__ void __launch_bounds__(DQ_THREADS, 1)
   auto ds_full = [&](int g) { return b0 + 112 + 8u * g; };
   // group g's dS columns have been read by the dQ MMAs
   auto dq_free = [&](int g) { return b0 + 136 + 8u * g; };
-  const uint32_t drain2 = b0 + 160;
+  const uint32_t drain2 = b0 + 160, drain3 = b0 + 168;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = p.n_tiles - 1 - (int)blockIdx.x;
@@ -464,11 +464,12 @@ __global__ void __launch_bounds__(DQ_THREADS, 1)
       mbar_init(kv_empty(st), 1);
     }
     for (int g = 0; g < DQ_GROUPS; ++g) {
-      mbar_init(sd_full(g), 1);
+      mbar_init(sd_full(g), 2);  // the S and the dP issuer
       mbar_init(ds_full(g), 4);
       mbar_init(dq_free(g), 1);
     }
     mbar_init(drain2, 1);
+    mbar_init(drain3, 1);
     *abort_flag = 0;
     mbar_init_fence();
   }
@@ -508,13 +509,17 @@ __global__ void __launch_bounds__(DQ_THREADS, 1)
           mbar_wait_drain(kv_full(j % BSTAGES), (j / BSTAGES) & 1);
       }
     }
-  } else if (warp == 1) {
-    // S and dP: this thread.  dQ += dS K is issued by warp 14, so that the
-    // two instruction streams are issued in parallel; S of tile j waits
-    // until the dQ MMAs of tile j - 3 (same group columns) have run.
+  } else if (warp == 1 || warp == 15) {
+    // S (warp 1) and dP (warp 15) are issued by two threads and dQ += dS K
+    // by warp 14, so that three instruction streams are issued in parallel;
+    // S and dP of tile j wait until the dQ MMAs of tile j - 3 (same group
+    // columns) have run.
     if (lane == 0) {
       constexpr uint32_t ID_SD = idesc_bf16(128, 64, false, false);   // Q K^T, dO V^T
-      const uint32_t qs = smem_u32(sQ), dos = smem_u32(sDO);
+      const bool is_s = warp == 1;
+      const uint32_t as = smem_u32(is_s ? sQ : sDO);
+      uint8_t* const bstage = is_s ? sK : sV;
+      const uint32_t dcol = is_s ? 128u : 192u;
       bool ok = mbar_wait(q_full, 0, abort_flag, 22);
       for (int j = 0; j < nt && ok; ++j) {
         const int g = j % DQ_GROUPS, st = j % BSTAGES;
@@ -522,18 +527,18 @@ __global__ void __launch_bounds__(DQ_THREADS, 1)
         if (j >= DQ_GROUPS &&
             !mbar_wait(dq_free(g), ((j - DQ_GROUPS) / DQ_GROUPS) & 1, abort_flag, 27)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t ks = smem_u32(sK + st * QTILE), vs = smem_u32(sV + st * QTILE);
+        const uint32_t bs = smem_u32(bstage + st * QTILE);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t oa = (k >> 2) * HALF + (k & 3) * 32;
           const uint32_t ob = (k >> 2) * QHALF + (k & 3) * 32;
-          mma_bf16(tmem + 128 + g * 128, kmajor_desc(qs + oa), kmajor_desc(ks + ob), ID_SD, k > 0);
-          mma_bf16(tmem + 192 + g * 128, kmajor_desc(dos + oa), kmajor_desc(vs + ob), ID_SD, k > 0);
+          mma_bf16(tmem + dcol + g * 128, kmajor_desc(as + oa), kmajor_desc(bs + ob), ID_SD, k > 0);
         }
         mma_commit(sd_full(g));
       }
-      mma_commit(drain);
-      mbar_wait_drain(drain, 0);
+      const uint32_t dr = is_s ? drain : drain3;
+      mma_commit(dr);
+      mbar_wait_drain(dr, 0);
     }
   } else if (warp == 14) {
     if (lane == 0) {
@@ -664,7 +669,7 @@ static_assert(kDqSmem <= 232448, "dQ kernel shared memory above the per-CTA limi
 // to group i & 1).  TMEM: dV 0-127, dK 128-255; group g: S^T_g 256+128g
 // (P^T packed in its first 32 columns), dP^T_g 320+128g (dS^T packed).
 // S^T = K Q^T, dP^T = V dO^T, dV += P^T dO, dK += dS^T Q.
-constexpr int DKDV_THREADS = 352;  // TMA, S MMA issuer, 2 x 4 elementwise, accumulate MMA issuer
+constexpr int DKDV_THREADS = 384;  // TMA, S^T issuer, 2 x 4 elementwise, accumulate issuer, dP^T issuer
 __global__ void __launch_bounds__(DKDV_THREADS, 1)
     k_attn_dkdv_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
@@ -688,7 +693,7 @@ __global__ void __launch_bounds__(DKDV_THREADS, 1)
   auto pd_full = [&](int g) { return b0 + 104 + 8u * g; };
   // group g's P^T / dS^T columns have been read by the accumulating MMAs
   auto acc_free = [&](int g) { return b0 + 136 + 8u * g; };
-  const uint32_t drain2 = b0 + 152;
+  const uint32_t drain2 = b0 + 152, drain3 = b0 + 160;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = (int)blockIdx.x;
@@ -708,11 +713,12 @@ __global__ void __launch_bounds__(DKDV_THREADS, 1)
       mbar_init(q_empty(st), 1);
     }
     for (int g = 0; g < 2; ++g) {
-      mbar_init(sd_full(g), 1);
+      mbar_init(sd_full(g), 2);  // the S^T and the dP^T issuer
       mbar_init(pd_full(g), 4);
       mbar_init(acc_free(g), 1);
     }
     mbar_init(drain2, 1);
+    mbar_init(drain3, 1);
     *abort_flag = 0;
     mbar_init_fence();
   }
@@ -751,32 +757,36 @@ __global__ void __launch_bounds__(DKDV_THREADS, 1)
           mbar_wait_drain(q_full(i % BSTAGES), (i / BSTAGES) & 1);
       }
     }
-  } else if (warp == 1) {
-    // S^T and dP^T: this thread.  The accumulating MMAs (dV += P^T dO,
-    // dK += dS^T Q) are issued by warp 10, so that the two streams of
-    // instructions are issued in parallel; S^T of pair i waits until the
-    // accumulating MMAs of pair i - 2 (same group columns) have run.
+  } else if (warp == 1 || warp == 11) {
+    // S^T (warp 1) and dP^T (warp 11) are issued by two threads and the
+    // accumulating MMAs (dV += P^T dO, dK += dS^T Q) by warp 10, so that
+    // three instruction streams are issued in parallel; S^T and dP^T of
+    // pair i wait until the accumulating MMAs of pair i - 2 (same group
+    // columns) have run.
     if (lane == 0) {
       constexpr uint32_t ID_ST = idesc_bf16(128, 64, false, false);   // K Q^T, V dO^T
-      const uint32_t ks = smem_u32(sK), vs = smem_u32(sV);
+      const bool is_s = warp == 1;
+      const uint32_t as = smem_u32(is_s ? sK : sV);
+      uint8_t* const bstage = is_s ? sQ : sDO;
+      const uint32_t dcol = is_s ? 256u : 320u;
       bool ok = mbar_wait(kv_full, 0, abort_flag, 32);
       for (int i = 0; i < total && ok; ++i) {
         const int g = i & 1, st = i % BSTAGES;
         if (!mbar_wait(q_full(st), (i / BSTAGES) & 1, abort_flag, 34)) { ok = false; break; }
         if (i >= 2 && !mbar_wait(acc_free(g), ((i - 2) >> 1) & 1, abort_flag, 35)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t qs = smem_u32(sQ + st * QTILE), dos = smem_u32(sDO + st * QTILE);
+        const uint32_t bs = smem_u32(bstage + st * QTILE);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t ka = (k >> 2) * HALF + (k & 3) * 32;   // K/V: two 16 KB d-boxes
           const uint32_t kb = (k >> 2) * QHALF + (k & 3) * 32;  // Q/dO: two 8 KB d-boxes
-          mma_bf16(tmem + 256 + g * 128, kmajor_desc(ks + ka), kmajor_desc(qs + kb), ID_ST, k > 0);
-          mma_bf16(tmem + 320 + g * 128, kmajor_desc(vs + ka), kmajor_desc(dos + kb), ID_ST, k > 0);
+          mma_bf16(tmem + dcol + g * 128, kmajor_desc(as + ka), kmajor_desc(bs + kb), ID_ST, k > 0);
         }
         mma_commit(sd_full(g));
       }
-      mma_commit(drain);
-      mbar_wait_drain(drain, 0);
+      const uint32_t dr = is_s ? drain : drain3;
+      mma_commit(dr);
+      mbar_wait_drain(dr, 0);
     }
   } else if (warp == 10) {
     if (lane == 0) {
