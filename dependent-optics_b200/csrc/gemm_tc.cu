@@ -556,6 +556,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               u4p[q] = ui[q];
             }
           }
+
           if (!empty_k) tmem_ld32(tbase + c * 32, v);
           else {
 #pragma unroll
@@ -615,9 +616,23 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
             } else {
               if (p.epi == kAddResF32) {
-                const float* r = p.R + m * p.ldr + n;
-                for (int j = 0; j < 32; ++j)
-                  if (n + j < p.N) v[j] += r[j];
+                // the residual in 16-byte loads when the 32 columns are whole
+                // and aligned
+                const float* rp = p.R + m * p.ldr + n;
+                if (full && ((uintptr_t)rp & 15) == 0) {
+#pragma unroll
+                  for (int q = 0; q < 8; ++q) {
+                    const float4 r4 = ((const float4*)rp)[q];
+                    v[4 * q] += r4.x;
+                    v[4 * q + 1] += r4.y;
+                    v[4 * q + 2] += r4.z;
+                    v[4 * q + 3] += r4.w;
+                  }
+                } else {
+                  const float* r = p.R + m * p.ldr + n;
+                  for (int j = 0; j < 32; ++j)
+                    if (n + j < p.N) v[j] += r[j];
+                }
               }
               if (full) {
 #pragma unroll
