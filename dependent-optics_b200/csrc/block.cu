@@ -537,7 +537,8 @@ void Block::fwd(const Act* P, const float* x, float* y, cudaStream_t s) {
       return;
     }
   }
-  gather_rows<Act>(xn2_, row_token, seg_off, (int)E, (int)D, rows_cap, xp_, s, launches);
+  scatter_rows<Act>(xn2_, slot_row, T, (int)K, row_token, seg_off, (int)E, (int)D, rows_cap, xp_, s,
+                    launches);
   ph_end(s);
   ph_begin("expert_gate_up", s);
   {

@@ -458,6 +458,30 @@ __global__ void k_gather_rows16(const uint4* __restrict__ src, const int* __rest
     dst[r * n16 + i] = t >= 0 ? src[(int64_t)t * n16 + i] : make_uint4(0u, 0u, 0u, 0u);
 }
 
+// Token-major form of k_gather_rows16: CTA t reads token row t once and
+// writes it to its K expert rows slot_row[t K + k] (16-byte words).
+__global__ void k_scatter_rows16(const uint4* __restrict__ src, const int* __restrict__ slot_row,
+                                 int K, int n16, uint4* __restrict__ dst) {
+  const int64_t t = blockIdx.x;
+  int64_t rows[kMaxTopK];
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) rows[k] = k < K ? slot_row[t * K + k] : 0;
+  for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+    const uint4 v = src[t * n16 + i];
+#pragma unroll
+    for (int k = 0; k < kMaxTopK; ++k)
+      if (k < K) dst[rows[k] * n16 + i] = v;
+  }
+}
+// The padding rows of the expert segments (row_token < 0) to zero, one warp
+// a row.
+__global__ void k_zero_pad_rows16(const int* __restrict__ row_token, const int* __restrict__ seg_off,
+                                  int E, int64_t rows_cap, int n16, uint4* __restrict__ dst) {
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (r >= rows_cap || r >= seg_off[E] || row_token[r] >= 0) return;
+  for (int i = threadIdx.x & 31; i < n16; i += 32) dst[r * n16 + i] = make_uint4(0u, 0u, 0u, 0u);
+}
+
 // dO[r] = row_w[r] * dy[row_token[r]], 4 elements per access.
 template <typename T>
 __global__ void k_gather_scale_rows_v(const float* __restrict__ src,
@@ -1297,6 +1321,23 @@ void gather_rows(const T* src, const int* row_token, const int* seg_off, int E, 
 }
 
 template <typename T>
+void scatter_rows(const T* src, const int* slot_row, int64_t Tn, int K, const int* row_token,
+                  const int* seg_off, int E, int D, int64_t rows_cap, T* dst, cudaStream_t s,
+                  int64_t& launches) {
+  const int64_t bytes = (int64_t)D * sizeof(T);
+  if (bytes % 16 != 0 || (uintptr_t)src % 16 != 0 || (uintptr_t)dst % 16 != 0 || K > kMaxTopK) {
+    gather_rows<T>(src, row_token, seg_off, E, D, rows_cap, dst, s, launches);
+    return;
+  }
+  const int n16 = (int)(bytes / 16);
+  k_scatter_rows16<<<(unsigned)Tn, 128, 0, s>>>((const uint4*)src, slot_row, K, n16, (uint4*)dst);
+  DOP_LAUNCHED(launches);
+  k_zero_pad_rows16<<<(unsigned)ceil_div(rows_cap, 8), 256, 0, s>>>(row_token, seg_off, E, rows_cap,
+                                                                     n16, (uint4*)dst);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename T>
 void gather_scale_rows(const float* src, const int* row_token, const float* row_w,
                        const int* seg_off, int E, int D, int64_t rows_cap, T* dst, cudaStream_t s,
                        int64_t& launches) {
@@ -1465,6 +1506,8 @@ void sgd(float* p, const float* g, int64_t n, float lr, cudaStream_t s, int64_t&
                                const float*, float, cudaStream_t, int64_t&);                    \
   template void gather_rows<T>(const T*, const int*, const int*, int, int, int64_t, T*,        \
                                cudaStream_t, int64_t&);                                         \
+  template void scatter_rows<T>(const T*, const int*, int64_t, int, const int*, const int*, int, \
+                                int, int64_t, T*, cudaStream_t, int64_t&);                       \
   template void silu_mul<T>(const T*, const T*, const int*, int, int64_t, int64_t, T*,         \
                             cudaStream_t, int64_t&);                                            \
   template void silu_mul_bwd<T>(const float*, const T*, const T*, const int*, int, int64_t,    \

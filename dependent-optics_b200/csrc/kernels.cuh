@@ -39,6 +39,12 @@ void permute(const int* top_i, const float* top_w, int64_t T, int E, int K, int*
 template <typename T>
 void gather_rows(const T* src, const int* row_token, const int* seg_off, int E, int D,
                  int64_t rows_cap, T* dst, cudaStream_t s, int64_t& launches);
+// The same rows written token-major (each token row read once, written to its
+// K expert rows slot_row[t K + k]; padding rows zeroed).
+template <typename T>
+void scatter_rows(const T* src, const int* slot_row, int64_t Tn, int K, const int* row_token,
+                  const int* seg_off, int E, int D, int64_t rows_cap, T* dst, cudaStream_t s,
+                  int64_t& launches);
 template <typename T>
 void gather_scale_rows(const float* src, const int* row_token, const float* row_w,
                        const int* seg_off, int E, int D, int64_t rows_cap, T* dst, cudaStream_t s,
