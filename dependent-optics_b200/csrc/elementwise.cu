@@ -1033,6 +1033,73 @@ __global__ void __launch_bounds__(256) k_unpermute_router_dx_v(
   }
 }
 
+// k_unpermute_router_dx with the router rows held in registers: a thread
+// owns four columns (one quad) of the model dimension, reads their router
+// rows once, and runs over a chunk of kUdTok tokens (their dz and expert rows
+// staged in shared memory), four tokens' loads in flight.  The weights are
+// read once per chunk instead of once per token; per element the sums run in
+// the same order as k_unpermute_router_dx's.
+constexpr int kUdTok = 64;
+template <typename T, int NE, int KK>
+__global__ void __launch_bounds__(256) k_unpermute_router_dx_ws(
+    const float* __restrict__ dxp, const int* __restrict__ slot_row, const float* __restrict__ dz,
+    const T* __restrict__ wr, int64_t Tn, int E, int K, int D, float* __restrict__ dxn) {
+  __shared__ float dzs[kUdTok][NE];
+  __shared__ int64_t rows_s[kUdTok][kMaxTopK];
+  const int64_t t0 = (int64_t)blockIdx.y * kUdTok;
+  const int nt = (int)(Tn - t0 < kUdTok ? Tn - t0 : kUdTok);
+  for (int k = threadIdx.x; k < kUdTok * NE; k += blockDim.x) {
+    const int tt = k / NE, e = k % NE;
+    dzs[tt][e] = (tt < nt && e < E) ? dz[(t0 + tt) * E + e] : 0.f;
+  }
+  for (int k = threadIdx.x; k < kUdTok * kMaxTopK; k += blockDim.x) {
+    const int tt = k / kMaxTopK, j = k % kMaxTopK;
+    rows_s[tt][j] = (tt < nt && j < K) ? slot_row[(t0 + tt) * K + j] : 0;
+  }
+  __syncthreads();
+  const int i = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= D) return;
+  float w[4][NE];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const T* wrow = wr + (int64_t)(i + u) * E;
+    if (NE == 8 && E == 8) {
+      ld_row8(wrow, w[u]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < NE; ++e) w[u][e] = e < E ? ld(&wrow[e]) : 0.f;
+    }
+  }
+  for (int tt0 = 0; tt0 < nt; tt0 += 4) {
+    float4 v[4][KK];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int k = 0; k < KK; ++k)
+        if (tt0 + q < nt && k < K) v[q][k] = ld4(dxp + rows_s[tt0 + q][k] * D + i);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int tt = tt0 + q;
+      if (tt >= nt) break;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < KK; ++k) {
+        if (k < K) { a.x += v[q][k].x; a.y += v[q][k].y; a.z += v[q][k].z; a.w += v[q][k].w; }
+      }
+      float rr[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float acc = 0.f;
+#pragma unroll
+        for (int e = 0; e < NE; ++e)
+          if (NE == 8 || e < E) acc += dzs[tt][e] * w[u][e];
+        rr[u] = acc;
+      }
+      st4(dxn + (t0 + tt) * D + i, make_float4(a.x + rr[0], a.y + rr[1], a.z + rr[2], a.w + rr[3]));
+    }
+  }
+}
+
 // Router weight adjoint partials: part[c, i, e] = sum_{t in chunk c}
 // xn2[t,i] * dz[t,e] with xn2 recomputed in fp32 from (mid, inv, w).
 template <typename T>
@@ -1398,6 +1465,19 @@ template <typename T>
 void unpermute_router_dx(const float* dxp, const int* slot_row, const float* dz, const T* wr,
                          int64_t Tn, int E, int K, int D, float* dxn, cudaStream_t s,
                          int64_t& launches) {
+  if (D % 4 == 0 && aligned4(dxp) && aligned4(dxn) && K <= kMaxTopK) {
+    const dim3 grid((unsigned)ceil_div(D / 4, 256), (unsigned)ceil_div(Tn, kUdTok));
+    const bool e8 = E == 8 && (uintptr_t)wr % 16 == 0;
+#define DOP_UDWS(NE, KK) k_unpermute_router_dx_ws<T, NE, KK><<<grid, 256, 0, s>>>( \
+    dxp, slot_row, dz, wr, Tn, E, K, D, dxn)
+    if (e8 && K <= 2) DOP_UDWS(8, 2);
+    else if (e8) DOP_UDWS(8, 4);
+    else if (K <= 2) DOP_UDWS(kMaxExperts, 2);
+    else DOP_UDWS(kMaxExperts, 4);
+#undef DOP_UDWS
+    DOP_LAUNCHED(launches);
+    return;
+  }
   const int nv = row_quads(D);
   if (nv && aligned4(dxp) && aligned4(dxn)) {
     const bool e8 = E == 8 && (uintptr_t)wr % 16 == 0;
