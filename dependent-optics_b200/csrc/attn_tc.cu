@@ -60,7 +60,7 @@ __device__ __forceinline__ void st_tile_row32(uint8_t* tile, int r, int c0, cons
 constexpr float kRescale = 8.0f;
 // kPolyPairs of every 16 exponential pairs of the forward softmax (spread
 // evenly) are evaluated by exp2_poly2 on the FMA pipe instead of the MUFU.
-constexpr int kPolyPairs = 4;
+constexpr int kPolyPairs = 2;
 __device__ __forceinline__ constexpr bool poly_pair(int i) { return (i * kPolyPairs) % 16 < kPolyPairs; }
 
 __global__ void __launch_bounds__(320, 1)
@@ -283,6 +283,20 @@ __global__ void __launch_bounds__(320, 1)
       // every score masked to -inf, and 2^(-inf) = 0
       const float nm = m == -INFINITY ? 0.f : -m;
       const float2 nmv = make_float2(nm, nm);
+      if (rescale) {
+        // O is complete (S_g(it) was issued after P V of the previous tile)
+        // and stays so until p_full is signalled below; 16 columns at a
+        // time, while the scores are held in registers
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          float ov[16];
+          uint32_t ou[16];
+          tmem_ld16(to + c * 16, ov);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) ou[i] = __float_as_uint(ov[i] * alpha);
+          tmem_st16u(to + c * 16, ou);
+        }
+      }
       float2 acc[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) acc[u] = make_float2(0.f, 0.f);
@@ -304,18 +318,6 @@ __global__ void __launch_bounds__(320, 1)
       const float2 s01 = fadd2(acc[0], acc[1]), s23 = fadd2(acc[2], acc[3]);
       const float2 s4 = fadd2(s01, s23);
       l = l * alpha + (s4.x + s4.y);
-      if (rescale) {
-        // O is complete (S_g(it) was issued after P V of the previous tile)
-        // and stays so until p_full is signalled below
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float ov[32];
-          tmem_ld32(to + c * 32, ov);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-          tmem_st32(to + c * 32, ov);
-        }
-      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
