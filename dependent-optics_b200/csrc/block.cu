@@ -592,7 +592,8 @@ void Block::bwd(const Act* P, const float* dy, float* dx, float* dP, cudaStream_
   ph_begin("router_bwd", s);
   router_bwd(dy, out, slot_row, top_i, top_p, top_w, probs, T, (int)E, (int)K, (int)D, dz, s,
              launches);
-  gather_scale_rows<Act>(dy, row_token, row_w, seg_off, (int)E, (int)D, rows_cap, dO_, s, launches);
+  scatter_scale_rows<Act>(dy, slot_row, top_w, T, (int)K, row_token, row_w, seg_off, (int)E, (int)D,
+                          rows_cap, dO_, s, launches);
   ph_end(s);
   bool ep = false;
   if constexpr (std::is_same<Act, bf16>::value) {

@@ -503,6 +503,43 @@ __global__ void k_gather_scale_rows_v(const float* __restrict__ src,
   }
 }
 
+// Token-major form of k_gather_scale_rows_v: CTA t reads dy row t once and
+// writes top_w[t K + k] * dy[t] to its K expert rows slot_row[t K + k] (the
+// same products as the row-major form, row_w[slot_row[p]] = top_w[p]).
+template <typename T>
+__global__ void __launch_bounds__(256) k_scatter_scale_rows_v(const float* __restrict__ src,
+                                                              const int* __restrict__ slot_row,
+                                                              const float* __restrict__ top_w,
+                                                              int K, int D, T* __restrict__ dst) {
+  const int64_t t = blockIdx.x;
+  int64_t rows[kMaxTopK];
+  float w[kMaxTopK];
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) {
+    rows[k] = k < K ? slot_row[t * K + k] : 0;
+    w[k] = k < K ? top_w[t * K + k] : 0.f;
+  }
+  constexpr int U = 4;  // float4 loads in flight per thread
+  for (int i0 = threadIdx.x * 4; i0 < D; i0 += U * 1024) {
+    float4 a[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u * 1024;
+      a[u] = i < D ? ld4(src + t * D + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u * 1024;
+      if (i >= D) break;
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k)
+        if (k < K)
+          st4(dst + rows[k] * D + i,
+              make_float4(w[k] * a[u].x, w[k] * a[u].y, w[k] * a[u].z, w[k] * a[u].w));
+    }
+  }
+}
+
 // y[t] = mid[t] + sum_k w_k * out[row(t,k)], 4 elements per access; the slot
 // sum is taken in slot order from zero, as in k_combine.
 __global__ void k_combine_v(const float* __restrict__ mid, const float* __restrict__ out,
@@ -1405,6 +1442,23 @@ void scatter_rows(const T* src, const int* slot_row, int64_t Tn, int K, const in
 }
 
 template <typename T>
+void scatter_scale_rows(const float* src, const int* slot_row, const float* top_w, int64_t Tn,
+                        int K, const int* row_token, const float* row_w, const int* seg_off, int E,
+                        int D, int64_t rows_cap, T* dst, cudaStream_t s, int64_t& launches) {
+  const int64_t bytes = (int64_t)D * sizeof(T);
+  if (D % 4 != 0 || bytes % 16 != 0 || !aligned4(src) || (uintptr_t)dst % 16 != 0 ||
+      K > kMaxTopK) {
+    gather_scale_rows<T>(src, row_token, row_w, seg_off, E, D, rows_cap, dst, s, launches);
+    return;
+  }
+  k_scatter_scale_rows_v<T><<<(unsigned)Tn, 256, 0, s>>>(src, slot_row, top_w, K, D, dst);
+  DOP_LAUNCHED(launches);
+  k_zero_pad_rows16<<<(unsigned)ceil_div(rows_cap, 8), 256, 0, s>>>(row_token, seg_off, E, rows_cap,
+                                                                     (int)(bytes / 16), (uint4*)dst);
+  DOP_LAUNCHED(launches);
+}
+
+template <typename T>
 void gather_scale_rows(const float* src, const int* row_token, const float* row_w,
                        const int* seg_off, int E, int D, int64_t rows_cap, T* dst, cudaStream_t s,
                        int64_t& launches) {
@@ -1581,6 +1635,9 @@ void sgd(float* p, const float* g, int64_t n, float lr, cudaStream_t s, int64_t&
                                cudaStream_t, int64_t&);                                         \
   template void gather_scale_rows<T>(const float*, const int*, const float*, const int*, int,  \
                                      int, int64_t, T*, cudaStream_t, int64_t&);                 \
+  template void scatter_scale_rows<T>(const float*, const int*, const float*, int64_t, int,    \
+                                      const int*, const float*, const int*, int, int, int64_t, \
+                                      T*, cudaStream_t, int64_t&);                              \
   template void convert<T>(const float*, T*, int64_t, cudaStream_t, int64_t&);                  \
   template void rope<float, T>(const float*, T*, int64_t, int, int, int, const float*,         \
                                const float*, float, cudaStream_t, int64_t&);                    \

@@ -49,6 +49,13 @@ template <typename T>
 void gather_scale_rows(const float* src, const int* row_token, const float* row_w,
                        const int* seg_off, int E, int D, int64_t rows_cap, T* dst, cudaStream_t s,
                        int64_t& launches);
+// dst[slot_row[t K + k]] = top_w[t K + k] dy[t] token-major (each dy row read
+// once); padding rows zeroed.  Falls back to gather_scale_rows when the rows
+// are not 16-byte aligned.
+template <typename T>
+void scatter_scale_rows(const float* src, const int* slot_row, const float* top_w, int64_t Tn,
+                        int K, const int* row_token, const float* row_w, const int* seg_off, int E,
+                        int D, int64_t rows_cap, T* dst, cudaStream_t s, int64_t& launches);
 template <typename T>
 void silu_mul(const T* g, const T* u, const int* seg_off, int E, int64_t I, int64_t rows_cap,
               T* h, cudaStream_t s, int64_t& launches);
