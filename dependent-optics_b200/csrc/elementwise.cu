@@ -672,6 +672,96 @@ __global__ void __launch_bounds__(256) k_rmsnorm_bwd_v(const float* __restrict__
   }
 }
 
+// k_rmsnorm_bwd_v and the weight adjoint partials in one pass: CTA c walks
+// the rows of chunk c (the same per-row arithmetic as k_rmsnorm_bwd_v, so dx
+// is bit-identical to it) and accumulates part[c, i] = sum over its rows of
+// dy[t,i] * (x[t,i] r[t]) in increasing row order, from the dy and x it
+// already holds, so the weight adjoint costs no second read of either.
+template <typename T, int NV>
+__global__ void __launch_bounds__(256, 3) k_rmsnorm_bwd_dw_v(
+    const float* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ inv,
+    const T* __restrict__ w, const float* __restrict__ res, int64_t rows, int D,
+    int rows_per_chunk, float* __restrict__ dx, T* __restrict__ dx_act, float* __restrict__ part) {
+  const int c = blockIdx.x;
+  const int64_t t0 = (int64_t)c * rows_per_chunk;
+  const int64_t t1 = ::min(rows, t0 + rows_per_chunk);
+  const int D4 = D >> 2;
+  __shared__ float red[33];
+  float4 dw[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) dw[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t row = t0; row < t1; ++row) {
+    const float r = inv[row];
+    float4 xv[NV], gv[NV], rv[NV];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = threadIdx.x + j * 256;
+      if (i < D4) {
+        xv[j] = ld4(x + row * D + 4 * i);
+        gv[j] = ld4(dy + row * D + 4 * i);
+        if (res) rv[j] = ld4(res + row * D + 4 * i);
+        const float4 wv = ld4(w + 4 * i);
+        dot += (gv[j].x * wv.x) * (xv[j].x * r) + (gv[j].y * wv.y) * (xv[j].y * r) +
+               (gv[j].z * wv.z) * (xv[j].z * r) + (gv[j].w * wv.w) * (xv[j].w * r);
+      }
+    }
+    const float mean = block_sum(dot, red) / (float)D;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = threadIdx.x + j * 256;
+      if (i < D4) {
+        const float4 wv = ld4(w + 4 * i);
+        const float4 xq = xv[j], gq = gv[j];
+        float4 o;
+        o.x = r * (gq.x * wv.x - (xq.x * r) * mean);
+        o.y = r * (gq.y * wv.y - (xq.y * r) * mean);
+        o.z = r * (gq.z * wv.z - (xq.z * r) * mean);
+        o.w = r * (gq.w * wv.w - (xq.w * r) * mean);
+        if (res) {
+          o.x += rv[j].x; o.y += rv[j].y; o.z += rv[j].z; o.w += rv[j].w;
+        }
+        st4(dx + row * D + 4 * i, o);
+        if (dx_act) st4(dx_act + row * D + 4 * i, o);
+        dw[j].x += gq.x * (xq.x * r);
+        dw[j].y += gq.y * (xq.y * r);
+        dw[j].z += gq.z * (xq.z * r);
+        dw[j].w += gq.w * (xq.w * r);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * 256;
+    if (i < D4) *reinterpret_cast<float4*>(part + (int64_t)c * D + 4 * i) = dw[j];
+  }
+}
+
+// out[i] += sum over c < chunks of part[c, i], for many chunks: warp w of a
+// CTA sums the chunks [w L, (w + 1) L) of 32 columns in order, then warp 0
+// adds the 32 slice sums in order (deterministic).
+__global__ void __launch_bounds__(1024) k_reduce_chunks_wide(const float* __restrict__ part,
+                                                             int chunks, int64_t n,
+                                                             float* __restrict__ out) {
+  __shared__ float sl[32][33];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * 32 + l;
+  const int L = (chunks + 31) / 32;
+  float s = 0.f;
+  if (i < n) {
+    const int c1 = ::min(chunks, (w + 1) * L);
+    for (int c = w * L; c < c1; ++c) s += part[(int64_t)c * n + i];
+  }
+  sl[w][l] = s;
+  __syncthreads();
+  if (w == 0 && i < n) {
+    float t = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) t += sl[k][l];
+    out[i] += t;
+  }
+}
+
 // Weight adjoint partials: part[c, i] = sum_{t in chunk c} dy[t,i] * x[t,i] r[t],
 // rows in increasing order (deterministic).
 __global__ void k_rmsnorm_dw_part(const float* __restrict__ dy, const float* __restrict__ x,
@@ -1359,6 +1449,23 @@ void rmsnorm_bwd(const float* dy, const float* x, const float* inv, const T* w,
   const bool vec = D % 128 == 0 && aligned4(dy) && aligned4(x) && aligned4(w) &&
                    (!res || aligned4(res)) && aligned4(dx) && (!dx_act || aligned4(dx_act));
   const int nv = row_quads(D);
+  if (vec && nv && nv <= 4 && aligned4(part_buf)) {
+    // the input adjoint and the weight adjoint's partials in one pass over
+    // dy and x, three CTAs per SM, each walking a chunk of rows
+    int64_t chunks = std::min<int64_t>({rows, part_cap / D, 3 * (int64_t)sm_count()});
+    chunks = std::max<int64_t>(1, chunks);
+    const int rows_per_chunk = (int)ceil_div(rows, chunks);
+    chunks = ceil_div(rows, rows_per_chunk);
+    auto k = nv == 1 ? k_rmsnorm_bwd_dw_v<T, 1> : nv == 2 ? k_rmsnorm_bwd_dw_v<T, 2>
+                                                          : k_rmsnorm_bwd_dw_v<T, 4>;
+    k<<<(unsigned)chunks, 256, 0, s>>>(dy, x, inv, w, res, rows, D, rows_per_chunk, dx, dx_act,
+                                       part_buf);
+    DOP_LAUNCHED(launches);
+    k_reduce_chunks_wide<<<(unsigned)ceil_div(D, 32), 1024, 0, s>>>(part_buf, (int)chunks, D,
+                                                                    dw_accum);
+    DOP_LAUNCHED(launches);
+    return;
+  }
   if (vec && nv) {
     auto k = nv == 1 ? k_rmsnorm_bwd_v<T, 1> : nv == 2 ? k_rmsnorm_bwd_v<T, 2>
            : nv == 4 ? k_rmsnorm_bwd_v<T, 4> : k_rmsnorm_bwd_v<T, 8>;
