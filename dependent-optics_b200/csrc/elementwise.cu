@@ -1446,6 +1446,7 @@ template <typename T>
 void rmsnorm_bwd(const float* dy, const float* x, const float* inv, const T* w,
                  const float* res, int64_t rows, int D, float* dx, T* dx_act, float* dw_accum,
                  float* part_buf, int64_t part_cap, cudaStream_t s, int64_t& launches) {
+  if (rows <= 0 || D <= 0) return;  // nothing to do (and no empty grid)
   const bool vec = D % 128 == 0 && aligned4(dy) && aligned4(x) && aligned4(w) &&
                    (!res || aligned4(res)) && aligned4(dx) && (!dx_act || aligned4(dx_act));
   const int nv = row_quads(D);
